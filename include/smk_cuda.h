@@ -1,0 +1,128 @@
+/*
+ * smk_cuda.h — C ABI of the B200 (sm_100a) decode-GEMV library,
+ * libsmk_cuda.so. Plain pointers and sizes; no CUDA, C++ or framework types
+ * in the signatures (a stream is an opaque `void*`, a cudaStream_t).
+ *
+ * It replaces, for the decode-GEMV path only, the CPU kernel-table entries of
+ * Mattral/simd-ml-kernels 0.3.0 (file:line into that tree):
+ *   GemvQ4_0Fn / GemvQ8_0Fn = void(int N, int K, const float* x,
+ *       const uint8_t* Wq, float* y)                     src/dispatch/kernels.hpp:50-53,70-71
+ *   quantize_q4_0_rows / quantize_q8_0_rows             src/kernels/quant/q4_0.hpp:60, q8_0.hpp:58
+ *   quantize_x_q8                                       src/kernels/quant/q8_0.hpp:64
+ *   SgemmFn / Sgemm16Fn with trans_b, M <= 8 (x·Wᵀ)     src/dispatch/kernels.hpp:38-45,66-68
+ *                                                       (dot path: gemm/avx2_gemm_packed.cpp:715-732)
+ * with the same semantics: x quantized to Q8 blocks (FP32 scales) once per
+ * call; a NaN or ±Inf anywhere in a row of x makes that row's outputs NaN;
+ * K == 0 gives zeros; N == 0 (or M == 0) writes nothing; K % 32 != 0 is an
+ * argument error. There is no CPU fallback: every entry point runs CUDA
+ * kernels (or fails).
+ *
+ * Two kinds of entry points:
+ *   smk_*           device pointers, asynchronous on `stream`, capturable in
+ *                   a CUDA graph (no allocation, no synchronisation, unless a
+ *                   call needs library scratch for the first time at a size).
+ *   smk_*_host      any mix of host and device pointers (told apart with
+ *                   cudaPointerGetAttributes); host operands are staged
+ *                   through library-owned device buffers; returns when y is
+ *                   written. These are the reference's synchronous contract.
+ *
+ * Errors: every function returns an smk_status; smk_last_error() gives the
+ * message of the calling thread's last failure.
+ */
+#ifndef SMK_CUDA_H
+#define SMK_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum smk_status {
+    SMK_OK = 0,
+    SMK_ERR_ARGUMENT = 1,   /* shape / size / value rejected (reference: ArgumentError) */
+    SMK_ERR_DTYPE = 2,      /* element type not supported for this call (reference: DTypeError) */
+    SMK_ERR_CUDA = 3,       /* a CUDA runtime call failed */
+    SMK_ERR_DEVICE = 4,     /* a kernel reported an error (e.g. a bounded wait ran out) */
+    SMK_ERR_REJECTED = 5    /* quantize: NaN/Inf input or a block scale that overflows binary16 */
+} smk_status;
+
+/* Weight formats of smk_gemv_q / smk_quantize. */
+typedef enum smk_qformat { SMK_Q4_0 = 0, SMK_Q8_0 = 1 } smk_qformat;
+/* Element types of the dense path. */
+typedef enum smk_dtype { SMK_F32 = 0, SMK_F16 = 1, SMK_BF16 = 2 } smk_dtype;
+
+typedef struct smk_ctx smk_ctx;
+
+/* Library version string, e.g. "0.1.0 (sm_100a)". */
+const char* smk_version(void);
+/* Message of the calling thread's last failed call ("" if none). */
+const char* smk_last_error(void);
+
+/* A context per device: its device number, SM count, scratch buffers, the
+ * staging buffers of the _host calls and the error word of the kernels.
+ * Replaces the reference's process-wide kernels() table (kernels.hpp:84). */
+smk_status smk_ctx_create(int device, smk_ctx** out);
+smk_status smk_ctx_destroy(smk_ctx* ctx);
+/* Options (smk_ctx_set):
+ *   SMK_OPT_PDL     1: launch with programmatic dependent launch, so a GEMV
+ *                   starts streaming its weights while the previous GEMV of
+ *                   the stream finishes. Requires that no kernel immediately
+ *                   before it in the stream writes its weights. Default 0.
+ *   SMK_OPT_WARPS   warps per CTA of the quantized fast kernel (1..8, default 4).
+ *   SMK_OPT_STAGES  shared-memory stages per warp (2..8, default 4). */
+enum { SMK_OPT_PDL = 1, SMK_OPT_WARPS = 2, SMK_OPT_STAGES = 3 };
+smk_status smk_ctx_set(smk_ctx* ctx, int option, long long value);
+smk_status smk_ctx_get(smk_ctx* ctx, int option, long long* value);
+/* The CUDA device that owns `ptr` (device or managed memory), or -1 for host memory. */
+smk_status smk_pointer_device(const void* ptr, int* device);
+/* Reads and clears the device error word (0: no kernel error since the last read). */
+smk_status smk_device_error(smk_ctx* ctx, unsigned* code, void* stream);
+
+/* ---- quantized decode GEMV (replaces KernelTable::gemv_q4_0 / gemv_q8_0) ----
+ * y[m][n] = Σ_k x[m][k]·W[n][k] for m < M <= 8 rows of x, W as ggml blocks
+ * (N rows of K/32 blocks: Q4_0 18 bytes, Q8_0 34 bytes per block), each row of
+ * x quantized to Q8 blocks as the reference's quantize_x_q8. x [M, ldx] fp32,
+ * y [M, ldy] fp32. M == 1 with ldx = K, ldy = N is the reference's call. */
+smk_status smk_gemv_q(smk_ctx* ctx, smk_qformat fmt, int M, int N, int K, const float* x, int64_t ldx,
+                      const uint8_t* Wq, float* y, int64_t ldy, void* stream);
+smk_status smk_gemv_q4_0(smk_ctx* ctx, int N, int K, const float* x, const uint8_t* Wq, float* y, void* stream);
+smk_status smk_gemv_q8_0(smk_ctx* ctx, int N, int K, const float* x, const uint8_t* Wq, float* y, void* stream);
+/* Host-or-device pointers, synchronous. The exact contract of GemvQ4_0Fn / GemvQ8_0Fn. */
+smk_status smk_gemv_q_host(smk_ctx* ctx, smk_qformat fmt, int M, int N, int K, const float* x, const uint8_t* Wq,
+                           float* y);
+
+/* ---- dense decode GEMV (replaces sgemm / sgemm_f16 / sgemm_bf16 with trans_b, M <= 8) ----
+ * C[m][n] = alpha·Σ_k X[m][k]·W[n][k] + beta·C[m][n]; beta == 0: C is not read.
+ * x_type is w_type (the reference's contract) or SMK_F32 (fp32 activations
+ * against 16-bit weights, an addition). X [M, ldx], W [N, ldw], C [M, ldc]. */
+smk_status smk_gemv_dense(smk_ctx* ctx, smk_dtype w_type, smk_dtype x_type, int M, int N, int K, float alpha,
+                          const void* X, int64_t ldx, const void* W, int64_t ldw, float beta, float* C, int64_t ldc,
+                          void* stream);
+smk_status smk_gemv_dense_host(smk_ctx* ctx, smk_dtype w_type, smk_dtype x_type, int M, int N, int K, float alpha,
+                               const void* X, const void* W, float beta, float* C);
+
+/* ---- weight quantization on the device (replaces quantize_q4_0_rows / quantize_q8_0_rows) ----
+ * W [rows, K] fp32 -> rows·K/32 blocks, byte-identical to ggml's
+ * quantize_row_q4_0_ref / quantize_row_q8_0_ref. Synchronous (the rejection
+ * flag is read back): SMK_ERR_REJECTED for NaN/Inf or a binary16 scale overflow. */
+smk_status smk_quantize(smk_ctx* ctx, smk_qformat fmt, int64_t rows, int K, const float* W, uint8_t* out,
+                        void* stream);
+smk_status smk_quantize_host(smk_ctx* ctx, smk_qformat fmt, int64_t rows, int K, const float* W, uint8_t* out);
+
+/* ---- test hooks (bit-exactness checks; same device code as the GEMV) ----
+ * smk_quantize_x: x [M, K] -> qs [M, K] int8 and dx [M, K/32] fp32 (NaN for a
+ * block with a non-finite value), the activation quantization of the GEMV.
+ * smk_block_sums: the GEMV's exact per-block integer sums, out [M, N, K/32]
+ * int32, produced by the production kernel's dump mode. Device pointers. */
+smk_status smk_quantize_x(smk_ctx* ctx, int M, int K, const float* x, int64_t ldx, int8_t* qs, float* dx,
+                          void* stream);
+smk_status smk_block_sums(smk_ctx* ctx, smk_qformat fmt, int M, int N, int K, const float* x, int64_t ldx,
+                          const uint8_t* Wq, int32_t* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SMK_CUDA_H */

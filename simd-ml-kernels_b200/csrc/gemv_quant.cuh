@@ -1,0 +1,76 @@
+// gemv_quant.cuh — launch parameters of the Q4_0 / Q8_0 decode-GEMV kernels
+// (gemv_quant.cu) shared with the C-ABI layer (smk_api.cu).
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace smk {
+
+enum QFmt : int { kQ4_0 = 0, kQ8_0 = 1 };
+
+constexpr int kQK = 32;           // values per block
+constexpr int kSbBlocks = 8;      // blocks per superblock (256 values)
+constexpr int kMaxRows = 8;       // rows of x per call (M)
+
+__host__ __device__ constexpr int block_bytes(int fmt) { return fmt == kQ4_0 ? 18 : 34; }
+__host__ __device__ constexpr int sb_bytes(int fmt) { return 8 * block_bytes(fmt); }   // 144 / 272
+
+// Quantized activations in device memory (shared memory or a global buffer),
+// laid out so that lanes reading consecutive superblocks hit distinct banks:
+//   quants of x row m, block b = 8·sb + j, half h (values 16h .. 16h+15):
+//       16 bytes at ((m·2 + h)·8 + j)·nsbp·16 + sb·16
+//   (dx, bias) of the block as float2 (bias = −8·Σ quants as int bits):
+//       at xq_bytes + ((m·8 + j)·nsbp + sb)·8
+// nsbp = ceil(nb / 8) superblocks per row (blocks past nb are never read).
+// A block whose values are not all finite stores dx = NaN, which makes every
+// output of that x row NaN, the reference's rule (q8_0_scalar.cpp:142-164).
+__host__ __device__ inline size_t xq_quant_bytes(int M, int nsbp) { return (size_t)M * nsbp * 256; }
+__host__ __device__ inline size_t xq_total_bytes(int M, int nsbp) {
+    return xq_quant_bytes(M, nsbp) + (size_t)M * nsbp * 8 * 8;
+}
+
+struct QGemvParams {
+    const float* x;        // [M, ldx] fp32 activations (device)
+    long long ldx;
+    const uint8_t* w;      // N rows of K/32 blocks (device)
+    float* y;              // [M, ldy]
+    long long ldy;
+    int M, N, K;
+    int nb;                // K / 32
+    int nsbp;              // ceil(nb / 8)
+    // Fast kernel tiling: a warp tile is TR rows × G superblocks (TR·G = 32,
+    // one superblock per lane); ksteps tiles cover a row.
+    int G, log2G, TR, ksteps, ntiles, stages;
+    const uint8_t* xq;     // quantized x in global memory (nullptr: each CTA quantizes into shared memory)
+    int32_t* dump;         // test-only: per-block integer sums [M, N, nb], or nullptr
+    unsigned* err;         // device error word
+};
+
+// CTAs per SM of `fn` at this launch shape; raises the kernel's dynamic
+// shared-memory limit as needed. Cached per (device, kernel, threads, smem).
+cudaError_t occupancy(const void* fn, int threads, size_t smem, int* per_sm);
+
+// Host-side launchers (gemv_quant.cu). All return cudaGetLastError() of the launch.
+struct LaunchCfg {
+    cudaStream_t stream;
+    bool pdl;              // programmatic dependent launch
+    int num_sms;
+    int warps;             // warps per CTA of the fast kernel
+};
+
+// Quantize x into the layout above in global memory (xq_total_bytes).
+cudaError_t launch_quantize_x(const LaunchCfg& c, const float* x, long long ldx, int M, int K, uint8_t* xq);
+// y = x · Wᵀ. fast: K % 256 == 0 and w 16-byte aligned (ggml superblocks
+// stream as whole 16-byte units); otherwise the generic kernel.
+cudaError_t launch_gemv_q(const LaunchCfg& c, int fmt, QGemvParams p, bool fast, size_t* smem_used);
+// Size of the fast kernel's dynamic shared memory for this launch.
+size_t gemv_q_smem(int fmt, int M, int nsbp, int warps, int stages, bool x_in_smem);
+
+// Weight quantizers (ggml quantize_row_q4_0_ref / q8_0_ref, bit-exact).
+// *reject gets 1 when a value is NaN/Inf or a scale overflows binary16.
+cudaError_t launch_quantize_w(cudaStream_t s, int fmt, const float* W, long long rows, int K, uint8_t* out,
+                              unsigned* reject);
+
+}  // namespace smk

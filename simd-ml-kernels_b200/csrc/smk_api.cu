@@ -1,0 +1,515 @@
+// smk_api.cu — the C ABI (include/smk_cuda.h) over the sm_100a kernels:
+// argument checks with the reference's rules, kernel selection and launch
+// shapes, library-owned scratch and staging buffers, host staging for the
+// synchronous *_host entry points, and error reporting.
+
+#include "../../include/smk_cuda.h"
+#include "gemv_dense.cuh"
+#include "gemv_quant.cuh"
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <limits>
+#include <map>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include <cuda_runtime.h>
+
+#define SMK_VERSION "0.1.0 (sm_100a)"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+smk_status fail(smk_status st, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return st;
+}
+
+smk_status cuda_fail(cudaError_t e, const char* what) {
+    return fail(SMK_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+}
+
+#define SMK_CUDA(call, what)                            \
+    do {                                                \
+        cudaError_t e_ = (call);                        \
+        if (e_ != cudaSuccess) return cuda_fail(e_, what); \
+    } while (0)
+
+// Switch to the context's device for the duration of a call.
+struct DeviceGuard {
+    int prev = -1;
+    bool ok = true;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != dev) ok = cudaSetDevice(dev) == cudaSuccess;
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+// A growable device buffer; old allocations are kept until the context dies,
+// so kernels still in flight on them stay valid.
+struct DevBuf {
+    void* ptr = nullptr;
+    size_t bytes = 0;
+    std::vector<void*> retired;
+    cudaError_t reserve(size_t want) {
+        if (want <= bytes) return cudaSuccess;
+        size_t n = std::max(want, bytes + bytes / 2);
+        n = (n + 4095) & ~(size_t)4095;
+        void* p = nullptr;
+        cudaError_t e = cudaMalloc(&p, n);
+        if (e != cudaSuccess) return e;
+        if (ptr) retired.push_back(ptr);
+        ptr = p;
+        bytes = n;
+        return cudaSuccess;
+    }
+    void release() {
+        for (void* p : retired) cudaFree(p);
+        retired.clear();
+        if (ptr) cudaFree(ptr);
+        ptr = nullptr;
+        bytes = 0;
+    }
+};
+
+bool is_device_ptr(const void* p) {
+    if (!p) return false;
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
+}
+
+size_t align256(size_t n) { return (n + 255) & ~(size_t)255; }
+
+}  // namespace
+
+struct smk_ctx {
+    int device = 0;
+    int num_sms = 148;
+    size_t smem_optin = 227 * 1024;
+    bool pdl = false;
+    int warps = 4;
+    int stages = 4;
+    unsigned* d_err = nullptr;      // device error word
+    unsigned* d_reject = nullptr;   // quantizer rejection flag
+    std::mutex mu_scratch;                    // guards scratch and test_buf
+    std::map<cudaStream_t, DevBuf> scratch;   // per-stream quantized-x scratch
+    DevBuf test_buf;                          // test hooks
+    std::mutex mu_stage;                      // held for a whole *_host call
+    DevBuf staging;                           // *_host operands
+};
+
+namespace {
+
+smk::LaunchCfg cfg_for(smk_ctx* c, cudaStream_t s) {
+    smk::LaunchCfg l;
+    l.stream = s;
+    l.pdl = c->pdl;
+    l.num_sms = c->num_sms;
+    l.warps = c->warps;
+    return l;
+}
+
+smk_status check_q_args(smk_qformat fmt, int M, int N, int K) {
+    if (fmt != SMK_Q4_0 && fmt != SMK_Q8_0) return fail(SMK_ERR_DTYPE, "unknown block format %d", (int)fmt);
+    if (M < 0 || N < 0 || K < 0) return fail(SMK_ERR_ARGUMENT, "N and K must be >= 0");
+    if (M > smk::kMaxRows) return fail(SMK_ERR_ARGUMENT, "at most %d rows of x per call (got %d)", smk::kMaxRows, M);
+    if (K % 32 != 0) return fail(SMK_ERR_ARGUMENT, "K must be a multiple of 32 (got %d)", K);
+    return SMK_OK;
+}
+
+// The launch shape of the quantized fast kernel for this call.
+struct QPlan {
+    bool fast;
+    bool x_in_smem;
+    size_t x_bytes;
+    smk::QGemvParams p;
+};
+
+QPlan plan_q(smk_ctx* c, smk_qformat fmt, int M, int N, int K, const float* x, int64_t ldx, const uint8_t* Wq, float* y,
+             int64_t ldy, bool want_dump) {
+    QPlan q = {};
+    smk::QGemvParams& p = q.p;
+    p.x = x; p.ldx = ldx; p.w = Wq; p.y = y; p.ldy = ldy;
+    p.M = M; p.N = N; p.K = K;
+    p.nb = K / 32;
+    p.nsbp = (p.nb + 7) / 8;
+    p.err = c->d_err;
+    q.x_bytes = smk::xq_total_bytes(M, p.nsbp);
+    q.fast = (K % 256 == 0) && ((reinterpret_cast<uintptr_t>(Wq) & 15) == 0);
+    if (q.fast) {
+        const int nsb = p.nsbp;
+        int G = 1, lg = 0;
+        while (G < nsb && G < 32) { G <<= 1; ++lg; }
+        p.G = G; p.log2G = lg; p.TR = 32 / G;
+        p.ksteps = (nsb + G - 1) / G;
+        p.ntiles = (N + p.TR - 1) / p.TR;
+        p.stages = c->stages;
+        // Quantized x in shared memory while it is small; otherwise one
+        // quantize kernel writes it to scratch and every CTA reads it there.
+        const size_t budget = 64 * 1024;
+        q.x_in_smem = q.x_bytes <= budget || want_dump;
+        size_t smem = smk::gemv_q_smem(fmt, M, nsb, c->warps, p.stages, q.x_in_smem);
+        while (smem > c->smem_optin && p.stages > 2) {
+            --p.stages;
+            smem = smk::gemv_q_smem(fmt, M, nsb, c->warps, p.stages, q.x_in_smem);
+        }
+        if (smem > c->smem_optin) q.fast = false;   // e.g. a dump of a huge M·K: the generic kernel
+    }
+    if (!q.fast) q.x_in_smem = false;
+    return q;
+}
+
+smk_status run_q(smk_ctx* c, smk_qformat fmt, int M, int N, int K, const float* x, int64_t ldx, const uint8_t* Wq,
+                 float* y, int64_t ldy, cudaStream_t s, int32_t* dump) {
+    if (M == 0 || N == 0) return SMK_OK;
+    if (K == 0) {
+        for (int m = 0; m < M; ++m) SMK_CUDA(cudaMemsetAsync(y + (size_t)m * ldy, 0, (size_t)N * 4, s), "cudaMemsetAsync");
+        return SMK_OK;
+    }
+    QPlan q = plan_q(c, fmt, M, N, K, x, ldx, Wq, y, ldy, dump != nullptr);
+    q.p.dump = dump;
+    const smk::LaunchCfg l = cfg_for(c, s);
+    if (!q.x_in_smem) {
+        uint8_t* xq;
+        {
+            std::lock_guard<std::mutex> g(c->mu_scratch);
+            DevBuf& b = c->scratch[s];
+            SMK_CUDA(b.reserve(q.x_bytes), "cudaMalloc (scratch)");
+            xq = static_cast<uint8_t*>(b.ptr);
+        }
+        SMK_CUDA(smk::launch_quantize_x(l, x, ldx, M, K, xq), "quantize_x launch");
+        q.p.xq = xq;
+    }
+    SMK_CUDA(smk::launch_gemv_q(l, fmt, q.p, q.fast, nullptr), "gemv launch");
+    return SMK_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* smk_version(void) { return SMK_VERSION; }
+const char* smk_last_error(void) { return g_last_error.c_str(); }
+
+smk_status smk_ctx_create(int device, smk_ctx** out) {
+    if (!out) return fail(SMK_ERR_ARGUMENT, "out must not be NULL");
+    *out = nullptr;
+    int n = 0;
+    SMK_CUDA(cudaGetDeviceCount(&n), "cudaGetDeviceCount");
+    if (device < 0 || device >= n) return fail(SMK_ERR_ARGUMENT, "device %d out of range (%d devices)", device, n);
+    DeviceGuard g(device);
+    if (!g.ok) return fail(SMK_ERR_CUDA, "cudaSetDevice(%d) failed", device);
+    cudaDeviceProp prop;
+    SMK_CUDA(cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties");
+    if (prop.major < 10)
+        return fail(SMK_ERR_CUDA, "device %d (%s, sm_%d%d) is not a Blackwell sm_100 GPU", device, prop.name,
+                    prop.major, prop.minor);
+    smk_ctx* c = new smk_ctx();
+    c->device = device;
+    c->num_sms = prop.multiProcessorCount;
+    c->smem_optin = prop.sharedMemPerBlockOptin;
+    cudaError_t e = cudaMalloc(&c->d_err, 2 * sizeof(unsigned));
+    if (e != cudaSuccess) {
+        delete c;
+        return cuda_fail(e, "cudaMalloc (error word)");
+    }
+    c->d_reject = c->d_err + 1;
+    e = cudaMemset(c->d_err, 0, 2 * sizeof(unsigned));
+    if (e != cudaSuccess) {
+        cudaFree(c->d_err);
+        delete c;
+        return cuda_fail(e, "cudaMemset");
+    }
+    *out = c;
+    return SMK_OK;
+}
+
+smk_status smk_ctx_destroy(smk_ctx* c) {
+    if (!c) return SMK_OK;
+    DeviceGuard g(c->device);
+    cudaDeviceSynchronize();
+    for (auto& kv : c->scratch) kv.second.release();
+    c->staging.release();
+    c->test_buf.release();
+    cudaFree(c->d_err);
+    delete c;
+    return SMK_OK;
+}
+
+smk_status smk_ctx_set(smk_ctx* c, int option, long long v) {
+    if (!c) return fail(SMK_ERR_ARGUMENT, "ctx must not be NULL");
+    switch (option) {
+        case SMK_OPT_PDL: c->pdl = v != 0; return SMK_OK;
+        case SMK_OPT_WARPS:
+            if (v < 1 || v > 8) return fail(SMK_ERR_ARGUMENT, "warps must be in 1..8");
+            c->warps = (int)v;
+            return SMK_OK;
+        case SMK_OPT_STAGES:
+            if (v < 2 || v > 8) return fail(SMK_ERR_ARGUMENT, "stages must be in 2..8");
+            c->stages = (int)v;
+            return SMK_OK;
+        default: return fail(SMK_ERR_ARGUMENT, "unknown option %d", option);
+    }
+}
+
+smk_status smk_ctx_get(smk_ctx* c, int option, long long* v) {
+    if (!c || !v) return fail(SMK_ERR_ARGUMENT, "ctx and value must not be NULL");
+    switch (option) {
+        case SMK_OPT_PDL: *v = c->pdl; return SMK_OK;
+        case SMK_OPT_WARPS: *v = c->warps; return SMK_OK;
+        case SMK_OPT_STAGES: *v = c->stages; return SMK_OK;
+        default: return fail(SMK_ERR_ARGUMENT, "unknown option %d", option);
+    }
+}
+
+smk_status smk_pointer_device(const void* ptr, int* device) {
+    if (!device) return fail(SMK_ERR_ARGUMENT, "device must not be NULL");
+    *device = -1;
+    if (!ptr) return SMK_OK;
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, ptr) != cudaSuccess) {
+        cudaGetLastError();
+        return SMK_OK;
+    }
+    if (a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged) *device = a.device;
+    return SMK_OK;
+}
+
+smk_status smk_device_error(smk_ctx* c, unsigned* code, void* stream) {
+    if (!c || !code) return fail(SMK_ERR_ARGUMENT, "ctx and code must not be NULL");
+    DeviceGuard g(c->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    unsigned h = 0;
+    SMK_CUDA(cudaMemcpyAsync(&h, c->d_err, sizeof h, cudaMemcpyDeviceToHost, s), "cudaMemcpyAsync");
+    SMK_CUDA(cudaMemsetAsync(c->d_err, 0, sizeof h, s), "cudaMemsetAsync");
+    SMK_CUDA(cudaStreamSynchronize(s), "cudaStreamSynchronize");
+    *code = h;
+    return SMK_OK;
+}
+
+smk_status smk_gemv_q(smk_ctx* c, smk_qformat fmt, int M, int N, int K, const float* x, int64_t ldx,
+                      const uint8_t* Wq, float* y, int64_t ldy, void* stream) {
+    if (!c) return fail(SMK_ERR_ARGUMENT, "ctx must not be NULL");
+    smk_status st = check_q_args(fmt, M, N, K);
+    if (st != SMK_OK) return st;
+    if (M == 0 || N == 0) return SMK_OK;
+    if (!y || (K > 0 && (!x || !Wq))) return fail(SMK_ERR_ARGUMENT, "x, Wq and y must not be NULL");
+    if (ldy < N || (K > 0 && ldx < K)) return fail(SMK_ERR_ARGUMENT, "ldx >= K and ldy >= N required");
+    DeviceGuard g(c->device);
+    if (!g.ok) return fail(SMK_ERR_CUDA, "cudaSetDevice(%d) failed", c->device);
+    return run_q(c, fmt, M, N, K, x, ldx, Wq, y, ldy, static_cast<cudaStream_t>(stream), nullptr);
+}
+
+smk_status smk_gemv_q4_0(smk_ctx* c, int N, int K, const float* x, const uint8_t* Wq, float* y, void* stream) {
+    return smk_gemv_q(c, SMK_Q4_0, 1, N, K, x, K, Wq, y, N, stream);
+}
+
+smk_status smk_gemv_q8_0(smk_ctx* c, int N, int K, const float* x, const uint8_t* Wq, float* y, void* stream) {
+    return smk_gemv_q(c, SMK_Q8_0, 1, N, K, x, K, Wq, y, N, stream);
+}
+
+smk_status smk_gemv_q_host(smk_ctx* c, smk_qformat fmt, int M, int N, int K, const float* x, const uint8_t* Wq,
+                           float* y) {
+    if (!c) return fail(SMK_ERR_ARGUMENT, "ctx must not be NULL");
+    smk_status st = check_q_args(fmt, M, N, K);
+    if (st != SMK_OK) return st;
+    if (M == 0 || N == 0) return SMK_OK;
+    if (!y || (K > 0 && (!x || !Wq))) return fail(SMK_ERR_ARGUMENT, "x, Wq and y must not be NULL");
+    DeviceGuard g(c->device);
+    if (!g.ok) return fail(SMK_ERR_CUDA, "cudaSetDevice(%d) failed", c->device);
+    const size_t xb = (size_t)M * K * 4, wb = (size_t)N * (K / 32) * smk::block_bytes(fmt), yb = (size_t)M * N * 4;
+    const bool xh = K > 0 && !is_device_ptr(x), wh = K > 0 && !is_device_ptr(Wq), yh = !is_device_ptr(y);
+    cudaStream_t s = nullptr;   // the legacy default stream: ordered after other blocking streams' work
+    std::lock_guard<std::mutex> lock(c->mu_stage);
+    const size_t ox = 0, ow = ox + (xh ? align256(xb) : 0), oy = ow + (wh ? align256(wb) : 0),
+                 total = oy + (yh ? align256(yb) : 0);
+    if (total) SMK_CUDA(c->staging.reserve(total), "cudaMalloc (staging)");
+    char* base = static_cast<char*>(c->staging.ptr);
+    const float* dx = xh ? reinterpret_cast<const float*>(base + ox) : x;
+    const uint8_t* dw = wh ? reinterpret_cast<const uint8_t*>(base + ow) : Wq;
+    float* dy = yh ? reinterpret_cast<float*>(base + oy) : y;
+    if (xh) SMK_CUDA(cudaMemcpyAsync(base + ox, x, xb, cudaMemcpyHostToDevice, s), "cudaMemcpyAsync (x)");
+    if (wh) SMK_CUDA(cudaMemcpyAsync(base + ow, Wq, wb, cudaMemcpyHostToDevice, s), "cudaMemcpyAsync (Wq)");
+    st = run_q(c, fmt, M, N, K, dx, K, dw, dy, N, s, nullptr);
+    if (st != SMK_OK) return st;
+    if (yh) SMK_CUDA(cudaMemcpyAsync(y, dy, yb, cudaMemcpyDeviceToHost, s), "cudaMemcpyAsync (y)");
+    SMK_CUDA(cudaStreamSynchronize(s), "cudaStreamSynchronize");
+    return SMK_OK;
+}
+
+smk_status smk_gemv_dense(smk_ctx* c, smk_dtype wt, smk_dtype xt, int M, int N, int K, float alpha, const void* X,
+                          int64_t ldx, const void* W, int64_t ldw, float beta, float* C, int64_t ldc, void* stream) {
+    if (!c) return fail(SMK_ERR_ARGUMENT, "ctx must not be NULL");
+    if (wt != SMK_F32 && wt != SMK_F16 && wt != SMK_BF16) return fail(SMK_ERR_DTYPE, "unknown weight type %d", (int)wt);
+    if (!(xt == wt || xt == SMK_F32)) return fail(SMK_ERR_DTYPE, "x must have the weights' type or float32");
+    if (M < 0 || N < 0 || K < 0) return fail(SMK_ERR_ARGUMENT, "M, N and K must be >= 0");
+    if (M > smk::kMaxRows) return fail(SMK_ERR_ARGUMENT, "the decode path takes at most %d rows of x (got %d)",
+                                       smk::kMaxRows, M);
+    if (M == 0 || N == 0) return SMK_OK;
+    if (!C || (K > 0 && (!X || !W))) return fail(SMK_ERR_ARGUMENT, "X, W and C must not be NULL");
+    if (ldc < N || (K > 0 && (ldx < K || ldw < K))) return fail(SMK_ERR_ARGUMENT, "leading dimensions too small");
+    DeviceGuard g(c->device);
+    if (!g.ok) return fail(SMK_ERR_CUDA, "cudaSetDevice(%d) failed", c->device);
+    smk::DenseParams p;
+    p.x = X; p.ldx = ldx; p.w = W; p.ldw = ldw; p.y = C; p.ldy = ldc;
+    p.M = M; p.N = N; p.K = K; p.alpha = alpha; p.beta = beta;
+    SMK_CUDA(smk::launch_gemv_dense(static_cast<cudaStream_t>(stream), c->pdl, c->num_sms, (int)wt, (int)xt, p),
+             "dense gemv launch");
+    return SMK_OK;
+}
+
+smk_status smk_gemv_dense_host(smk_ctx* c, smk_dtype wt, smk_dtype xt, int M, int N, int K, float alpha,
+                               const void* X, const void* W, float beta, float* C) {
+    if (!c) return fail(SMK_ERR_ARGUMENT, "ctx must not be NULL");
+    if (M <= 0 || N <= 0) return smk_gemv_dense(c, wt, xt, M, N, K, alpha, X, K, W, K, beta, C, N, nullptr);
+    DeviceGuard g(c->device);
+    if (!g.ok) return fail(SMK_ERR_CUDA, "cudaSetDevice(%d) failed", c->device);
+    const size_t xes = xt == SMK_F32 ? 4 : 2, wes = wt == SMK_F32 ? 4 : 2;
+    const size_t xb = (size_t)M * K * xes, wb = (size_t)N * K * wes, cb = (size_t)M * N * 4;
+    const bool xh = K > 0 && !is_device_ptr(X), wh = K > 0 && !is_device_ptr(W), ch = !is_device_ptr(C);
+    cudaStream_t s = nullptr;
+    std::lock_guard<std::mutex> lock(c->mu_stage);
+    const size_t ox = 0, ow = ox + (xh ? align256(xb) : 0), oc = ow + (wh ? align256(wb) : 0),
+                 total = oc + (ch ? align256(cb) : 0);
+    if (total) SMK_CUDA(c->staging.reserve(total), "cudaMalloc (staging)");
+    char* base = static_cast<char*>(c->staging.ptr);
+    const void* dX = xh ? base + ox : X;
+    const void* dW = wh ? base + ow : W;
+    float* dC = ch ? reinterpret_cast<float*>(base + oc) : C;
+    if (xh) SMK_CUDA(cudaMemcpyAsync(base + ox, X, xb, cudaMemcpyHostToDevice, s), "cudaMemcpyAsync (X)");
+    if (wh) SMK_CUDA(cudaMemcpyAsync(base + ow, W, wb, cudaMemcpyHostToDevice, s), "cudaMemcpyAsync (W)");
+    if (ch && beta != 0.0f) SMK_CUDA(cudaMemcpyAsync(dC, C, cb, cudaMemcpyHostToDevice, s), "cudaMemcpyAsync (C)");
+    smk_status st = smk_gemv_dense(c, wt, xt, M, N, K, alpha, dX, K, dW, K, beta, dC, N, s);
+    if (st != SMK_OK) return st;
+    if (K == 0 && beta == 0.0f) SMK_CUDA(cudaMemsetAsync(dC, 0, cb, s), "cudaMemsetAsync");
+    if (ch) SMK_CUDA(cudaMemcpyAsync(C, dC, cb, cudaMemcpyDeviceToHost, s), "cudaMemcpyAsync (C)");
+    SMK_CUDA(cudaStreamSynchronize(s), "cudaStreamSynchronize");
+    return SMK_OK;
+}
+
+smk_status smk_quantize(smk_ctx* c, smk_qformat fmt, int64_t rows, int K, const float* W, uint8_t* out, void* stream) {
+    if (!c) return fail(SMK_ERR_ARGUMENT, "ctx must not be NULL");
+    if (fmt != SMK_Q4_0 && fmt != SMK_Q8_0) return fail(SMK_ERR_DTYPE, "unknown block format %d", (int)fmt);
+    if (rows < 0 || K < 0 || K % 32 != 0)
+        return fail(SMK_ERR_ARGUMENT, "K (the last dimension of W) must be a multiple of 32 (got %d)", K);
+    if (rows == 0 || K == 0) return SMK_OK;
+    DeviceGuard g(c->device);
+    if (!g.ok) return fail(SMK_ERR_CUDA, "cudaSetDevice(%d) failed", c->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    SMK_CUDA(cudaMemsetAsync(c->d_reject, 0, sizeof(unsigned), s), "cudaMemsetAsync");
+    SMK_CUDA(smk::launch_quantize_w(s, (int)fmt, W, rows, K, out, c->d_reject), "quantize launch");
+    unsigned rej = 0;
+    SMK_CUDA(cudaMemcpyAsync(&rej, c->d_reject, sizeof rej, cudaMemcpyDeviceToHost, s), "cudaMemcpyAsync");
+    SMK_CUDA(cudaStreamSynchronize(s), "cudaStreamSynchronize");
+    if (rej)
+        return fail(SMK_ERR_REJECTED, "W must be finite, with every block scale representable in float16");
+    return SMK_OK;
+}
+
+smk_status smk_quantize_host(smk_ctx* c, smk_qformat fmt, int64_t rows, int K, const float* W, uint8_t* out) {
+    if (!c) return fail(SMK_ERR_ARGUMENT, "ctx must not be NULL");
+    if (fmt != SMK_Q4_0 && fmt != SMK_Q8_0) return fail(SMK_ERR_DTYPE, "unknown block format %d", (int)fmt);
+    if (rows < 0 || K < 0 || K % 32 != 0)
+        return fail(SMK_ERR_ARGUMENT, "K (the last dimension of W) must be a multiple of 32 (got %d)", K);
+    if (rows == 0 || K == 0) return SMK_OK;
+    DeviceGuard g(c->device);
+    if (!g.ok) return fail(SMK_ERR_CUDA, "cudaSetDevice(%d) failed", c->device);
+    const size_t wb = (size_t)rows * K * 4, ob = (size_t)rows * (K / 32) * smk::block_bytes(fmt);
+    const bool wh = !is_device_ptr(W), oh = !is_device_ptr(out);
+    cudaStream_t s = nullptr;
+    std::lock_guard<std::mutex> lock(c->mu_stage);
+    const size_t total = (wh ? align256(wb) : 0) + (oh ? align256(ob) : 0);
+    if (total) SMK_CUDA(c->staging.reserve(total), "cudaMalloc (staging)");
+    char* base = static_cast<char*>(c->staging.ptr);
+    const float* dW = wh ? reinterpret_cast<const float*>(base) : W;
+    uint8_t* dO = oh ? reinterpret_cast<uint8_t*>(base + (wh ? align256(wb) : 0)) : out;
+    if (wh) SMK_CUDA(cudaMemcpyAsync(base, W, wb, cudaMemcpyHostToDevice, s), "cudaMemcpyAsync (W)");
+    smk_status st = smk_quantize(c, fmt, rows, K, dW, dO, s);
+    if (st != SMK_OK) return st;
+    if (oh) {
+        SMK_CUDA(cudaMemcpyAsync(out, dO, ob, cudaMemcpyDeviceToHost, s), "cudaMemcpyAsync (out)");
+        SMK_CUDA(cudaStreamSynchronize(s), "cudaStreamSynchronize");
+    }
+    return SMK_OK;
+}
+
+}  // extern "C"
+
+// ---- test hooks --------------------------------------------------------------
+
+namespace {
+
+// Un-swizzle the quantized-x layout into plain int8 [M, K] and fp32 [M, K/32].
+__global__ void unswizzle_x(const uint8_t* xq, int M, int nb, int nsbp, int8_t* qs, float* dx) {
+    const int K = nb * 32;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < (long long)M * K;
+         i += (long long)gridDim.x * blockDim.x) {
+        const int m = (int)(i / K), k = (int)(i % K), b = k / 32, v = k % 32;
+        const int sb = b >> 3, j = b & 7, h = v >> 4;
+        qs[i] = (int8_t)xq[((size_t)((m * 2 + h) * 8 + j) * nsbp + sb) * 16 + (v & 15)];
+        if (v == 0)
+            dx[(size_t)m * nb + b] =
+                reinterpret_cast<const float2*>(xq + smk::xq_quant_bytes(M, nsbp))[(size_t)(m * 8 + j) * nsbp + sb].x;
+    }
+}
+
+}  // namespace
+
+extern "C" {
+
+smk_status smk_quantize_x(smk_ctx* c, int M, int K, const float* x, int64_t ldx, int8_t* qs, float* dx, void* stream) {
+    if (!c) return fail(SMK_ERR_ARGUMENT, "ctx must not be NULL");
+    smk_status st = check_q_args(SMK_Q8_0, M, 1, K);
+    if (st != SMK_OK) return st;
+    if (M == 0 || K == 0) return SMK_OK;
+    DeviceGuard g(c->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int nb = K / 32, nsbp = (nb + 7) / 8;
+    uint8_t* xq;
+    {
+        std::lock_guard<std::mutex> lock(c->mu_scratch);
+        SMK_CUDA(c->test_buf.reserve(smk::xq_total_bytes(M, nsbp)), "cudaMalloc (test)");
+        xq = static_cast<uint8_t*>(c->test_buf.ptr);
+    }
+    SMK_CUDA(smk::launch_quantize_x(cfg_for(c, s), x, ldx, M, K, xq), "quantize_x launch");
+    unswizzle_x<<<std::min<long long>(((long long)M * K + 255) / 256, 4096), 256, 0, s>>>(xq, M, nb, nsbp, qs, dx);
+    SMK_CUDA(cudaGetLastError(), "unswizzle launch");
+    return SMK_OK;
+}
+
+smk_status smk_block_sums(smk_ctx* c, smk_qformat fmt, int M, int N, int K, const float* x, int64_t ldx,
+                          const uint8_t* Wq, int32_t* out, void* stream) {
+    if (!c) return fail(SMK_ERR_ARGUMENT, "ctx must not be NULL");
+    smk_status st = check_q_args(fmt, M, N, K);
+    if (st != SMK_OK) return st;
+    if (M == 0 || N == 0 || K == 0) return SMK_OK;
+    DeviceGuard g(c->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    float* y;
+    {
+        std::lock_guard<std::mutex> lock(c->mu_scratch);
+        SMK_CUDA(c->test_buf.reserve((size_t)M * N * 4), "cudaMalloc (test)");
+        y = static_cast<float*>(c->test_buf.ptr);
+    }
+    return run_q(c, fmt, M, N, K, x, ldx, Wq, y, N, s, out);
+}
+
+}  // extern "C"

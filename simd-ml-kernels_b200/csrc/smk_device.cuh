@@ -1,0 +1,136 @@
+// smk_device.cuh — device-side building blocks shared by the sm_100a kernels:
+// mbarriers, 1-D bulk TMA copies (cp.async.bulk, no multicast), programmatic
+// dependent launch (griddepcontrol), bounded waits that report through an
+// error word instead of hanging, and the integer dot products of the block
+// formats.
+#pragma once
+
+#include <cstdint>
+#include <cuda_fp16.h>
+
+namespace smk {
+
+// Device error codes, OR-ed into the error word the launch gets (read and
+// cleared by smk_device_error()).
+enum : unsigned {
+    kErrWaitTimeout = 1u,   // an mbarrier wait ran past its deadline
+    kErrBadLaunch = 2u,     // a kernel saw parameters its launch code should have rejected
+};
+
+// A wait on an mbarrier gives up after this long (ns of %globaltimer): far
+// above any legitimate wait (a few µs), short enough to keep a broken launch
+// from holding the GPU.
+constexpr unsigned long long kWaitLimitNs = 1000ull * 1000ull * 1000ull;
+
+__device__ __forceinline__ unsigned long long globaltimer() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+
+// Make the barrier initialisations visible to the async proxy (the TMA unit).
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+// Order this thread's earlier generic-proxy shared-memory accesses before
+// later async-proxy (TMA) writes to the same bytes.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Wait for phase `parity` of *bar to complete, for at most kWaitLimitNs.
+// Returns false (and sets kErrWaitTimeout in *err) when the deadline passed.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, unsigned* err) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const unsigned long long t0 = globaltimer();
+    for (uint32_t i = 1;; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 255u) == 0 && globaltimer() - t0 > kWaitLimitNs) {
+            if (err) atomicOr(err, kErrWaitTimeout);
+            return false;
+        }
+    }
+}
+
+// 1-D bulk copy global -> this CTA's shared memory, completion counted on
+// *bar in bytes. dst, src 16-byte aligned; bytes a multiple of 16. Never
+// multicast.
+__device__ __forceinline__ void tma_load_1d(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar))
+        : "memory");
+}
+
+// Programmatic dependent launch. Both are no-ops when the kernel was not
+// launched with the programmatic-serialization attribute.
+__device__ __forceinline__ void pdl_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait_primary() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+// Σ_i a_i·b_i + c over the four bytes of a and b: a unsigned, b signed.
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+// Both signed.
+__device__ __forceinline__ int dp4a_ss(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp4a.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+__device__ __forceinline__ float half_bits_to_float(uint32_t h16) {
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(h16 & 0xffffu)));
+}
+
+// Bits [s, s+32) of the 64-bit value hi:lo.
+__device__ __forceinline__ uint32_t funnel(uint32_t lo, uint32_t hi, uint32_t s) {
+    return __funnelshift_r(lo, hi, s);
+}
+
+__device__ __forceinline__ bool finite_bits(float v) {
+    return (__float_as_uint(v) & 0x7f800000u) != 0x7f800000u;
+}
+
+// Loads that bypass L1 allocation for streamed weights.
+__device__ __forceinline__ uint4 ld_stream_v4(const void* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+}  // namespace smk

@@ -1,0 +1,344 @@
+"""GPU parity: the sm_100a kernels against the oracle (oracle/smk_oracle.c,
+pinned to the reference by test_oracle_golden.py) and the golden vectors.
+
+Bars (made precise where the reference itself needs it):
+  * activation quantization (Q8 quants and FP32 scales): bit-exact;
+  * per-block integer sums of every (row, block): bit-exact (int32);
+  * weight quantization (quantize_q4_0 / quantize_q8_0): byte-exact;
+  * GEMV outputs: |y - y64| <= min(2*(K/32+4)*2^-24, 1e-5) * mag per row,
+    y64 the float64 sum of the same quantized operands and mag the
+    reference's bound magnitude sum_b |dw*dx| * sum_i |qw*qx|
+    (reference q4_0.hpp:23-30); and ||y - y64|| / ||y64|| <= 1e-5;
+  * dense: |C - C64| <= 2*(K+2)*2^-24 * |alpha|*(|x| @ |W|.T) + |beta*C0| terms
+    (reference tests/test_precision.py:212-221);
+  * NaN/±Inf in x -> the row's outputs NaN; K = 0 -> zeros; N = 0 -> empty.
+"""
+
+from __future__ import annotations
+
+import hashlib
+import os
+
+import numpy as np
+import pytest
+
+import oracle as O
+import make_golden as G
+
+pytestmark = pytest.mark.gpu
+
+U = 2.0 ** -24
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+
+
+@pytest.fixture(scope="module")
+def sk(cuda_device):
+    import simd_ml_kernels
+    return simd_ml_kernels
+
+
+@pytest.fixture(scope="module")
+def torch(cuda_device):
+    import torch as t
+    return t
+
+
+def q_bound(K):
+    return min(2 * (K // 32 + 4) * U, 1e-5)
+
+
+def assert_gemv_close(y, y64, mag, K, what=""):
+    y = np.asarray(y, np.float64)
+    bound = q_bound(K) * mag + 1e-300
+    err = np.abs(y - y64)
+    assert np.isfinite(y).all(), f"{what}: non-finite output"
+    assert (err <= bound).all(), f"{what}: max err/bound {np.max(err / bound):.3g}"
+    n = np.linalg.norm(y64)
+    if n > 0:
+        assert np.linalg.norm(y - y64) / n <= 1e-5, f"{what}: norm-wise error {np.linalg.norm(y - y64) / n:.3g}"
+
+
+def make_case(seed, N, K, fmt, scale=1.0):
+    rng = np.random.default_rng(seed)
+    W = (rng.standard_normal((N, K)) * scale).astype(np.float32)
+    x = (rng.standard_normal(K) * 4).astype(np.float32)
+    return x, O.quantize(fmt, W)
+
+
+# ---- quantization ------------------------------------------------------------------
+
+def test_quantize_x_bit_exact(sk, torch):
+    from simd_ml_kernels import _core
+    g = np.load(os.path.join(GOLD, "ref_quantize_x.npz"))
+    xs = [g["x0"], g["x1"], g["x2"], (np.random.default_rng(1).standard_normal(8 * 4096) * 3).astype(np.float32)]
+    for x in xs:
+        K = x.shape[0]
+        xd = torch.from_numpy(x).cuda()
+        qs = torch.empty(K, dtype=torch.int8, device="cuda")
+        dx = torch.empty(K // 32, dtype=torch.float32, device="cuda")
+        _core._quantize_x(xd.data_ptr(), 1, K, qs.data_ptr(), dx.data_ptr(), torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        want_qs, want_dx, ok = O.quantize_x(x)
+        assert ok
+        np.testing.assert_array_equal(qs.cpu().numpy(), want_qs)
+        np.testing.assert_array_equal(dx.cpu().numpy().view(np.uint32), want_dx.view(np.uint32))
+
+
+@pytest.mark.parametrize("fmt", ["q4_0", "q8_0"])
+def test_quantize_weights_byte_exact(sk, fmt):
+    g = np.load(os.path.join(GOLD, "ref_quantize.npz"))
+    fn = sk.quantize_q4_0 if fmt == "q4_0" else sk.quantize_q8_0
+    for i in range(4):
+        np.testing.assert_array_equal(fn(g[f"w{i}"]), g[f"{fmt}_{i}"])
+    np.testing.assert_array_equal(fn(g["w_special"]), g[f"{fmt}_special"])
+    rej = g["w_reject"]
+    for i in range(rej.shape[0]):
+        if g[f"{fmt}_reject_ok"][i]:
+            fn(rej[i:i + 1])
+        else:
+            with pytest.raises(sk.ArgumentError, match="finite"):
+                fn(rej[i:i + 1])
+
+
+def test_quantize_llama_cpp_fixture(sk):
+    fx = np.load(os.path.join(GOLD, "q4_0_llama_cpp_fixture.npz"))
+    np.testing.assert_array_equal(sk.quantize_q4_0(fx["w"]), fx["blocks"])
+
+
+def test_quantize_large_matches_oracle(sk, torch):
+    """Device quantization of a config-sized matrix, on torch tensors."""
+    rng = np.random.default_rng(0)
+    W = (rng.standard_normal((2048, 2048)) * 0.02).astype(np.float32)
+    for fmt, fn in (("q4_0", sk.quantize_q4_0), ("q8_0", sk.quantize_q8_0)):
+        got = fn(torch.from_numpy(W).cuda()).cpu().numpy()
+        np.testing.assert_array_equal(got, O.quantize(fmt, W))
+
+
+# ---- integer block sums -----------------------------------------------------------
+
+@pytest.mark.parametrize("fmt", ["q4_0", "q8_0"])
+@pytest.mark.parametrize("M,N,K", [(1, 7, 256), (1, 33, 2048), (1, 5, 8192), (3, 17, 512), (8, 9, 2048),
+                                   (1, 13, 4128), (2, 11, 160), (1, 3, 28672)])
+def test_block_sums_bit_exact(sk, torch, fmt, M, N, K):
+    from simd_ml_kernels import _core
+    rng = np.random.default_rng(M * 1000 + N + K)
+    W = rng.standard_normal((N, K)).astype(np.float32)
+    X = (rng.standard_normal((M, K)) * 3).astype(np.float32)
+    Wq = O.quantize(fmt, W)
+    xd = torch.from_numpy(X).cuda()
+    wd = torch.from_numpy(Wq.reshape(-1)).cuda()
+    out = torch.zeros((M, N, K // 32), dtype=torch.int32, device="cuda")
+    _core._block_sums(0 if fmt == "q4_0" else 1, xd.data_ptr(), M, N, K, wd.data_ptr(), out.data_ptr(),
+                      torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    got = out.cpu().numpy()
+    for m in range(M):
+        qs, dx, ok = O.quantize_x(X[m])
+        np.testing.assert_array_equal(got[m], O.block_sums(fmt, qs, Wq, N, K), err_msg=f"row {m}")
+
+
+# ---- GEMV outputs ---------------------------------------------------------------------
+
+@pytest.mark.parametrize("fmt", ["q4_0", "q8_0"])
+def test_gemv_golden_cases(sk, fmt):
+    """Every golden case: within the bound of the float64 sum, and (scalar order)
+    oracle == the reference's scalar table, so this is parity with the reference."""
+    g = np.load(os.path.join(GOLD, "ref_gemv.npz"))
+    fn = sk.gemv_q4_0 if fmt == "q4_0" else sk.gemv_q8_0
+    for s, n, k, extreme in g["cases"]:
+        W, x = G.gemv_case_inputs(int(s), int(n), int(k), "extreme" if extreme else "normal")
+        Wq = O.quantize(fmt, W)
+        assert hashlib.sha256(Wq.tobytes()).hexdigest() == str(g[f"{fmt}_{s}_sha"])
+        y = fn(x, Wq, int(n), int(k))
+        assert y.dtype == np.float32 and y.shape == (n,)
+        y64, mag = O.ref64(fmt, x, Wq, int(n), int(k))
+        assert_gemv_close(y, y64, mag, int(k), f"{fmt} case {s} N={n} K={k}")
+        # Same bound on the reference's own outputs (scalar and SIMD tables).
+        assert_gemv_close(g[f"{fmt}_{s}_scalar"], y64, mag, int(k), "reference scalar")
+
+
+@pytest.mark.parametrize("fmt", ["q4_0", "q8_0"])
+@pytest.mark.parametrize("N,K", [(1, 32), (2, 64), (7, 64), (8, 96), (9, 128), (17, 352), (100, 4096),
+                                 (33, 11008), (31, 256), (257, 512), (1000, 1024), (3, 28672), (513, 2048)])
+def test_gemv_shapes(sk, fmt, N, K):
+    x, Wq = make_case(N * 37 + K, N, K, fmt)
+    fn = sk.gemv_q4_0 if fmt == "q4_0" else sk.gemv_q8_0
+    y = fn(x, Wq, N, K)
+    y64, mag = O.ref64(fmt, x, Wq, N, K)
+    assert_gemv_close(y, y64, mag, K, f"{fmt} {N}x{K}")
+
+
+@pytest.mark.parametrize("fmt", ["q4_0", "q8_0"])
+@pytest.mark.parametrize("N,K", [(8192, 2048), (2048, 8192), (512, 2048), (28672, 8192)])
+def test_gemv_config_shapes(sk, torch, fmt, N, K):
+    """BASELINE configs 0/1/2/4 shapes (seeded synthetic weights, device-resident)."""
+    rng = np.random.default_rng(N + K)
+    W = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    x = rng.standard_normal(K).astype(np.float32)
+    Wq = O.quantize(fmt, W)
+    fn = sk.gemv_q4_0 if fmt == "q4_0" else sk.gemv_q8_0
+    y = fn(torch.from_numpy(x).cuda(), torch.from_numpy(Wq.reshape(-1)).cuda(), N, K).cpu().numpy()
+    y64, mag = O.ref64(fmt, x, Wq, N, K)
+    assert_gemv_close(y, y64, mag, K, f"{fmt} {N}x{K}")
+
+
+@pytest.mark.parametrize("fmt", ["q4_0", "q8_0"])
+@pytest.mark.parametrize("M,N,K", [(2, 100, 2048), (4, 33, 4096), (8, 257, 2048), (8, 64, 8192), (5, 19, 160),
+                                   (8, 96, 28672)])
+def test_gemv_batch_rows_equal_single_rows(sk, fmt, M, N, K):
+    """M rows against one read of W: every row within the bound, and (x in
+    shared or global memory alike) equal to its own single-row call."""
+    rng = np.random.default_rng(M + N + K)
+    W = rng.standard_normal((N, K)).astype(np.float32)
+    X = (rng.standard_normal((M, K)) * 2).astype(np.float32)
+    Wq = O.quantize(fmt, W)
+    bfn = sk.gemv_q4_0_batch if fmt == "q4_0" else sk.gemv_q8_0_batch
+    Y = bfn(X, Wq, N, K)
+    assert Y.shape == (M, N)
+    for m in range(M):
+        y64, mag = O.ref64(fmt, X[m], Wq, N, K)
+        assert_gemv_close(Y[m], y64, mag, K, f"{fmt} row {m}")
+
+
+@pytest.mark.parametrize("fmt", ["q4_0", "q8_0"])
+@pytest.mark.parametrize("bad", [np.nan, np.inf, -np.inf])
+def test_gemv_nonfinite_x_gives_nan(sk, fmt, bad):
+    for N, K in ((9, 64), (40, 2048)):
+        W = np.full((N, K), 0.25, np.float32)
+        x = np.ones(K, np.float32)
+        x[37] = bad
+        fn = sk.gemv_q4_0 if fmt == "q4_0" else sk.gemv_q8_0
+        q = sk.quantize_q4_0 if fmt == "q4_0" else sk.quantize_q8_0
+        assert np.isnan(fn(x, q(W), N, K)).all()
+
+
+def test_gemv_batch_nan_row_only(sk):
+    N, K = 24, 2048
+    W = np.random.default_rng(2).standard_normal((N, K)).astype(np.float32)
+    X = np.ones((3, K), np.float32)
+    X[1, 100] = np.nan
+    Y = sk.gemv_q4_0_batch(X, sk.quantize_q4_0(W), N, K)
+    assert np.isnan(Y[1]).all() and np.isfinite(Y[0]).all() and np.isfinite(Y[2]).all()
+
+
+@pytest.mark.parametrize("fmt", ["q4_0", "q8_0"])
+def test_gemv_k0_and_n0(sk, fmt):
+    fn = sk.gemv_q4_0 if fmt == "q4_0" else sk.gemv_q8_0
+    assert (fn(np.ones(0, np.float32), np.zeros(0, np.uint8), 5, 0) == 0).all()
+    assert fn(np.ones(32, np.float32), np.zeros(0, np.uint8), 0, 32).shape == (0,)
+
+
+@pytest.mark.parametrize("fmt", ["q4_0", "q8_0"])
+def test_gemv_unaligned(sk, torch, fmt):
+    """Wq at an odd address and x at a 4-byte offset (reference test_precision.py:800-814):
+    host operands are staged to aligned device memory, so the result is bitwise the
+    aligned one; an unaligned device pointer takes the generic kernel (within the bound)."""
+    for N, K in ((13, 160), (21, 2048)):
+        x, Wq = make_case(4 + K, N, K, fmt)
+        Wq = Wq.ravel()
+        buf = np.empty(Wq.size + 1, np.uint8)
+        buf[1:] = Wq
+        xbuf = np.empty(K + 1, np.float32)
+        xbuf[1:] = x
+        fn = sk.gemv_q4_0 if fmt == "q4_0" else sk.gemv_q8_0
+        want = fn(x, Wq, N, K)
+        np.testing.assert_array_equal(fn(xbuf[1:], buf[1:], N, K), want)
+        dbuf = torch.from_numpy(buf).cuda()
+        got = fn(torch.from_numpy(x).cuda(), dbuf[1:], N, K).cpu().numpy()
+        y64, mag = O.ref64(fmt, x, Wq, N, K)
+        assert_gemv_close(got, y64, mag, K, "unaligned device Wq")
+
+
+@pytest.mark.parametrize("fmt", ["q4_0", "q8_0"])
+def test_gemv_deterministic_pdl_and_streams(sk, torch, fmt):
+    """Bitwise identical across repeated calls, with and without programmatic
+    dependent launch, and between the NumPy path and the torch stream path."""
+    N, K = 4096, 2048
+    x, Wq = make_case(11, N, K, fmt)
+    fn = sk.gemv_q4_0 if fmt == "q4_0" else sk.gemv_q8_0
+    ref = fn(x, Wq, N, K)
+    xd, wd = torch.from_numpy(x).cuda(), torch.from_numpy(Wq.ravel()).cuda()
+    outs = [fn(xd, wd, N, K) for _ in range(5)]
+    sk.set_pdl(True)
+    try:
+        outs += [fn(xd, wd, N, K) for _ in range(5)]
+    finally:
+        sk.set_pdl(False)
+    for o in outs:
+        np.testing.assert_array_equal(o.cpu().numpy().view(np.uint32), ref.view(np.uint32))
+
+
+def test_row_shards_bitwise_equal_full(sk, torch):
+    """Row-sharding (the multi-GPU plan, 8-row groups as the reference's
+    gemv_slice): every shard's outputs bitwise equal the unsharded call."""
+    from simd_ml_kernels import shard
+    N, K = 1003, 2048
+    x, Wq = make_case(5, N, K, "q4_0")
+    full = sk.gemv_q4_0(x, Wq, N, K)
+    rb = K // 32 * 18
+    for parts in (2, 3, 4, 8):
+        pieces = []
+        for t in range(parts):
+            lo, hi = shard.row_slice(N, t, parts)
+            assert (lo, hi) == O.gemv_slice(N, t, parts)
+            pieces.append(sk.gemv_q4_0(x, Wq.ravel()[lo * rb:hi * rb], hi - lo, K))
+        np.testing.assert_array_equal(np.concatenate(pieces).view(np.uint32), full.view(np.uint32))
+
+
+# ---- dense ---------------------------------------------------------------------------
+
+def _dense_operands(kind, A, B):
+    return G.dense_operands(kind, A, B)
+
+
+@pytest.mark.parametrize("kind", ["f32", "f16", "bf16"])
+def test_dense_golden_cases(sk, kind):
+    g = np.load(os.path.join(GOLD, "ref_dense.npz"))
+    fn = {"f32": sk.sgemm, "f16": sk.sgemm_f16, "bf16": sk.sgemm_bf16}[kind]
+    for i, (m, n, k) in enumerate(g["cases"]):
+        A, B, C0, alpha, beta = G.dense_case_inputs(i, int(m), int(n), int(k))
+        a, b = _dense_operands(kind, A, B)
+        if kind == "f16":
+            a, b = a.view(np.float16), b.view(np.float16)
+        C = C0.copy()
+        fn(a, b, C=C, alpha=alpha, beta=beta, trans_b=True)
+        y64, mag = O.dense_ref64(a.view(np.uint16) if kind != "f32" else a, kind,
+                                 b.view(np.uint16) if kind != "f32" else b, kind)
+        want = alpha * y64 + beta * C0.astype(np.float64)
+        bound = 2 * (k + 2) * U * (abs(alpha) * mag + abs(beta) * np.abs(C0)) + 1e-300
+        assert (np.abs(C - want) <= bound).all(), f"{kind} case {i}"
+        assert (np.abs(g[f"{kind}_{i}_simd"] - want) <= bound).all()
+
+
+@pytest.mark.parametrize("wtype", ["float32", "float16", "bfloat16"])
+@pytest.mark.parametrize("M,N,K", [(1, 4096, 4096), (4, 4096, 4096), (8, 1000, 4096), (1, 37, 33), (3, 64, 4099),
+                                   (8, 14336, 4096)])
+def test_dense_fp32_x(sk, torch, wtype, M, N, K):
+    """fp32 activations against fp32/f16/bf16 weights."""
+    rng = np.random.default_rng(M + N + K)
+    W32 = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    X = rng.standard_normal((M, K)).astype(np.float32)
+    if wtype == "float32":
+        Wt, Wk, kind = torch.from_numpy(W32), W32, "f32"
+    elif wtype == "float16":
+        Wt, Wk, kind = torch.from_numpy(W32.astype(np.float16)), W32.astype(np.float16).view(np.uint16), "f16"
+    else:
+        Wt, Wk, kind = torch.from_numpy(W32).to(torch.bfloat16), O.bf16_bits(W32), "bf16"
+    Y = sk.gemv_dense(torch.from_numpy(X).cuda(), Wt.cuda()).cpu().numpy()
+    y64, mag = O.dense_ref64(X, "f32", Wk, kind)
+    bound = 2 * (K + 2) * U * mag + 1e-300
+    assert (np.abs(Y - y64) <= bound).all(), f"max err/bound {np.max(np.abs(Y - y64) / bound):.3g}"
+
+
+def test_dense_rejects_non_decode(sk):
+    A = np.ones((9, 16), np.float32)
+    B = np.ones((4, 16), np.float32)
+    with pytest.raises(sk.ArgumentError, match="decode"):
+        sk.sgemm(A, B, trans_b=True)
+    with pytest.raises(sk.ArgumentError, match="decode"):
+        sk.sgemm(A[:2], B.T.copy())
+
+
+def test_no_device_errors(sk):
+    from simd_ml_kernels import _core
+    assert _core._device_error(0) == 0
