@@ -195,13 +195,14 @@ py::object gemv_blocks(const py::handle& xh, const py::handle& wh, py::ssize_t N
         result = out;
     }
     const bool all_device = x.device && w.device && y_device;
+    const bool async = all_device && !stream.is_none();
+    void* strm = async ? reinterpret_cast<void*>(stream.cast<uintptr_t>()) : nullptr;   // read with the GIL held
     smk_status st;
     {
         py::gil_scoped_release release;
-        if (all_device && !stream.is_none()) {
+        if (async) {
             st = smk_gemv_q(c, fmt, M, (int)N, (int)K, static_cast<const float*>(x.ptr), K,
-                            static_cast<const uint8_t*>(w.ptr), yp, N,
-                            reinterpret_cast<void*>(stream.cast<uintptr_t>()));
+                            static_cast<const uint8_t*>(w.ptr), yp, N, strm);
         } else {
             st = smk_gemv_q_host(c, fmt, M, (int)N, (int)K, static_cast<const float*>(x.ptr),
                                  static_cast<const uint8_t*>(w.ptr), yp);
@@ -288,13 +289,13 @@ py::object dense_call(smk_dtype wt, smk_dtype xt, const Arr& A, const Arr& B, in
         c_device = ci.device;
         result = C;
     }
-    const bool all_device = A.device && B.device && c_device;
+    const bool async = A.device && B.device && c_device && !stream.is_none();
+    void* strm = async ? reinterpret_cast<void*>(stream.cast<uintptr_t>()) : nullptr;   // read with the GIL held
     smk_status st;
     {
         py::gil_scoped_release release;
-        if (all_device && !stream.is_none())
-            st = smk_gemv_dense(c, wt, xt, M, N, K, alpha, A.ptr, K, B.ptr, K, beta, cp, N,
-                                reinterpret_cast<void*>(stream.cast<uintptr_t>()));
+        if (async)
+            st = smk_gemv_dense(c, wt, xt, M, N, K, alpha, A.ptr, K, B.ptr, K, beta, cp, N, strm);
         else
             st = smk_gemv_dense_host(c, wt, xt, M, N, K, alpha, A.ptr, B.ptr, beta, cp);
     }

@@ -370,7 +370,7 @@ __global__ void __launch_bounds__(256) quantize_w_kernel(const float* __restrict
             int hi[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i) hi[i] = __shfl_down_sync(gmask, q[i], 4, 8);
-            const unsigned short h = __half_as_ushort(__float2half_rn(d));
+            const uint32_t h = f32_to_f16_bits(d);
             if (gq < 4) {
 #pragma unroll
                 for (int i = 0; i < 4; ++i) o[2 + gq * 4 + i] = (uint8_t)(q[i] | (hi[i] << 4));
@@ -393,7 +393,7 @@ __global__ void __launch_bounds__(256) quantize_w_kernel(const float* __restrict
 #pragma unroll
             for (int i = 0; i < 4; ++i) o[2 + gq * 4 + i] = (uint8_t)(int8_t)(int)roundf(__fmul_rn(v[i], id));
             if (gq == 0) {
-                const unsigned short h = __half_as_ushort(__float2half_rn(d));
+                const uint32_t h = f32_to_f16_bits(d);
                 o[0] = (uint8_t)(h & 0xff);
                 o[1] = (uint8_t)(h >> 8);
                 if (!fin || (h & 0x7fffu) == 0x7c00u) atomicOr(reject, 1u);

@@ -115,6 +115,34 @@ __device__ __forceinline__ float half_bits_to_float(uint32_t h16) {
     return __half2float(__ushort_as_half(static_cast<unsigned short>(h16 & 0xffffu)));
 }
 
+// binary32 -> binary16 bit pattern, round to nearest even, by integer
+// arithmetic: the float is m·2^(e−150) (e its biased exponent, 1 for
+// subnormals), the half with exponent Eh >= −14 has ulp 2^(Eh−10), so the
+// value is m·2^−s half ulps with s = 140 + Eh − e; ((Eh + 15) << 10) + q − 1024
+// is then the pattern for every rounded q (a carry to 2048 moves into the
+// exponent, Eh = −14 gives the subnormals), and patterns at or past 0x7c00
+// overflow to infinity. NaN -> 0x7e00 with the sign.
+__device__ __forceinline__ uint32_t f32_to_f16_bits(float f) {
+    const uint32_t u = __float_as_uint(f);
+    const uint32_t sign = (u >> 16) & 0x8000u;
+    const uint32_t a = u & 0x7fffffffu;
+    if (a > 0x7f800000u) return sign | 0x7e00u;
+    if (a == 0x7f800000u) return sign | 0x7c00u;
+    int e = (int)(a >> 23);
+    uint32_t m = a & 0x7fffffu;
+    if (e == 0) e = 1; else m |= 0x800000u;
+    const int Eh = max(e - 127, -14);
+    const int s = 140 + Eh - e;
+    uint32_t q = 0;
+    if (s <= 31) {
+        q = m >> s;
+        const uint32_t rem = m & ((1u << s) - 1u), half = 1u << (s - 1);
+        if (rem > half || (rem == half && (q & 1u))) ++q;
+    }
+    const int bits = ((Eh + 15) << 10) + (int)q - 1024;
+    return sign | (bits >= 0x7c00 ? 0x7c00u : (uint32_t)bits);
+}
+
 // Bits [s, s+32) of the 64-bit value hi:lo.
 __device__ __forceinline__ uint32_t funnel(uint32_t lo, uint32_t hi, uint32_t s) {
     return __funnelshift_r(lo, hi, s);
