@@ -121,6 +121,28 @@ smk_status smk_quantize_x(smk_ctx* ctx, int M, int K, const float* x, int64_t ld
 smk_status smk_block_sums(smk_ctx* ctx, smk_qformat fmt, int M, int N, int K, const float* x, int64_t ldx,
                           const uint8_t* Wq, int32_t* out, void* stream);
 
+/* ---- quantized decode GEMV without any allocation -------------------------
+ * No counterpart in the reference. For callers that cannot call cudaMalloc:
+ * hosts whose memory pools own every device allocation, servers that plan all
+ * memory at start-up and allocate nothing per request, plugins inside either.
+ * Same result as smk_gemv_q (same kernels), with these differences:
+ *   - no smk_ctx: runs on the calling thread's current device; Wq, x and y
+ *     are device memory; errors through smk_last_error();
+ *   - the quantized activations go to a fixed scratch array of
+ *     SMK_NOALLOC_SCRATCH_BYTES inside the library, which every GPU that loads
+ *     the library holds until the process exits; a call needing more
+ *     (M * ceil(K/256) > 3276) is rejected with SMK_ERR_ARGUMENT;
+ *   - the first call on each device looks up the array's device address and
+ *     the SM count (set-up, once per device, with that device current); make
+ *     that first call before any stream capture;
+ *   - every call on a device shares the one array (it keeps the last call's
+ *     contents), so calls whose kernels overlap on the GPU — on different
+ *     streams, or from different threads — race: serialise them.
+ * It calls no cudaMalloc, cudaFree or other allocating routine. */
+#define SMK_NOALLOC_SCRATCH_BYTES (1u << 20)
+smk_status smk_gemv_q_noalloc(smk_qformat fmt, int M, int N, int K, const float* x, int64_t ldx, const uint8_t* Wq,
+                              float* y, int64_t ldy, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

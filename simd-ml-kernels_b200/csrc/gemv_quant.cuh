@@ -48,6 +48,9 @@ struct QGemvParams {
     unsigned* err;         // device error word
 };
 
+// Sets the message smk_last_error() returns on this thread.
+void set_last_error(const char* msg);
+
 // CTAs per SM of `fn` at this launch shape; raises the kernel's dynamic
 // shared-memory limit as needed. Cached per (device, kernel, threads, smem).
 cudaError_t occupancy(const void* fn, int threads, size_t smem, int* per_sm);

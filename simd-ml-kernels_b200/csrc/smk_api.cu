@@ -100,6 +100,8 @@ size_t align256(size_t n) { return (n + 255) & ~(size_t)255; }
 
 }  // namespace
 
+void smk::set_last_error(const char* msg) { g_last_error = msg; }
+
 struct smk_ctx {
     int device = 0;
     int num_sms = 148;
