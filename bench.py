@@ -117,17 +117,28 @@ class ClockSampler:
 # ---- the reference's CPU kernel -------------------------------------------------------
 
 def llc_bytes() -> int:
-    best = 0
-    base = "/sys/devices/system/cpu/cpu0/cache"
-    try:
-        for idx in os.listdir(base):
-            with open(os.path.join(base, idx, "size")) as f:
-                s = f.read().strip()
-            v = int(s[:-1]) * (1024 if s.endswith("K") else 1024 * 1024 if s.endswith("M") else 1)
-            best = max(best, v)
-    except OSError:
-        pass
-    return best or 64 << 20
+    """Total last-level cache of the host: every distinct cache instance of the
+    highest level, summed (a multi-die CPU has several L3s)."""
+    import glob as _glob
+
+    def size(path):
+        s = open(path).read().strip()
+        return int(s[:-1]) * {"K": 1 << 10, "M": 1 << 20, "G": 1 << 30}.get(s[-1], 1) if s[-1].isalpha() else int(s)
+
+    seen, best_level, total = set(), 0, 0
+    for d in _glob.glob("/sys/devices/system/cpu/cpu[0-9]*/cache/index[0-9]*"):
+        try:
+            level = int(open(os.path.join(d, "level")).read())
+            shared = open(os.path.join(d, "shared_cpu_list")).read().strip()
+            sz = size(os.path.join(d, "size"))
+        except (OSError, ValueError):
+            continue
+        if level > best_level:
+            seen, best_level, total = set(), level, 0
+        if level == best_level and shared not in seen:
+            seen.add(shared)
+            total += sz
+    return total or 64 << 20
 
 
 def reference_setup(threads: int):
@@ -275,6 +286,13 @@ def gpu_bench(args, rank: int, world: int, local_rank: int) -> dict | None:
         kernel_ms = s2.elapsed_time(e2) * steps / (reps * chunk)
         del gk
     del g_full, g_rem
+
+    if args.only_gemv:
+        if rank == 0:
+            return {"metric": METRIC, "value": round(STEP_BYTES * world * steps / (ms_max * 1e-3) / 1e9, 2),
+                    "unit": "GB/s", "n_gpus": world, "steps": steps, "ms_per_step": ms_max / steps,
+                    "only_gemv": True}
+        return None
 
     # End to end through the public API: x from pinned host memory, y back to
     # host memory, weights resident on the device (uploaded once, as a model's).
@@ -478,6 +496,8 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--all", action="store_true", help="also time configs 1, 3 and 4 (one GPU)")
     ap.add_argument("--cpu-baseline-seconds", type=float, default=8.0)
+    ap.add_argument("--only-gemv", action="store_true",
+                    help="time the config-0 GEMV only (no e2e, Llama stack or CPU baseline): for profilers")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -515,7 +535,7 @@ def main() -> None:
     try:
         out = gpu_bench(args, rank, world, local_rank)
         if rank == 0 and out is not None:
-            if world == 1:
+            if world == 1 and not args.only_gemv:
                 cb = time_reference(None, 2, args.cpu_baseline_seconds)
                 out["cpu_baseline"] = None if cb is None else {
                     "value": round(cb["value"], 3), "unit": "GB/s", "cores": cb["cores"], "kind": "reference",

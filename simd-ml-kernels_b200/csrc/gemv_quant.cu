@@ -50,40 +50,67 @@ __device__ __forceinline__ size_t xd_off(int M, int nsbp, int m, int j, int sb) 
 // Eight threads per 32-value block, four values each; tid in [0, nthreads),
 // nthreads a multiple of 8. Bit-exact with the reference's quantize_x_q8
 // (q8_0_scalar.cpp:45-61,113-118): amax/127 and 1/d as IEEE divisions,
-// w·id rounded once, then rounded half away from zero.
+// w·id rounded once, then rounded half away from zero. Each thread first
+// loads the values of up to kXUnroll blocks, so the prologue of a GEMV waits
+// for one round trip to L2 rather than one per block.
+constexpr int kXUnroll = 4;
+
+__device__ __forceinline__ float4 load_x4(const float* p) {
+    if ((reinterpret_cast<uintptr_t>(p) & 15) == 0) return *reinterpret_cast<const float4*>(p);
+    return make_float4(p[0], p[1], p[2], p[3]);
+}
+
+__device__ __forceinline__ void quantize_x_block(float4 v, int gq, unsigned gmask, int M, int nsbp, int m, int b,
+                                                 uint8_t* xb) {
+    unsigned fin = finite_bits(v.x) & finite_bits(v.y) & finite_bits(v.z) & finite_bits(v.w);
+    float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1) {
+        amax = fmaxf(amax, __shfl_xor_sync(gmask, amax, o));
+        fin &= __shfl_xor_sync(gmask, fin, o);
+    }
+    const float d = __fdiv_rn(amax, 127.0f);
+    float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+    if (!(id <= FLT_MAX)) id = 0.0f;
+    const int q0 = fin ? (int)roundf(__fmul_rn(v.x, id)) : 0;
+    const int q1 = fin ? (int)roundf(__fmul_rn(v.y, id)) : 0;
+    const int q2 = fin ? (int)roundf(__fmul_rn(v.z, id)) : 0;
+    const int q3 = fin ? (int)roundf(__fmul_rn(v.w, id)) : 0;
+    const uint32_t word = (uint32_t)(q0 & 0xff) | ((uint32_t)(q1 & 0xff) << 8) | ((uint32_t)(q2 & 0xff) << 16) |
+                          ((uint32_t)(q3 & 0xff) << 24);
+    int s = q0 + q1 + q2 + q3;
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1) s += __shfl_xor_sync(gmask, s, o);
+    const int sb = b >> 3, j = b & 7;
+    *reinterpret_cast<uint32_t*>(xb + xq_off(nsbp, m, gq >> 2, j, sb) + (gq & 3) * 4) = word;
+    if (gq == 0) {
+        const float dxv = fin ? d : __int_as_float(0x7fc00000);
+        *reinterpret_cast<float2*>(xb + xd_off(M, nsbp, m, j, sb)) = make_float2(dxv, __int_as_float(-8 * s));
+    }
+}
+
 __device__ __forceinline__ void quantize_x_rows(const float* __restrict__ x, long long ldx, int M, int nb,
                                                 int nsbp, uint8_t* xb, int tid, int nthreads) {
     const int gq = tid & 7;
     const unsigned gmask = 0xffu << ((tid & 31) & ~7);
-    const int total = M * nb;
-    for (int blk = tid >> 3; blk < total; blk += nthreads >> 3) {
-        const int m = blk / nb, b = blk - m * nb;
-        const float* xp = x + (size_t)m * ldx + (size_t)b * kQK + gq * 4;
-        const float v0 = xp[0], v1 = xp[1], v2 = xp[2], v3 = xp[3];
-        unsigned fin = finite_bits(v0) & finite_bits(v1) & finite_bits(v2) & finite_bits(v3);
-        float amax = fmaxf(fmaxf(fabsf(v0), fabsf(v1)), fmaxf(fabsf(v2), fabsf(v3)));
+    const int total = M * nb, stride = nthreads >> 3;
+    for (int base = tid >> 3; base < total; base += kXUnroll * stride) {
+        float4 v[kXUnroll];
 #pragma unroll
-        for (int o = 4; o > 0; o >>= 1) {
-            amax = fmaxf(amax, __shfl_xor_sync(gmask, amax, o));
-            fin &= __shfl_xor_sync(gmask, fin, o);
+        for (int u = 0; u < kXUnroll; ++u) {
+            const int blk = base + u * stride;
+            if (blk < total) {
+                const int m = blk / nb, b = blk - m * nb;
+                v[u] = load_x4(x + (size_t)m * ldx + (size_t)b * kQK + gq * 4);
+            }
         }
-        const float d = __fdiv_rn(amax, 127.0f);
-        float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-        if (!(id <= FLT_MAX)) id = 0.0f;
-        const int q0 = fin ? (int)roundf(__fmul_rn(v0, id)) : 0;
-        const int q1 = fin ? (int)roundf(__fmul_rn(v1, id)) : 0;
-        const int q2 = fin ? (int)roundf(__fmul_rn(v2, id)) : 0;
-        const int q3 = fin ? (int)roundf(__fmul_rn(v3, id)) : 0;
-        const uint32_t word = (uint32_t)(q0 & 0xff) | ((uint32_t)(q1 & 0xff) << 8) | ((uint32_t)(q2 & 0xff) << 16) |
-                              ((uint32_t)(q3 & 0xff) << 24);
-        int s = q0 + q1 + q2 + q3;
 #pragma unroll
-        for (int o = 4; o > 0; o >>= 1) s += __shfl_xor_sync(gmask, s, o);
-        const int sb = b >> 3, j = b & 7;
-        *reinterpret_cast<uint32_t*>(xb + xq_off(nsbp, m, gq >> 2, j, sb) + (gq & 3) * 4) = word;
-        if (gq == 0) {
-            const float dxv = fin ? d : __int_as_float(0x7fc00000);
-            *reinterpret_cast<float2*>(xb + xd_off(M, nsbp, m, j, sb)) = make_float2(dxv, __int_as_float(-8 * s));
+        for (int u = 0; u < kXUnroll; ++u) {
+            const int blk = base + u * stride;
+            if (blk < total) {
+                const int m = blk / nb, b = blk - m * nb;
+                quantize_x_block(v[u], gq, gmask, M, nsbp, m, b, xb);
+            }
         }
     }
 }
@@ -215,7 +242,12 @@ __device__ __forceinline__ void issue_item(const QGemvParams& p, int it, int gw,
     const uint32_t bytes = (uint32_t)cnt * SBB;
     if (lane == 0) mbar_arrive_expect_tx(&bars[slot], bytes * rows);
     __syncwarp();
-    if (lane < rows) {
+    if (p.ksteps == 1 && p.G == p.nsbp) {
+        // Whole rows, back to back in memory and in the stage: one copy.
+        if (lane == 0)
+            tma_load_1d(stages + (size_t)slot * 32 * SBB, p.w + (size_t)tile * p.TR * ((size_t)p.nsbp * SBB),
+                        bytes * rows, &bars[slot]);
+    } else if (lane < rows) {
         const size_t row = (size_t)tile * p.TR + lane;
         const uint8_t* src = p.w + row * ((size_t)p.nsbp * SBB) + (size_t)sb0 * SBB;
         tma_load_1d(stages + (size_t)slot * 32 * SBB + (size_t)lane * p.G * SBB, src, bytes, &bars[slot]);
@@ -470,8 +502,13 @@ cudaError_t launch_fast_m(const LaunchCfg& c, const QGemvParams& p, size_t smem,
     cudaError_t e = occupancy_cached((const void*)k, c.warps * 32, smem, &per_sm);
     if (e != cudaSuccess) return e;
     if (per_sm < 1) return cudaErrorInvalidConfiguration;
-    const long long want = ((long long)p.ntiles + c.warps - 1) / c.warps;
-    const long long grid = std::min<long long>(want, (long long)per_sm * c.num_sms);
+    // Persistent: at most ctas_per_sm CTAs per SM (one by default, which
+    // leaves room for the next GEMV's CTA beside it under programmatic
+    // dependent launch); small problems still spread over every SM.
+    const long long cap = (long long)std::min(per_sm, std::max(c.ctas_per_sm, 1)) * c.num_sms;
+    const long long want = std::max<long long>(((long long)p.ntiles + c.warps - 1) / c.warps,
+                                               std::min<long long>(p.ntiles, c.num_sms));
+    const long long grid = std::min(want, cap);
     return launch(k, dim3((unsigned)std::max<long long>(grid, 1)), dim3(c.warps * 32), smem, c, p);
 }
 

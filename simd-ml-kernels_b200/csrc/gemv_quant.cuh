@@ -61,6 +61,7 @@ struct LaunchCfg {
     bool pdl;              // programmatic dependent launch
     int num_sms;
     int warps;             // warps per CTA of the fast kernel
+    int ctas_per_sm = 1;   // cap on resident CTAs per SM of the fast kernel
 };
 
 // Quantize x into the layout above in global memory (xq_total_bytes).

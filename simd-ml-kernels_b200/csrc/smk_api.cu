@@ -107,8 +107,9 @@ struct smk_ctx {
     int num_sms = 148;
     size_t smem_optin = 227 * 1024;
     bool pdl = false;
-    int warps = 4;
-    int stages = 4;
+    int warps = 8;
+    int stages = 2;
+    int ctas_per_sm = 1;
     unsigned* d_err = nullptr;      // device error word
     unsigned* d_reject = nullptr;   // quantizer rejection flag
     std::mutex mu_scratch;                    // guards scratch and test_buf
@@ -126,6 +127,7 @@ smk::LaunchCfg cfg_for(smk_ctx* c, cudaStream_t s) {
     l.pdl = c->pdl;
     l.num_sms = c->num_sms;
     l.warps = c->warps;
+    l.ctas_per_sm = c->ctas_per_sm;
     return l;
 }
 
@@ -268,6 +270,10 @@ smk_status smk_ctx_set(smk_ctx* c, int option, long long v) {
             if (v < 2 || v > 8) return fail(SMK_ERR_ARGUMENT, "stages must be in 2..8");
             c->stages = (int)v;
             return SMK_OK;
+        case SMK_OPT_CTAS_PER_SM:
+            if (v < 1 || v > 8) return fail(SMK_ERR_ARGUMENT, "CTAs per SM must be in 1..8");
+            c->ctas_per_sm = (int)v;
+            return SMK_OK;
         default: return fail(SMK_ERR_ARGUMENT, "unknown option %d", option);
     }
 }
@@ -278,6 +284,7 @@ smk_status smk_ctx_get(smk_ctx* c, int option, long long* v) {
         case SMK_OPT_PDL: *v = c->pdl; return SMK_OK;
         case SMK_OPT_WARPS: *v = c->warps; return SMK_OK;
         case SMK_OPT_STAGES: *v = c->stages; return SMK_OK;
+        case SMK_OPT_CTAS_PER_SM: *v = c->ctas_per_sm; return SMK_OK;
         default: return fail(SMK_ERR_ARGUMENT, "unknown option %d", option);
     }
 }
