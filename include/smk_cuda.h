@@ -70,8 +70,9 @@ smk_status smk_ctx_destroy(smk_ctx* ctx);
  *                   starts streaming its weights while the previous GEMV of
  *                   the stream finishes. Requires that no kernel immediately
  *                   before it in the stream writes its weights. Default 0.
- *   SMK_OPT_WARPS   warps per CTA of the quantized fast kernel (1..8, default 8).
- *   SMK_OPT_STAGES  shared-memory stages per warp (2..8, default 2).
+ *   SMK_OPT_WARPS   warps per CTA of the quantized fast kernel (1..16, default 8).
+ *   SMK_OPT_STAGES  shared-memory stages per warp of that kernel, each one
+ *                   tile of weights (1..8, default 2).
  *   SMK_OPT_CTAS_PER_SM  resident CTAs per SM of that kernel (1..8, default 1:
  *                   one persistent CTA per SM, leaving room for the next
  *                   GEMV's CTA under programmatic dependent launch). */
@@ -134,7 +135,7 @@ smk_status smk_block_sums(smk_ctx* ctx, smk_qformat fmt, int M, int N, int K, co
  *   - the quantized activations go to a fixed scratch array of
  *     SMK_NOALLOC_SCRATCH_BYTES inside the library, which every GPU that loads
  *     the library holds until the process exits; a call needing more
- *     (M * ceil(K/256) > 3276) is rejected with SMK_ERR_ARGUMENT;
+ *     (M * ceil(K/8192) > 102) is rejected with SMK_ERR_ARGUMENT;
  *   - the first call on each device looks up the array's device address and
  *     the SM count (set-up, once per device, with that device current); make
  *     that first call before any stream capture;

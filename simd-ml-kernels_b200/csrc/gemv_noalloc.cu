@@ -20,6 +20,7 @@
 #include "../../include/smk_cuda.h"
 #include "gemv_quant.cuh"
 
+#include <algorithm>
 #include <cstdio>
 #include <mutex>
 #include <string>
@@ -28,8 +29,9 @@
 
 namespace {
 
-// Maximum scratch: 1 MiB of quantized activations, i.e. M · ceil(K/256) up
-// to 3276 (K up to 838,656 for one row of x; K up to 104,704 for eight).
+// Maximum scratch: 1 MiB of quantized activations, 10 KiB per row of x and
+// per 8192 values of K: M · ceil(K/8192) up to 102 (K up to 835,584 for one
+// row of x; K up to 98,304 for eight).
 constexpr size_t kNoAllocScratchBytes = SMK_NOALLOC_SCRATCH_BYTES;
 
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
@@ -84,14 +86,18 @@ extern "C" smk_status smk_gemv_q_noalloc(smk_qformat fmt, int M, int N, int K, c
     if (M < 0 || N < 0 || K < 0) return noalloc_fail(SMK_ERR_ARGUMENT, "M, N and K must be >= 0");
     if (M > smk::kMaxRows) return noalloc_fail(SMK_ERR_ARGUMENT, "at most 8 rows of x per call");
     if (K % 32 != 0) return noalloc_fail(SMK_ERR_ARGUMENT, "K must be a multiple of 32");
-    const int nb = K / 32, nsbp = (nb + 7) / 8;
-    const size_t need = smk::xq_total_bytes(M, nsbp);
+    const bool fast = (K % 256 == 0) && ((reinterpret_cast<uintptr_t>(Wq) & 15) == 0);
+    smk::QGemvParams p = {};
+    p.x = x; p.ldx = ldx; p.w = Wq; p.y = y; p.ldy = ldy;
+    p.M = M; p.N = N; p.K = K;
+    smk::plan_tiles(p, fast);
+    const size_t need = smk::xq_total_bytes(M, p.ksteps);
     if (need > kNoAllocScratchBytes) {
         char buf[256];
         snprintf(buf, sizeof buf,
                  "smk_gemv_q_noalloc: M=%d rows of K=%d need %zu bytes of scratch, more than its fixed %zu "
-                 "(M * ceil(K/256) must be <= %zu); use smk_gemv_q",
-                 M, K, need, kNoAllocScratchBytes, kNoAllocScratchBytes / 320);
+                 "(M * ceil(K/8192) must be <= %zu); use smk_gemv_q",
+                 M, K, need, kNoAllocScratchBytes, kNoAllocScratchBytes / 10240);
         return noalloc_fail(SMK_ERR_ARGUMENT, buf);
     }
     if (M == 0 || N == 0) return SMK_OK;
@@ -121,23 +127,12 @@ extern "C" smk_status smk_gemv_q_noalloc(smk_qformat fmt, int M, int N, int K, c
     l.stream = strm;
     l.pdl = false;
     l.num_sms = s->num_sms;
-    l.warps = 4;
-    smk::QGemvParams p = {};
-    p.x = x; p.ldx = ldx; p.w = Wq; p.y = y; p.ldy = ldy;
-    p.M = M; p.N = N; p.K = K; p.nb = nb; p.nsbp = nsbp;
+    l.warps = 8;
     p.xq = s->scratch;
     p.dump = nullptr;
     p.err = s->error;
-    const bool fast = (K % 256 == 0) && ((reinterpret_cast<uintptr_t>(Wq) & 15) == 0);
-    if (fast) {
-        int G = 1, lg = 0;
-        while (G < nsbp && G < 32) { G <<= 1; ++lg; }
-        p.G = G; p.log2G = lg; p.TR = 32 / G;
-        p.ksteps = (nsbp + G - 1) / G;
-        p.ntiles = (N + p.TR - 1) / p.TR;
-        p.stages = 2;
-    }
-    e = smk::launch_quantize_x(l, x, ldx, M, K, s->scratch);
+    p.stages = 2;
+    e = smk::launch_quantize_x(l, p, s->scratch);
     if (e != cudaSuccess) return noalloc_fail(SMK_ERR_CUDA, std::string("quantize_x launch: ") + cudaGetErrorString(e));
     e = smk::launch_gemv_q(l, (int)fmt, p, fast, nullptr);
     if (e != cudaSuccess) return noalloc_fail(SMK_ERR_CUDA, std::string("gemv launch: ") + cudaGetErrorString(e));

@@ -4,11 +4,11 @@
 // Q8 blocks once per call with FP32 scales, q8_0_scalar.cpp:113-166).
 //
 // Fast kernel (K % 256 == 0, weights 16-byte aligned): a row of K/32 ggml
-// blocks is K/256 "superblocks" of 8 blocks = 144 bytes (Q4_0) or 272 (Q8_0),
+// blocks is K/256 superblocks of 8 blocks = 144 bytes (Q4_0) or 272 (Q8_0),
 // both multiples of 16, so every superblock of every row starts on a 16-byte
-// boundary. Each warp owns a private ring of shared-memory stages filled by
-// 1-D bulk TMA copies (cp.async.bulk, no multicast) and completed on an
-// mbarrier per stage; a stage is a tile of TR rows × G superblocks with one
+// boundary. Each warp owns a ring of shared-memory stages that it fills with
+// 1-D bulk TMA copies (cp.async.bulk, no multicast), completed on one
+// mbarrier per stage; a stage is a tile of TR rows × G superblocks, one
 // superblock per lane (TR·G = 32), read back with 128-bit shared loads (the
 // 144/272-byte lane stride puts each 8-lane phase on distinct banks). The
 // quants are unpacked in registers: Q4_0 nibbles as q & 0x0F0F0F0F and
@@ -39,20 +39,13 @@ namespace {
 
 constexpr int kThreadsQuantX = 256;
 
-__device__ __forceinline__ size_t xq_off(int nsbp, int m, int h, int j, int sb) {
-    return ((size_t)((m * 2 + h) * 8 + j) * nsbp + sb) * 16;
-}
-__device__ __forceinline__ size_t xd_off(int M, int nsbp, int m, int j, int sb) {
-    return xq_quant_bytes(M, nsbp) + ((size_t)(m * 8 + j) * nsbp + sb) * 8;
-}
+// ---- activation quantization --------------------------------------------------
 
-// Quantize x [M, K] into the swizzled layout at xb (shared or global memory).
-// Eight threads per 32-value block, four values each; tid in [0, nthreads),
-// nthreads a multiple of 8. Bit-exact with the reference's quantize_x_q8
-// (q8_0_scalar.cpp:45-61,113-118): amax/127 and 1/d as IEEE divisions,
-// w·id rounded once, then rounded half away from zero. Each thread first
-// loads the values of up to kXUnroll blocks, so the prologue of a GEMV waits
-// for one round trip to L2 rather than one per block.
+// Eight threads per 32-value block, four values each. Bit-exact with the
+// reference's quantize_x_q8 (q8_0_scalar.cpp:45-61,113-118): amax/127 and 1/d
+// as IEEE divisions, w·id rounded once, then rounded half away from zero.
+// Each thread first loads the values of up to kXUnroll blocks, so a GEMV's
+// prologue waits for one round trip to L2 rather than one per block.
 constexpr int kXUnroll = 4;
 
 __device__ __forceinline__ float4 load_x4(const float* p) {
@@ -60,8 +53,16 @@ __device__ __forceinline__ float4 load_x4(const float* p) {
     return make_float4(p[0], p[1], p[2], p[3]);
 }
 
-__device__ __forceinline__ void quantize_x_block(float4 v, int gq, unsigned gmask, int M, int nsbp, int m, int b,
+struct XGeom {
+    int M, nb, log2G, ksteps;
+};
+
+// All 32 lanes of the warp call this together (full-mask shuffles; the xor
+// offsets stay inside each 8-lane group); lanes with valid == false compute
+// on their (zero) values and store nothing.
+__device__ __forceinline__ void quantize_x_block(float4 v, int gq, bool valid, const XGeom& xg, int m, int b,
                                                  uint8_t* xb) {
+    constexpr unsigned gmask = 0xffffffffu;
     unsigned fin = finite_bits(v.x) & finite_bits(v.y) & finite_bits(v.z) & finite_bits(v.w);
     float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
 #pragma unroll
@@ -70,7 +71,8 @@ __device__ __forceinline__ void quantize_x_block(float4 v, int gq, unsigned gmas
         fin &= __shfl_xor_sync(gmask, fin, o);
     }
     const float d = __fdiv_rn(amax, 127.0f);
-    float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+    // IEEE reciprocal, round to nearest: the same value as 1.0f / d.
+    float id = d != 0.0f ? __frcp_rn(d) : 0.0f;
     if (!(id <= FLT_MAX)) id = 0.0f;
     const int q0 = fin ? (int)roundf(__fmul_rn(v.x, id)) : 0;
     const int q1 = fin ? (int)roundf(__fmul_rn(v.y, id)) : 0;
@@ -81,46 +83,58 @@ __device__ __forceinline__ void quantize_x_block(float4 v, int gq, unsigned gmas
     int s = q0 + q1 + q2 + q3;
 #pragma unroll
     for (int o = 4; o > 0; o >>= 1) s += __shfl_xor_sync(gmask, s, o);
-    const int sb = b >> 3, j = b & 7;
-    *reinterpret_cast<uint32_t*>(xb + xq_off(nsbp, m, gq >> 2, j, sb) + (gq & 3) * 4) = word;
+    // Offsets in 32 bits (the layout stays far below 4 GiB), no division.
+    const unsigned sb = (unsigned)b >> 3, j = (unsigned)b & 7u;
+    const unsigned ks = sb >> xg.log2G, g = sb & ((1u << xg.log2G) - 1u);
+    const unsigned mk = (unsigned)m * (unsigned)xg.ksteps + ks;
+    if (!valid) return;
+    *reinterpret_cast<uint32_t*>(xb + ((mk * 16u + 2u * j + (unsigned)(gq >> 2)) * 32u + g) * 16u + (gq & 3) * 4) = word;
     if (gq == 0) {
         const float dxv = fin ? d : __int_as_float(0x7fc00000);
-        *reinterpret_cast<float2*>(xb + xd_off(M, nsbp, m, j, sb)) = make_float2(dxv, __int_as_float(-8 * s));
+        *reinterpret_cast<float2*>(xb + (unsigned)xg.M * (unsigned)xg.ksteps * 8192u + ((mk * 8u + j) * 32u + g) * 8u) =
+            make_float2(dxv, __int_as_float(-8 * s));
     }
 }
 
-__device__ __forceinline__ void quantize_x_rows(const float* __restrict__ x, long long ldx, int M, int nb,
-                                                int nsbp, uint8_t* xb, int tid, int nthreads) {
-    const int gq = tid & 7;
-    const unsigned gmask = 0xffu << ((tid & 31) & ~7);
-    const int total = M * nb, stride = nthreads >> 3;
-    for (int base = tid >> 3; base < total; base += kXUnroll * stride) {
-        float4 v[kXUnroll];
+// Quantize x [M, K] into the lane-major layout at xb; tid in [0, nthreads),
+// nthreads a multiple of 32. Warp w takes blocks 4w .. 4w+3 (one per 8-lane
+// group), then the next 4·warps, so every lane of a warp runs every
+// iteration. MT: rows of x known at compile time (0: xg.M).
+template <int MT>
+__device__ __forceinline__ void quantize_x_rows(const float* __restrict__ x, long long ldx, const XGeom& xg,
+                                                uint8_t* xb, int tid, int nthreads) {
+    const int gq = tid & 7, grp = (tid & 31) >> 3;
+    const int wstride = (nthreads >> 5) * 4, nb = xg.nb;
+    const int rows = MT > 0 ? MT : xg.M;
 #pragma unroll
-        for (int u = 0; u < kXUnroll; ++u) {
-            const int blk = base + u * stride;
-            if (blk < total) {
-                const int m = blk / nb, b = blk - m * nb;
-                v[u] = load_x4(x + (size_t)m * ldx + (size_t)b * kQK + gq * 4);
+    for (int m = 0; m < (MT > 0 ? MT : kMaxRows); ++m) {
+        if (m >= rows) break;
+        const float* xr = x + (size_t)m * ldx + gq * 4;
+        for (int wbase = (tid >> 5) * 4; wbase < nb; wbase += kXUnroll * wstride) {
+            float4 v[kXUnroll];
+#pragma unroll
+            for (int u = 0; u < kXUnroll; ++u) {
+                const int b = wbase + u * wstride + grp;
+                v[u] = b < nb ? load_x4(xr + (size_t)b * kQK) : make_float4(0.f, 0.f, 0.f, 0.f);
             }
-        }
 #pragma unroll
-        for (int u = 0; u < kXUnroll; ++u) {
-            const int blk = base + u * stride;
-            if (blk < total) {
-                const int m = blk / nb, b = blk - m * nb;
-                quantize_x_block(v[u], gq, gmask, M, nsbp, m, b, xb);
+            for (int u = 0; u < kXUnroll; ++u) {
+                if (wbase + u * wstride >= nb) break;   // warp-uniform
+                const int b = wbase + u * wstride + grp;
+                quantize_x_block(v[u], gq, b < nb, xg, m, b, xb);
             }
         }
     }
 }
 
 __global__ void __launch_bounds__(kThreadsQuantX) quantize_x_kernel(const float* __restrict__ x, long long ldx,
-                                                                     int M, int nb, int nsbp, uint8_t* xq) {
+                                                                     XGeom xg, uint8_t* xq) {
     pdl_launch_dependents();
     pdl_wait_primary();   // x comes from the previous kernel; xq may still be read by it
-    quantize_x_rows(x, ldx, M, nb, nsbp, xq, blockIdx.x * blockDim.x + threadIdx.x, gridDim.x * blockDim.x);
+    quantize_x_rows<0>(x, ldx, xg, xq, blockIdx.x * blockDim.x + threadIdx.x, gridDim.x * blockDim.x);
 }
+
+// ---- integer block dots -----------------------------------------------------------
 
 template <bool kShared>
 __device__ __forceinline__ uint4 ld_x16(const uint8_t* p) {
@@ -133,15 +147,23 @@ __device__ __forceinline__ float2 ld_x8(const uint8_t* p) {
     else return __ldg(reinterpret_cast<const float2*>(p));
 }
 
-// One block: integer sums against every x row, then acc[m] += isum·(dw·dx).
+// The x data of one lane for one superblock: quants at xq + (2j + h)·512 and
+// (dx, bias) at xd + j·256, for each row m at + m·mstride_q / m·mstride_d.
+struct XPtr {
+    const uint8_t* xq;
+    const uint8_t* xd;
+    size_t mstride_q, mstride_d;
+};
+
+// One block j: integer sums against every x row, then acc[m] += isum·(dw·dx).
 template <int F, int M, bool kShX, bool kDump>
-__device__ __forceinline__ void block_dot(const uint32_t (&q)[8], float dw, const uint8_t* xb, int nsbp, int j,
-                                          int sb, float (&acc)[M], int32_t* dump, size_t dump_stride, size_t dump_idx) {
+__device__ __forceinline__ void block_dot(const uint32_t (&q)[8], float dw, const XPtr& xp, int j, float (&acc)[M],
+                                          int32_t* dump, size_t dump_stride, size_t dump_idx) {
 #pragma unroll
     for (int m = 0; m < M; ++m) {
-        const uint4 xl = ld_x16<kShX>(xb + xq_off(nsbp, m, 0, j, sb));
-        const uint4 xh = ld_x16<kShX>(xb + xq_off(nsbp, m, 1, j, sb));
-        const float2 db = ld_x8<kShX>(xb + xd_off(M, nsbp, m, j, sb));
+        const uint4 xl = ld_x16<kShX>(xp.xq + m * xp.mstride_q + (2 * j) * 512);
+        const uint4 xh = ld_x16<kShX>(xp.xq + m * xp.mstride_q + (2 * j + 1) * 512);
+        const float2 db = ld_x8<kShX>(xp.xd + m * xp.mstride_d + j * 256);
         int isum;
         if constexpr (F == kQ4_0) {
             // q[0..3]: the 16 nibble bytes; low nibbles are values 0-15, high 16-31.
@@ -170,10 +192,10 @@ __device__ __forceinline__ void block_dot(const uint32_t (&q)[8], float dw, cons
     }
 }
 
-// One superblock (8 blocks) at sp in shared memory.
+// One superblock (8 blocks) of weights at sp (shared memory, 16-byte aligned).
 template <int F, int M, bool kShX, bool kDump>
-__device__ __forceinline__ void superblock(const uint8_t* sp, const uint8_t* xb, int nsbp, int sb, float (&acc)[M],
-                                           int32_t* dump, size_t dump_stride, size_t dump_row) {
+__device__ __forceinline__ void superblock(const uint8_t* sp, const XPtr& xp, float (&acc)[M], int32_t* dump,
+                                           size_t dump_stride, size_t dump_base) {
     if constexpr (F == kQ4_0) {
         uint32_t w[36];
 #pragma unroll
@@ -195,8 +217,7 @@ __device__ __forceinline__ void superblock(const uint8_t* sp, const uint8_t* xb,
 #pragma unroll
                 for (int i = 0; i < 4; ++i) q[i] = w[b + 1 + i];
             }
-            block_dot<F, M, kShX, kDump>(q, half_bits_to_float(sc), xb, nsbp, j, sb, acc, dump, dump_stride,
-                                         dump_row + sb * 8 + j);
+            block_dot<F, M, kShX, kDump>(q, half_bits_to_float(sc), xp, j, acc, dump, dump_stride, dump_base + j);
         }
     } else {
 #pragma unroll
@@ -222,40 +243,48 @@ __device__ __forceinline__ void superblock(const uint8_t* sp, const uint8_t* xb,
 #pragma unroll
                     for (int i = 0; i < 8; ++i) q[i] = w[b + 1 + i];
                 }
-                block_dot<F, M, kShX, kDump>(q, half_bits_to_float(sc), xb, nsbp, j, sb, acc, dump, dump_stride,
-                                             dump_row + sb * 8 + j);
+                block_dot<F, M, kShX, kDump>(q, half_bits_to_float(sc), xp, j, acc, dump, dump_stride, dump_base + j);
             }
         }
     }
 }
 
-// Issue the bulk copies of work item `it` (tile, k-step) into its stage.
+// ---- the fast kernel -----------------------------------------------------------------
+
+// Issue the bulk copies of one work item (tile, k-step ks) of this warp into stage `slot`.
 template <int F>
-__device__ __forceinline__ void issue_item(const QGemvParams& p, int it, int gw, int GW, uint8_t* stages,
+__device__ __forceinline__ void issue_item(const QGemvParams& p, int tile, int ks, int slot, uint8_t* stages,
                                            uint64_t* bars, int lane) {
     constexpr int SBB = sb_bytes(F);
-    const int tile = gw + (it / p.ksteps) * GW, ks = it - (it / p.ksteps) * p.ksteps;
-    const int slot = it % p.stages;
     const int rows = min(p.TR, p.N - tile * p.TR);
     const int sb0 = ks * p.G;
     const int cnt = min(p.G, p.nsbp - sb0);
     const uint32_t bytes = (uint32_t)cnt * SBB;
+    const size_t row_bytes = (size_t)p.nsbp * SBB;
+    uint8_t* dst = stages + (size_t)slot * (32 * SBB);
     if (lane == 0) mbar_arrive_expect_tx(&bars[slot], bytes * rows);
     __syncwarp();
     if (p.ksteps == 1 && p.G == p.nsbp) {
         // Whole rows, back to back in memory and in the stage: one copy.
-        if (lane == 0)
-            tma_load_1d(stages + (size_t)slot * 32 * SBB, p.w + (size_t)tile * p.TR * ((size_t)p.nsbp * SBB),
-                        bytes * rows, &bars[slot]);
+        if (lane == 0) tma_load_1d(dst, p.w + (size_t)tile * p.TR * row_bytes, bytes * rows, &bars[slot]);
     } else if (lane < rows) {
-        const size_t row = (size_t)tile * p.TR + lane;
-        const uint8_t* src = p.w + row * ((size_t)p.nsbp * SBB) + (size_t)sb0 * SBB;
-        tma_load_1d(stages + (size_t)slot * 32 * SBB + (size_t)lane * p.G * SBB, src, bytes, &bars[slot]);
+        const uint8_t* src = p.w + ((size_t)tile * p.TR + lane) * row_bytes + (size_t)sb0 * SBB;
+        tma_load_1d(dst + (size_t)lane * p.G * SBB, src, bytes, &bars[slot]);
     }
 }
 
+// Position of a warp in its sequence of work items, advanced without division.
+struct ItemCursor {
+    int tile, ks, slot;
+    uint32_t phase;
+    __device__ __forceinline__ void next(const QGemvParams& p, int GW) {
+        if (++ks == p.ksteps) { ks = 0; tile += GW; }
+        if (++slot == p.stages) { slot = 0; phase ^= 1u; }
+    }
+};
+
 template <int F, int M, bool kXGlobal, bool kDump>
-__global__ void __launch_bounds__(256) gemv_q_fast(const QGemvParams p) {
+__global__ void __launch_bounds__(512) gemv_q_fast(const QGemvParams p) {
     constexpr int SBB = sb_bytes(F);
     extern __shared__ __align__(128) uint8_t smem[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
@@ -263,7 +292,7 @@ __global__ void __launch_bounds__(256) gemv_q_fast(const QGemvParams p) {
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem) + warp * p.stages;
     size_t off = ((size_t)nwarps * p.stages * 8 + 127) & ~(size_t)127;
     uint8_t* xs = smem + off;
-    if constexpr (!kXGlobal) off += (xq_total_bytes(M, p.nsbp) + 127) & ~(size_t)127;
+    if constexpr (!kXGlobal) off += (xq_total_bytes(M, p.ksteps) + 127) & ~(size_t)127;
     uint8_t* stages = smem + off + (size_t)warp * p.stages * 32 * SBB;
 
     pdl_launch_dependents();
@@ -280,36 +309,54 @@ __global__ void __launch_bounds__(256) gemv_q_fast(const QGemvParams p) {
         fence_mbar_init();
     }
     __syncwarp();
-    const int pre = min(p.stages, nitems);
-    for (int it = 0; it < pre; ++it) issue_item<F>(p, it, gw, GW, stages, bars, lane);
+    // Cursors: `cur` consumes, `iss` issues (p.stages items ahead).
+    ItemCursor cur{gw, 0, 0, 0u}, iss{gw, 0, 0, 0u};
+    int issued = 0;
+    for (; issued < min(p.stages, nitems); ++issued) {
+        issue_item<F>(p, iss.tile, iss.ks, iss.slot, stages, bars, lane);
+        iss.next(p, GW);
+    }
 
     pdl_wait_primary();
     if constexpr (!kXGlobal) {
-        quantize_x_rows(p.x, p.ldx, M, p.nb, p.nsbp, xs, threadIdx.x, blockDim.x);
+        const XGeom xg{M, p.nb, p.log2G, p.ksteps};
+        quantize_x_rows<M>(p.x, p.ldx, xg, xs, threadIdx.x, blockDim.x);
         __syncthreads();
     }
     const uint8_t* xb = kXGlobal ? p.xq : xs;
 
     const int r = lane >> p.log2G, g = lane & (p.G - 1);
+    XPtr xp;
+    xp.mstride_q = (size_t)p.ksteps * 8192;
+    xp.mstride_d = (size_t)p.ksteps * 2048;
+    const uint8_t* xd0 = xb + (size_t)M * p.ksteps * 8192;
     float acc[M];
 #pragma unroll
     for (int m = 0; m < M; ++m) acc[m] = 0.0f;
 
     for (int it = 0; it < nitems; ++it) {
-        const int slot = it % p.stages;
-        if (!mbar_wait_bounded(&bars[slot], (uint32_t)((it / p.stages) & 1), p.err)) {
+        if (!mbar_wait_bounded(&bars[cur.slot], cur.phase, p.err)) {
             // Give the copies still in flight a bounded chance to land before
             // the CTA's shared memory is released, then stop.
-            for (int k = it + 1; k < min(nitems, it + p.stages); ++k)
-                mbar_wait_bounded(&bars[k % p.stages], (uint32_t)((k / p.stages) & 1), nullptr);
+            ItemCursor c2 = cur;
+            for (int k = it + 1; k < issued; ++k) {
+                c2.next(p, GW);
+                mbar_wait_bounded(&bars[c2.slot], c2.phase, nullptr);
+            }
             return;
         }
-        const int tile = gw + (it / p.ksteps) * GW, ks = it - (it / p.ksteps) * p.ksteps;
-        const int row = tile * p.TR + r, sb = ks * p.G + g;
-        if (row < p.N && sb < p.nsbp)
-            superblock<F, M, !kXGlobal, kDump>(stages + (size_t)slot * 32 * SBB + (size_t)lane * SBB, xb, p.nsbp, sb,
-                                               acc, p.dump, (size_t)p.N * p.nb, (size_t)row * p.nb);
-        if (ks == p.ksteps - 1) {
+        const int row = cur.tile * p.TR + r, sb = cur.ks * p.G + g;
+        xp.xq = xb + ((size_t)cur.ks * 16 * 32 + g) * 16;
+        xp.xd = xd0 + ((size_t)cur.ks * 8 * 32 + g) * 8;
+        const uint8_t* sp = stages + (size_t)cur.slot * (32 * SBB) + (size_t)lane * SBB;
+        const size_t dstride = (size_t)p.N * p.nb, dbase = (size_t)row * p.nb + (size_t)sb * 8;
+        // A full tile (every lane has a row and a superblock: warp-uniform)
+        // runs without a per-lane guard.
+        if ((cur.tile + 1) * p.TR <= p.N && (cur.ks + 1) * p.G <= p.nsbp)
+            superblock<F, M, !kXGlobal, kDump>(sp, xp, acc, p.dump, dstride, dbase);
+        else if (row < p.N && sb < p.nsbp)
+            superblock<F, M, !kXGlobal, kDump>(sp, xp, acc, p.dump, dstride, dbase);
+        if (cur.ks == p.ksteps - 1) {
 #pragma unroll
             for (int m = 0; m < M; ++m) {
                 float v = acc[m];
@@ -319,15 +366,20 @@ __global__ void __launch_bounds__(256) gemv_q_fast(const QGemvParams p) {
             }
         }
         __syncwarp();
-        if (it + p.stages < nitems) {
+        if (issued < nitems) {
             fence_proxy_async_smem();
-            issue_item<F>(p, it + p.stages, gw, GW, stages, bars, lane);
+            issue_item<F>(p, iss.tile, iss.ks, iss.slot, stages, bars, lane);
+            iss.next(p, GW);
+            ++issued;
         }
+        cur.next(p, GW);
     }
 }
 
-// Generic kernel: any K % 32 == 0 and any weight alignment. One warp per row,
-// lanes over blocks, byte loads; x already quantized in global memory.
+// ---- the generic kernel --------------------------------------------------------------
+
+// Any K % 32 == 0 and any weight alignment. One warp per row, lanes over
+// blocks, byte loads; x already quantized in global memory (layout G = 32).
 template <int F, int M, bool kDump>
 __global__ void __launch_bounds__(256) gemv_q_generic(const QGemvParams p) {
     constexpr int BB = block_bytes(F);
@@ -336,6 +388,10 @@ __global__ void __launch_bounds__(256) gemv_q_generic(const QGemvParams p) {
     const int lane = threadIdx.x & 31;
     const int nwarps_total = gridDim.x * (blockDim.x >> 5);
     const size_t row_bytes = (size_t)p.nb * BB;
+    XPtr xp;
+    xp.mstride_q = (size_t)p.ksteps * 8192;
+    xp.mstride_d = (size_t)p.ksteps * 2048;
+    const uint8_t* xd0 = p.xq + (size_t)M * p.ksteps * 8192;
     for (int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); row < p.N; row += nwarps_total) {
         float acc[M];
 #pragma unroll
@@ -348,8 +404,11 @@ __global__ void __launch_bounds__(256) gemv_q_generic(const QGemvParams p) {
             for (int i = 0; i < (F == kQ4_0 ? 4 : 8); ++i)
                 q[i] = (uint32_t)__ldg(blk + 2 + 4 * i) | ((uint32_t)__ldg(blk + 3 + 4 * i) << 8) |
                        ((uint32_t)__ldg(blk + 4 + 4 * i) << 16) | ((uint32_t)__ldg(blk + 5 + 4 * i) << 24);
-            block_dot<F, M, false, kDump>(q, half_bits_to_float(sc), p.xq, p.nsbp, b & 7, b >> 3, acc, p.dump,
-                                          (size_t)p.N * p.nb, (size_t)row * p.nb + b);
+            const int sb = b >> 3, ks = sb >> 5, g = sb & 31;
+            xp.xq = p.xq + ((size_t)ks * 16 * 32 + g) * 16;
+            xp.xd = xd0 + ((size_t)ks * 8 * 32 + g) * 8;
+            block_dot<F, M, false, kDump>(q, half_bits_to_float(sc), xp, b & 7, acc, p.dump, (size_t)p.N * p.nb,
+                                          (size_t)row * p.nb + b);
         }
 #pragma unroll
         for (int m = 0; m < M; ++m) {
@@ -477,8 +536,8 @@ cudaError_t occupancy_cached(const void* fn, int threads, size_t smem, int* per_
     return cudaSuccess;
 }
 
-template <typename K>
-cudaError_t launch(K kernel, dim3 grid, dim3 block, size_t smem, const LaunchCfg& c, const QGemvParams& p) {
+template <typename Kern, typename... Args>
+cudaError_t launch(Kern kernel, dim3 grid, dim3 block, size_t smem, const LaunchCfg& c, Args... args) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = block;
@@ -489,7 +548,7 @@ cudaError_t launch(K kernel, dim3 grid, dim3 block, size_t smem, const LaunchCfg
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = c.pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, kernel, p);
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
 }
 
 template <int F, int M>
@@ -538,33 +597,42 @@ cudaError_t occupancy(const void* fn, int threads, size_t smem, int* per_sm) {
     return occupancy_cached(fn, threads, smem, per_sm);
 }
 
-size_t gemv_q_smem(int fmt, int M, int nsbp, int warps, int stages, bool x_in_smem) {
+void plan_tiles(QGemvParams& p, bool fast) {
+    p.nb = p.K / kQK;
+    p.nsbp = (p.nb + 7) / 8;
+    int G = 1, lg = 0;
+    if (fast) {
+        while (G < p.nsbp && G < 32) { G <<= 1; ++lg; }
+    } else {
+        G = 32;
+        lg = 5;
+    }
+    p.G = G;
+    p.log2G = lg;
+    p.TR = 32 / G;
+    p.ksteps = std::max(1, (p.nsbp + G - 1) / G);
+    p.ntiles = (p.N + p.TR - 1) / p.TR;
+}
+
+size_t gemv_q_smem(int fmt, int M, int ksteps, int warps, int stages, bool x_in_smem) {
     size_t off = ((size_t)warps * stages * 8 + 127) & ~(size_t)127;
-    if (x_in_smem) off += (xq_total_bytes(M, nsbp) + 127) & ~(size_t)127;
+    if (x_in_smem) off += (xq_total_bytes(M, ksteps) + 127) & ~(size_t)127;
     return off + (size_t)warps * stages * 32 * sb_bytes(fmt);
 }
 
-cudaError_t launch_quantize_x(const LaunchCfg& c, const float* x, long long ldx, int M, int K, uint8_t* xq) {
-    const int nb = K / kQK, nsbp = (nb + 7) / 8;
-    const long long groups = (long long)M * nb;
+cudaError_t launch_quantize_x(const LaunchCfg& c, const QGemvParams& p, uint8_t* xq) {
+    const long long groups = (long long)p.M * p.nb;
     const long long grid = std::min<long long>((groups + kThreadsQuantX / 8 - 1) / (kThreadsQuantX / 8),
                                                (long long)c.num_sms * 4);
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)std::max<long long>(grid, 1));
-    cfg.blockDim = dim3(kThreadsQuantX);
-    cfg.stream = c.stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = c.pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, quantize_x_kernel, x, ldx, M, nb, nsbp, xq);
+    const XGeom xg{p.M, p.nb, p.log2G, p.ksteps};
+    return launch(quantize_x_kernel, dim3((unsigned)std::max<long long>(grid, 1)), dim3(kThreadsQuantX), 0, c, p.x,
+                  p.ldx, xg, xq);
 }
 
 cudaError_t launch_gemv_q(const LaunchCfg& c, int fmt, QGemvParams p, bool fast, size_t* smem_used) {
     const bool dump = p.dump != nullptr;
     size_t smem = 0;
-    if (fast) smem = gemv_q_smem(fmt, p.M, p.nsbp, c.warps, p.stages, p.xq == nullptr);
+    if (fast) smem = gemv_q_smem(fmt, p.M, p.ksteps, c.warps, p.stages, p.xq == nullptr);
     if (smem_used) *smem_used = smem;
     return fmt == kQ4_0 ? dispatch_m<kQ4_0>(c, p, fast, smem, dump) : dispatch_m<kQ8_0>(c, p, fast, smem, dump);
 }

@@ -1,5 +1,5 @@
 // gemv_quant.cuh — launch parameters of the Q4_0 / Q8_0 decode-GEMV kernels
-// (gemv_quant.cu) shared with the C-ABI layer (smk_api.cu).
+// (gemv_quant.cu) shared with the C-ABI layer (smk_api.cu, gemv_noalloc.cu).
 #pragma once
 
 #include <cstddef>
@@ -17,18 +17,27 @@ constexpr int kMaxRows = 8;       // rows of x per call (M)
 __host__ __device__ constexpr int block_bytes(int fmt) { return fmt == kQ4_0 ? 18 : 34; }
 __host__ __device__ constexpr int sb_bytes(int fmt) { return 8 * block_bytes(fmt); }   // 144 / 272
 
-// Quantized activations in device memory (shared memory or a global buffer),
-// laid out so that lanes reading consecutive superblocks hit distinct banks:
-//   quants of x row m, block b = 8·sb + j, half h (values 16h .. 16h+15):
-//       16 bytes at ((m·2 + h)·8 + j)·nsbp·16 + sb·16
-//   (dx, bias) of the block as float2 (bias = −8·Σ quants as int bits):
-//       at xq_bytes + ((m·8 + j)·nsbp + sb)·8
-// nsbp = ceil(nb / 8) superblocks per row (blocks past nb are never read).
-// A block whose values are not all finite stores dx = NaN, which makes every
-// output of that x row NaN, the reference's rule (q8_0_scalar.cpp:142-164).
-__host__ __device__ inline size_t xq_quant_bytes(int M, int nsbp) { return (size_t)M * nsbp * 256; }
-__host__ __device__ inline size_t xq_total_bytes(int M, int nsbp) {
-    return xq_quant_bytes(M, nsbp) + (size_t)M * nsbp * 8 * 8;
+// Work decomposition. A row of K/32 ggml blocks is nsbp = ceil(K/256)
+// "superblocks" of 8 blocks. A warp tile is TR rows × G superblocks,
+// TR·G = 32 (one superblock per lane: lane = r·G + g); ksteps tiles cover a
+// row (superblock sb = ks·G + g).
+//
+// Quantized activations (shared memory or a global buffer), "lane-major":
+//   quants of x row m, k-step ks, block j of the superblock, half h (values
+//   16h .. 16h+15), lane g: 16 bytes at (((m·ksteps + ks)·16 + 2j + h)·32 + g)·16
+//   (dx, bias) of that block as float2 (bias = −8·Σ quants, as int bits) at
+//   xd_base + (((m·ksteps + ks)·8 + j)·32 + g)·8,  xd_base = M·ksteps·8192.
+// Lanes of a warp read consecutive 16-byte (8-byte) chunks, one bank set per
+// 8 (16) lanes, and within a superblock every offset from the lane's base is
+// a compile-time constant. A block whose values are not all finite stores
+// dx = NaN, which makes every output of that x row NaN, the reference's rule
+// (q8_0_scalar.cpp:142-164).
+__host__ __device__ inline size_t xq_total_bytes(int M, int ksteps) { return (size_t)M * ksteps * 10240; }
+__host__ __device__ inline size_t xq_off(int ksteps, int m, int ks, int j, int h, int g) {
+    return (((((size_t)m * ksteps + ks) * 16 + 2 * j + h) * 32) + g) * 16;
+}
+__host__ __device__ inline size_t xd_off(int M, int ksteps, int m, int ks, int j, int g) {
+    return (size_t)M * ksteps * 8192 + (((((size_t)m * ksteps + ks) * 8 + j) * 32) + g) * 8;
 }
 
 struct QGemvParams {
@@ -40,13 +49,16 @@ struct QGemvParams {
     int M, N, K;
     int nb;                // K / 32
     int nsbp;              // ceil(nb / 8)
-    // Fast kernel tiling: a warp tile is TR rows × G superblocks (TR·G = 32,
-    // one superblock per lane); ksteps tiles cover a row.
-    int G, log2G, TR, ksteps, ntiles, stages;
+    int G, log2G, TR, ksteps, ntiles;
+    int stages;            // shared-memory stages per warp (fast kernel)
     const uint8_t* xq;     // quantized x in global memory (nullptr: each CTA quantizes into shared memory)
     int32_t* dump;         // test-only: per-block integer sums [M, N, nb], or nullptr
     unsigned* err;         // device error word
 };
+
+// Fill the tiling of p (p.M, p.N, p.K set): the fast kernel's G = the
+// smallest power of two >= nsbp, at most 32; the generic kernel's G = 32.
+void plan_tiles(QGemvParams& p, bool fast);
 
 // Sets the message smk_last_error() returns on this thread.
 void set_last_error(const char* msg);
@@ -64,13 +76,13 @@ struct LaunchCfg {
     int ctas_per_sm = 1;   // cap on resident CTAs per SM of the fast kernel
 };
 
-// Quantize x into the layout above in global memory (xq_total_bytes).
-cudaError_t launch_quantize_x(const LaunchCfg& c, const float* x, long long ldx, int M, int K, uint8_t* xq);
+// Quantize p.x into the layout above at xq (global memory, xq_total_bytes(M, ksteps)).
+cudaError_t launch_quantize_x(const LaunchCfg& c, const QGemvParams& p, uint8_t* xq);
 // y = x · Wᵀ. fast: K % 256 == 0 and w 16-byte aligned (ggml superblocks
 // stream as whole 16-byte units); otherwise the generic kernel.
 cudaError_t launch_gemv_q(const LaunchCfg& c, int fmt, QGemvParams p, bool fast, size_t* smem_used);
 // Size of the fast kernel's dynamic shared memory for this launch.
-size_t gemv_q_smem(int fmt, int M, int nsbp, int warps, int stages, bool x_in_smem);
+size_t gemv_q_smem(int fmt, int M, int ksteps, int warps, int stages, bool x_in_smem);
 
 // Weight quantizers (ggml quantize_row_q4_0_ref / q8_0_ref, bit-exact).
 // *reject gets 1 when a value is NaN/Inf or a scale overflows binary16.

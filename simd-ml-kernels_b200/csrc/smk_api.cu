@@ -107,8 +107,8 @@ struct smk_ctx {
     int num_sms = 148;
     size_t smem_optin = 227 * 1024;
     bool pdl = false;
-    int warps = 8;
-    int stages = 2;
+    int warps = 8;         // warps per CTA of the fast kernel
+    int stages = 2;        // shared-memory stages per warp
     int ctas_per_sm = 1;
     unsigned* d_err = nullptr;      // device error word
     unsigned* d_reject = nullptr;   // quantizer rejection flag
@@ -153,29 +153,26 @@ QPlan plan_q(smk_ctx* c, smk_qformat fmt, int M, int N, int K, const float* x, i
     smk::QGemvParams& p = q.p;
     p.x = x; p.ldx = ldx; p.w = Wq; p.y = y; p.ldy = ldy;
     p.M = M; p.N = N; p.K = K;
-    p.nb = K / 32;
-    p.nsbp = (p.nb + 7) / 8;
     p.err = c->d_err;
-    q.x_bytes = smk::xq_total_bytes(M, p.nsbp);
     q.fast = (K % 256 == 0) && ((reinterpret_cast<uintptr_t>(Wq) & 15) == 0);
+    smk::plan_tiles(p, q.fast);
+    q.x_bytes = smk::xq_total_bytes(M, p.ksteps);
     if (q.fast) {
-        const int nsb = p.nsbp;
-        int G = 1, lg = 0;
-        while (G < nsb && G < 32) { G <<= 1; ++lg; }
-        p.G = G; p.log2G = lg; p.TR = 32 / G;
-        p.ksteps = (nsb + G - 1) / G;
-        p.ntiles = (N + p.TR - 1) / p.TR;
         p.stages = c->stages;
         // Quantized x in shared memory while it is small; otherwise one
         // quantize kernel writes it to scratch and every CTA reads it there.
         const size_t budget = 64 * 1024;
         q.x_in_smem = q.x_bytes <= budget || want_dump;
-        size_t smem = smk::gemv_q_smem(fmt, M, nsb, c->warps, p.stages, q.x_in_smem);
-        while (smem > c->smem_optin && p.stages > 2) {
+        size_t smem = smk::gemv_q_smem(fmt, M, p.ksteps, c->warps, p.stages, q.x_in_smem);
+        while (smem > c->smem_optin && p.stages > 1) {
             --p.stages;
-            smem = smk::gemv_q_smem(fmt, M, nsb, c->warps, p.stages, q.x_in_smem);
+            smem = smk::gemv_q_smem(fmt, M, p.ksteps, c->warps, p.stages, q.x_in_smem);
         }
-        if (smem > c->smem_optin) q.fast = false;   // e.g. a dump of a huge M·K: the generic kernel
+        if (smem > c->smem_optin) {   // e.g. a dump of a huge M·K: the generic kernel
+            q.fast = false;
+            smk::plan_tiles(p, false);
+            q.x_bytes = smk::xq_total_bytes(M, p.ksteps);
+        }
     }
     if (!q.fast) q.x_in_smem = false;
     return q;
@@ -199,7 +196,7 @@ smk_status run_q(smk_ctx* c, smk_qformat fmt, int M, int N, int K, const float* 
             SMK_CUDA(b.reserve(q.x_bytes), "cudaMalloc (scratch)");
             xq = static_cast<uint8_t*>(b.ptr);
         }
-        SMK_CUDA(smk::launch_quantize_x(l, x, ldx, M, K, xq), "quantize_x launch");
+        SMK_CUDA(smk::launch_quantize_x(l, q.p, xq), "quantize_x launch");
         q.p.xq = xq;
     }
     SMK_CUDA(smk::launch_gemv_q(l, fmt, q.p, q.fast, nullptr), "gemv launch");
@@ -263,11 +260,11 @@ smk_status smk_ctx_set(smk_ctx* c, int option, long long v) {
     switch (option) {
         case SMK_OPT_PDL: c->pdl = v != 0; return SMK_OK;
         case SMK_OPT_WARPS:
-            if (v < 1 || v > 8) return fail(SMK_ERR_ARGUMENT, "warps must be in 1..8");
+            if (v < 1 || v > 16) return fail(SMK_ERR_ARGUMENT, "warps must be in 1..16");
             c->warps = (int)v;
             return SMK_OK;
         case SMK_OPT_STAGES:
-            if (v < 2 || v > 8) return fail(SMK_ERR_ARGUMENT, "stages must be in 2..8");
+            if (v < 1 || v > 8) return fail(SMK_ERR_ARGUMENT, "stages must be in 1..8");
             c->stages = (int)v;
             return SMK_OK;
         case SMK_OPT_CTAS_PER_SM:
@@ -466,17 +463,17 @@ smk_status smk_quantize_host(smk_ctx* c, smk_qformat fmt, int64_t rows, int K, c
 
 namespace {
 
-// Un-swizzle the quantized-x layout into plain int8 [M, K] and fp32 [M, K/32].
-__global__ void unswizzle_x(const uint8_t* xq, int M, int nb, int nsbp, int8_t* qs, float* dx) {
-    const int K = nb * 32;
-    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < (long long)M * K;
+// Un-swizzle the quantized-x layout (gemv_quant.cuh) into plain int8 [M, K]
+// and fp32 [M, K/32].
+__global__ void unswizzle_x(const uint8_t* xq, smk::QGemvParams p, int8_t* qs, float* dx) {
+    const int K = p.nb * 32;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < (long long)p.M * K;
          i += (long long)gridDim.x * blockDim.x) {
         const int m = (int)(i / K), k = (int)(i % K), b = k / 32, v = k % 32;
-        const int sb = b >> 3, j = b & 7, h = v >> 4;
-        qs[i] = (int8_t)xq[((size_t)((m * 2 + h) * 8 + j) * nsbp + sb) * 16 + (v & 15)];
+        const int sb = b >> 3, j = b & 7, h = v >> 4, ks = sb >> p.log2G, g = sb & (p.G - 1);
+        qs[i] = (int8_t)xq[smk::xq_off(p.ksteps, m, ks, j, h, g) + (v & 15)];
         if (v == 0)
-            dx[(size_t)m * nb + b] =
-                reinterpret_cast<const float2*>(xq + smk::xq_quant_bytes(M, nsbp))[(size_t)(m * 8 + j) * nsbp + sb].x;
+            dx[(size_t)m * p.nb + b] = reinterpret_cast<const float2*>(xq + smk::xd_off(p.M, p.ksteps, m, ks, j, g))->x;
     }
 }
 
@@ -491,15 +488,17 @@ smk_status smk_quantize_x(smk_ctx* c, int M, int K, const float* x, int64_t ldx,
     if (M == 0 || K == 0) return SMK_OK;
     DeviceGuard g(c->device);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    const int nb = K / 32, nsbp = (nb + 7) / 8;
+    smk::QGemvParams p = {};
+    p.x = x; p.ldx = ldx; p.M = M; p.N = 1; p.K = K;
+    smk::plan_tiles(p, false);
     uint8_t* xq;
     {
         std::lock_guard<std::mutex> lock(c->mu_scratch);
-        SMK_CUDA(c->test_buf.reserve(smk::xq_total_bytes(M, nsbp)), "cudaMalloc (test)");
+        SMK_CUDA(c->test_buf.reserve(smk::xq_total_bytes(M, p.ksteps)), "cudaMalloc (test)");
         xq = static_cast<uint8_t*>(c->test_buf.ptr);
     }
-    SMK_CUDA(smk::launch_quantize_x(cfg_for(c, s), x, ldx, M, K, xq), "quantize_x launch");
-    unswizzle_x<<<std::min<long long>(((long long)M * K + 255) / 256, 4096), 256, 0, s>>>(xq, M, nb, nsbp, qs, dx);
+    SMK_CUDA(smk::launch_quantize_x(cfg_for(c, s), p, xq), "quantize_x launch");
+    unswizzle_x<<<std::min<long long>(((long long)M * K + 255) / 256, 4096), 256, 0, s>>>(xq, p, qs, dx);
     SMK_CUDA(cudaGetLastError(), "unswizzle launch");
     return SMK_OK;
 }

@@ -268,6 +268,77 @@ def test_gemv_deterministic_pdl_and_streams(sk, torch, fmt):
         np.testing.assert_array_equal(o.cpu().numpy().view(np.uint32), ref.view(np.uint32))
 
 
+@pytest.mark.parametrize("fmt", ["q4_0", "q8_0"])
+def test_launch_settings_bitwise_equal(sk, torch, fmt):
+    """Outputs do not depend on the launch shape of the fast kernel (warps per
+    CTA, shared-memory stages per warp, CTAs per SM, programmatic dependent
+    launch): bitwise identical."""
+    from simd_ml_kernels import _core
+    cases = [(28672, 8192), (8192, 2048), (1000, 28672), (300, 256)]
+    ref = {}
+    for N, K in cases:
+        x, Wq = make_case(N + K, N, K, fmt)
+        ref[(N, K)] = (torch.from_numpy(x).cuda(), torch.from_numpy(Wq.ravel()).cuda(), x, Wq)
+    base = {key: (sk.gemv_q4_0 if fmt == "q4_0" else sk.gemv_q8_0)(v[0], v[1], *key).cpu().numpy()
+            for key, v in ref.items()}
+    for key, y in base.items():
+        y64, mag = O.ref64(fmt, ref[key][2], ref[key][3], *key)
+        assert_gemv_close(y, y64, mag, key[1], f"{fmt} {key}")
+    settings = [(16, 2, 1, False), (8, 3, 1, True), (2, 8, 1, False), (4, 2, 2, True), (12, 1, 3, False)]
+    try:
+        for warps, stages, ctas, pdl in settings:
+            _core._ctx_set(2, warps)
+            _core._ctx_set(3, stages)
+            _core._ctx_set(4, ctas)
+            sk.set_pdl(pdl)
+            for key, v in ref.items():
+                fn = sk.gemv_q4_0 if fmt == "q4_0" else sk.gemv_q8_0
+                for _ in range(2):
+                    got = fn(v[0], v[1], *key).cpu().numpy()
+                    np.testing.assert_array_equal(got.view(np.uint32), base[key].view(np.uint32),
+                                                  err_msg=f"{fmt} {key} warps={warps} stages={stages} ctas={ctas}")
+    finally:
+        _core._ctx_set(2, 8)
+        _core._ctx_set(3, 2)
+        _core._ctx_set(4, 1)
+        sk.set_pdl(False)
+
+
+@pytest.mark.parametrize("fmt", ["q4_0", "q8_0"])
+def test_dependent_chain_under_pdl(sk, torch, fmt):
+    """A chain of GEMVs where each output is the next input, queued back to
+    back on one stream with programmatic dependent launch: every GEMV must
+    see its predecessor's finished output. Equal, bit for bit, to the chain
+    run with a host synchronisation between the calls."""
+    K, links = 2048, 12
+    rng = np.random.default_rng(21)
+    quant = sk.quantize_q4_0 if fmt == "q4_0" else sk.quantize_q8_0
+    fn = sk.gemv_q4_0 if fmt == "q4_0" else sk.gemv_q8_0
+    Ws = [quant(torch.from_numpy((rng.standard_normal((K, K)) * 0.03).astype(np.float32)).cuda()).reshape(-1)
+          for _ in range(3)]
+    x0 = torch.from_numpy(rng.standard_normal(K).astype(np.float32)).cuda()
+    ys = [torch.empty(K, device="cuda") for _ in range(links)]
+    want = []
+    x = x0
+    for i in range(links):
+        x = fn(x, Ws[i % 3], K, K)
+        torch.cuda.synchronize()
+        want.append(x.cpu().numpy())
+    sk.set_pdl(True)
+    try:
+        for trial in range(3):
+            x = x0
+            for i in range(links):
+                fn(x, Ws[i % 3], K, K, out=ys[i])
+                x = ys[i]
+            torch.cuda.synchronize()
+            for i in range(links):
+                np.testing.assert_array_equal(ys[i].cpu().numpy().view(np.uint32), want[i].view(np.uint32),
+                                              err_msg=f"{fmt} link {i} trial {trial}")
+    finally:
+        sk.set_pdl(False)
+
+
 def test_row_shards_bitwise_equal_full(sk, torch):
     """Row-sharding (the multi-GPU plan, 8-row groups as the reference's
     gemv_slice): every shard's outputs bitwise equal the unsharded call."""

@@ -75,7 +75,7 @@ def test_noalloc_rejects_beyond_its_scratch(cuda_device):
     import torch
 
     lib, noalloc = _lib()
-    M, N, K = 8, 4, 131072          # 8 * 512 superblocks * 320 B = 1.25 MiB > 1 MiB
+    M, N, K = 8, 4, 131072          # 8 rows * 16 k-steps * 10 KiB = 1.25 MiB > 1 MiB
     st = noalloc(0, M, N, K, None, K, None, None, N, None)
     assert st == 1                  # SMK_ERR_ARGUMENT, before any device work
     assert b"scratch" in lib.smk_last_error()
