@@ -70,12 +70,15 @@ smk_status smk_ctx_destroy(smk_ctx* ctx);
  *                   starts streaming its weights while the previous GEMV of
  *                   the stream finishes. Requires that no kernel immediately
  *                   before it in the stream writes its weights. Default 0.
- *   SMK_OPT_WARPS   warps per CTA of the quantized fast kernel (1..16, default 8).
+ *   SMK_OPT_WARPS   warps per CTA of the quantized fast kernel (1..16).
  *   SMK_OPT_STAGES  shared-memory stages per warp of that kernel, each one
- *                   tile of weights (1..8, default 2).
- *   SMK_OPT_CTAS_PER_SM  resident CTAs per SM of that kernel (1..8, default 1:
- *                   one persistent CTA per SM, leaving room for the next
- *                   GEMV's CTA under programmatic dependent launch). */
+ *                   tile of weights (1..8).
+ *   SMK_OPT_CTAS_PER_SM  resident CTAs per SM of that kernel (1..8).
+ *                   For these three, 0 (the default) picks per call: 16 warps,
+ *                   1 stage, 1 CTA per SM for GEMVs of up to 64 tiles per SM
+ *                   (latency-bound; leaves room for the next GEMV's CTA under
+ *                   programmatic dependent launch), else 8 warps, 2 stages,
+ *                   2 CTAs per SM. */
 enum { SMK_OPT_PDL = 1, SMK_OPT_WARPS = 2, SMK_OPT_STAGES = 3, SMK_OPT_CTAS_PER_SM = 4 };
 smk_status smk_ctx_set(smk_ctx* ctx, int option, long long value);
 smk_status smk_ctx_get(smk_ctx* ctx, int option, long long* value);

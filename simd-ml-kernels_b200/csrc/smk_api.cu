@@ -107,9 +107,10 @@ struct smk_ctx {
     int num_sms = 148;
     size_t smem_optin = 227 * 1024;
     bool pdl = false;
-    int warps = 8;         // warps per CTA of the fast kernel
-    int stages = 2;        // shared-memory stages per warp
-    int ctas_per_sm = 1;
+    // Launch shape of the quantized fast kernel; 0 = chosen per call (see plan_q).
+    int warps = 0;
+    int stages = 0;
+    int ctas_per_sm = 0;
     unsigned* d_err = nullptr;      // device error word
     unsigned* d_reject = nullptr;   // quantizer rejection flag
     std::mutex mu_scratch;                    // guards scratch and test_buf
@@ -126,9 +127,21 @@ smk::LaunchCfg cfg_for(smk_ctx* c, cudaStream_t s) {
     l.stream = s;
     l.pdl = c->pdl;
     l.num_sms = c->num_sms;
-    l.warps = c->warps;
-    l.ctas_per_sm = c->ctas_per_sm;
+    l.warps = c->warps > 0 ? c->warps : 16;
+    l.ctas_per_sm = c->ctas_per_sm > 0 ? c->ctas_per_sm : 1;
     return l;
+}
+
+// The automatic launch shape (measured on B200, config-0 to LM-head sizes):
+// a GEMV of up to ~64 tiles per SM is latency-bound, best with 16 warps of
+// one stage each and one CTA per SM (the next GEMV's CTA fits beside it under
+// programmatic dependent launch); a larger one is bandwidth-bound, best with
+// 8 warps of two stages and two CTAs per SM.
+void auto_shape(smk_ctx* c, const smk::QGemvParams& p, smk::LaunchCfg* l, int* stages) {
+    const bool large = (long long)p.ntiles >= 64LL * c->num_sms;
+    if (c->warps <= 0) l->warps = large ? 8 : 16;
+    if (c->ctas_per_sm <= 0) l->ctas_per_sm = large ? 2 : 1;
+    *stages = c->stages > 0 ? c->stages : (large ? 2 : 1);
 }
 
 smk_status check_q_args(smk_qformat fmt, int M, int N, int K) {
@@ -147,8 +160,8 @@ struct QPlan {
     smk::QGemvParams p;
 };
 
-QPlan plan_q(smk_ctx* c, smk_qformat fmt, int M, int N, int K, const float* x, int64_t ldx, const uint8_t* Wq, float* y,
-             int64_t ldy, bool want_dump) {
+QPlan plan_q(smk_ctx* c, smk::LaunchCfg* l, smk_qformat fmt, int M, int N, int K, const float* x, int64_t ldx,
+             const uint8_t* Wq, float* y, int64_t ldy, bool want_dump) {
     QPlan q = {};
     smk::QGemvParams& p = q.p;
     p.x = x; p.ldx = ldx; p.w = Wq; p.y = y; p.ldy = ldy;
@@ -158,15 +171,15 @@ QPlan plan_q(smk_ctx* c, smk_qformat fmt, int M, int N, int K, const float* x, i
     smk::plan_tiles(p, q.fast);
     q.x_bytes = smk::xq_total_bytes(M, p.ksteps);
     if (q.fast) {
-        p.stages = c->stages;
+        auto_shape(c, p, l, &p.stages);
         // Quantized x in shared memory while it is small; otherwise one
         // quantize kernel writes it to scratch and every CTA reads it there.
         const size_t budget = 64 * 1024;
         q.x_in_smem = q.x_bytes <= budget || want_dump;
-        size_t smem = smk::gemv_q_smem(fmt, M, p.ksteps, c->warps, p.stages, q.x_in_smem);
+        size_t smem = smk::gemv_q_smem(fmt, M, p.ksteps, l->warps, p.stages, q.x_in_smem);
         while (smem > c->smem_optin && p.stages > 1) {
             --p.stages;
-            smem = smk::gemv_q_smem(fmt, M, p.ksteps, c->warps, p.stages, q.x_in_smem);
+            smem = smk::gemv_q_smem(fmt, M, p.ksteps, l->warps, p.stages, q.x_in_smem);
         }
         if (smem > c->smem_optin) {   // e.g. a dump of a huge M·K: the generic kernel
             q.fast = false;
@@ -185,9 +198,9 @@ smk_status run_q(smk_ctx* c, smk_qformat fmt, int M, int N, int K, const float* 
         for (int m = 0; m < M; ++m) SMK_CUDA(cudaMemsetAsync(y + (size_t)m * ldy, 0, (size_t)N * 4, s), "cudaMemsetAsync");
         return SMK_OK;
     }
-    QPlan q = plan_q(c, fmt, M, N, K, x, ldx, Wq, y, ldy, dump != nullptr);
+    smk::LaunchCfg l = cfg_for(c, s);
+    QPlan q = plan_q(c, &l, fmt, M, N, K, x, ldx, Wq, y, ldy, dump != nullptr);
     q.p.dump = dump;
-    const smk::LaunchCfg l = cfg_for(c, s);
     if (!q.x_in_smem) {
         uint8_t* xq;
         {
@@ -260,15 +273,15 @@ smk_status smk_ctx_set(smk_ctx* c, int option, long long v) {
     switch (option) {
         case SMK_OPT_PDL: c->pdl = v != 0; return SMK_OK;
         case SMK_OPT_WARPS:
-            if (v < 1 || v > 16) return fail(SMK_ERR_ARGUMENT, "warps must be in 1..16");
+            if (v < 0 || v > 16) return fail(SMK_ERR_ARGUMENT, "warps must be in 0..16 (0: automatic)");
             c->warps = (int)v;
             return SMK_OK;
         case SMK_OPT_STAGES:
-            if (v < 1 || v > 8) return fail(SMK_ERR_ARGUMENT, "stages must be in 1..8");
+            if (v < 0 || v > 8) return fail(SMK_ERR_ARGUMENT, "stages must be in 0..8 (0: automatic)");
             c->stages = (int)v;
             return SMK_OK;
         case SMK_OPT_CTAS_PER_SM:
-            if (v < 1 || v > 8) return fail(SMK_ERR_ARGUMENT, "CTAs per SM must be in 1..8");
+            if (v < 0 || v > 8) return fail(SMK_ERR_ARGUMENT, "CTAs per SM must be in 0..8 (0: automatic)");
             c->ctas_per_sm = (int)v;
             return SMK_OK;
         default: return fail(SMK_ERR_ARGUMENT, "unknown option %d", option);

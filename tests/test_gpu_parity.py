@@ -298,9 +298,9 @@ def test_launch_settings_bitwise_equal(sk, torch, fmt):
                     np.testing.assert_array_equal(got.view(np.uint32), base[key].view(np.uint32),
                                                   err_msg=f"{fmt} {key} warps={warps} stages={stages} ctas={ctas}")
     finally:
-        _core._ctx_set(2, 8)
-        _core._ctx_set(3, 2)
-        _core._ctx_set(4, 1)
+        _core._ctx_set(2, 0)
+        _core._ctx_set(3, 0)
+        _core._ctx_set(4, 0)
         sk.set_pdl(False)
 
 
