@@ -514,6 +514,22 @@ PYBIND11_MODULE(_core, m) {
           py::arg("stream") = py::none());
     m.def("gemv_dense", &py_gemv_dense, py::arg("x"), py::arg("W"), py::arg("wtype") = "float32",
           py::arg("out") = py::none(), py::arg("stream") = py::none());
+    // The device path of the Python package for torch CUDA tensors: the
+    // package validated dtypes, shapes and contiguity (the reference's
+    // checks and messages); this only launches.
+    m.def("_gemv_q_dev",
+          [](int fmt, int M, int N, int K, uintptr_t x, long long ldx, uintptr_t w, uintptr_t y, long long ldy,
+             uintptr_t stream, int device) {
+              smk_ctx* c = ctx_for(device);
+              smk_status st;
+              {
+                  py::gil_scoped_release release;
+                  st = smk_gemv_q(c, (smk_qformat)fmt, M, N, K, reinterpret_cast<const float*>(x), ldx,
+                                  reinterpret_cast<const uint8_t*>(w), reinterpret_cast<float*>(y), ldy,
+                                  reinterpret_cast<void*>(stream));
+              }
+              check(st);
+          });
     m.def("version", []() { return std::string(smk_version()); });
     m.def("_set_device", [](int d) { current_device_hint = d; });
     m.def("_ctx_set", [](int option, long long value) { check(smk_ctx_set(ctx_for(current_device_hint), option, value)); });

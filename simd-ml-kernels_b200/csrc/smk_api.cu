@@ -98,6 +98,48 @@ bool is_device_ptr(const void* p) {
 
 size_t align256(size_t n) { return (n + 255) & ~(size_t)255; }
 
+// Where a pointer lives: device (or managed) memory, page-locked host memory
+// mapped into the device's address space (the device address is returned),
+// or ordinary pageable host memory.
+enum class Mem { kDevice, kPinned, kPageable };
+Mem mem_kind(const void* p, void** dev_addr) {
+    *dev_addr = nullptr;
+    cudaPointerAttributes a;
+    if (!p || cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return Mem::kPageable;
+    }
+    if (a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged) return Mem::kDevice;
+    if (a.type == cudaMemoryTypeHost && a.devicePointer) {
+        *dev_addr = a.devicePointer;
+        return Mem::kPinned;
+    }
+    return Mem::kPageable;
+}
+
+// Page-locked, device-mapped host buffer, grown on demand.
+struct PinnedBuf {
+    void* ptr = nullptr;
+    size_t bytes = 0;
+    cudaError_t reserve(size_t want) {
+        if (want <= bytes) return cudaSuccess;
+        size_t n = std::max(want, bytes * 2);
+        n = (n + 4095) & ~(size_t)4095;
+        void* p = nullptr;
+        cudaError_t e = cudaHostAlloc(&p, n, cudaHostAllocMapped | cudaHostAllocPortable);
+        if (e != cudaSuccess) return e;
+        if (ptr) cudaFreeHost(ptr);
+        ptr = p;
+        bytes = n;
+        return cudaSuccess;
+    }
+    void release() {
+        if (ptr) cudaFreeHost(ptr);
+        ptr = nullptr;
+        bytes = 0;
+    }
+};
+
 }  // namespace
 
 void smk::set_last_error(const char* msg) { g_last_error = msg; }
@@ -117,7 +159,8 @@ struct smk_ctx {
     std::map<cudaStream_t, DevBuf> scratch;   // per-stream quantized-x scratch
     DevBuf test_buf;                          // test hooks
     std::mutex mu_stage;                      // held for a whole *_host call
-    DevBuf staging;                           // *_host operands
+    DevBuf staging;                           // *_host operands copied to the device (weights)
+    PinnedBuf pinned;                         // *_host activations and outputs in pageable memory
 };
 
 namespace {
@@ -192,7 +235,7 @@ QPlan plan_q(smk_ctx* c, smk::LaunchCfg* l, smk_qformat fmt, int M, int N, int K
 }
 
 smk_status run_q(smk_ctx* c, smk_qformat fmt, int M, int N, int K, const float* x, int64_t ldx, const uint8_t* Wq,
-                 float* y, int64_t ldy, cudaStream_t s, int32_t* dump) {
+                 float* y, int64_t ldy, cudaStream_t s, int32_t* dump, bool x_read_once = false) {
     if (M == 0 || N == 0) return SMK_OK;
     if (K == 0) {
         for (int m = 0; m < M; ++m) SMK_CUDA(cudaMemsetAsync(y + (size_t)m * ldy, 0, (size_t)N * 4, s), "cudaMemsetAsync");
@@ -201,6 +244,11 @@ smk_status run_q(smk_ctx* c, smk_qformat fmt, int M, int N, int K, const float* 
     smk::LaunchCfg l = cfg_for(c, s);
     QPlan q = plan_q(c, &l, fmt, M, N, K, x, ldx, Wq, y, ldy, dump != nullptr);
     q.p.dump = dump;
+    if (x_read_once && q.x_in_smem && !dump) {
+        // x lives in host memory mapped into the device: one quantize kernel
+        // reads it once, instead of every CTA reading it over the bus.
+        q.x_in_smem = false;
+    }
     if (!q.x_in_smem) {
         uint8_t* xq;
         {
@@ -262,6 +310,7 @@ smk_status smk_ctx_destroy(smk_ctx* c) {
     cudaDeviceSynchronize();
     for (auto& kv : c->scratch) kv.second.release();
     c->staging.release();
+    c->pinned.release();
     c->test_buf.release();
     cudaFree(c->d_err);
     delete c;
@@ -355,22 +404,52 @@ smk_status smk_gemv_q_host(smk_ctx* c, smk_qformat fmt, int M, int N, int K, con
     DeviceGuard g(c->device);
     if (!g.ok) return fail(SMK_ERR_CUDA, "cudaSetDevice(%d) failed", c->device);
     const size_t xb = (size_t)M * K * 4, wb = (size_t)N * (K / 32) * smk::block_bytes(fmt), yb = (size_t)M * N * 4;
-    const bool xh = K > 0 && !is_device_ptr(x), wh = K > 0 && !is_device_ptr(Wq), yh = !is_device_ptr(y);
+    // Host activations reach the device by one DMA copy (from page-locked
+    // memory: the caller's, or this context's page-locked buffer for a
+    // pageable array); reading them in place over the bus is slower. Host
+    // outputs are written by the GEMV straight into page-locked memory
+    // (mapped into the device's address space under unified addressing),
+    // which costs less than a copy back. Weights in host memory are copied
+    // to the device (device-resident weights are the fast path).
+    void *xmap = nullptr, *wmap = nullptr, *ymap = nullptr;
+    const Mem xk = K > 0 ? mem_kind(x, &xmap) : Mem::kDevice;
+    const Mem wk = K > 0 ? mem_kind(Wq, &wmap) : Mem::kDevice;
+    const Mem yk = mem_kind(y, &ymap);
     cudaStream_t s = nullptr;   // the legacy default stream: ordered after other blocking streams' work
     std::lock_guard<std::mutex> lock(c->mu_stage);
-    const size_t ox = 0, ow = ox + (xh ? align256(xb) : 0), oy = ow + (wh ? align256(wb) : 0),
-                 total = oy + (yh ? align256(yb) : 0);
-    if (total) SMK_CUDA(c->staging.reserve(total), "cudaMalloc (staging)");
-    char* base = static_cast<char*>(c->staging.ptr);
-    const float* dx = xh ? reinterpret_cast<const float*>(base + ox) : x;
-    const uint8_t* dw = wh ? reinterpret_cast<const uint8_t*>(base + ow) : Wq;
-    float* dy = yh ? reinterpret_cast<float*>(base + oy) : y;
-    if (xh) SMK_CUDA(cudaMemcpyAsync(base + ox, x, xb, cudaMemcpyHostToDevice, s), "cudaMemcpyAsync (x)");
-    if (wh) SMK_CUDA(cudaMemcpyAsync(base + ow, Wq, wb, cudaMemcpyHostToDevice, s), "cudaMemcpyAsync (Wq)");
+    const size_t px = xk == Mem::kPageable ? align256(xb) : 0, py = yk == Mem::kPageable ? align256(yb) : 0;
+    if (px + py) SMK_CUDA(c->pinned.reserve(px + py), "cudaHostAlloc (staging)");
+    char* pin = static_cast<char*>(c->pinned.ptr);
+    const size_t dxo = 0, dwo = xk != Mem::kDevice ? align256(xb) : 0;
+    const size_t dev_bytes = dwo + (wk != Mem::kDevice ? wb : 0);
+    if (dev_bytes) SMK_CUDA(c->staging.reserve(dev_bytes), "cudaMalloc (staging)");
+    char* dst = static_cast<char*>(c->staging.ptr);
+    const float* dx = x;
+    if (xk != Mem::kDevice) {
+        const void* src = x;
+        if (xk == Mem::kPageable) {
+            std::memcpy(pin, x, xb);
+            src = pin;
+        }
+        SMK_CUDA(cudaMemcpyAsync(dst + dxo, src, xb, cudaMemcpyHostToDevice, s), "cudaMemcpyAsync (x)");
+        dx = reinterpret_cast<const float*>(dst + dxo);
+    }
+    const uint8_t* dw = Wq;
+    if (wk != Mem::kDevice) {
+        SMK_CUDA(cudaMemcpyAsync(dst + dwo, Wq, wb, cudaMemcpyHostToDevice, s), "cudaMemcpyAsync (Wq)");
+        dw = reinterpret_cast<const uint8_t*>(dst + dwo);
+    }
+    float* dy = y;
+    if (yk == Mem::kPinned) dy = static_cast<float*>(ymap);
+    if (yk == Mem::kPageable) {
+        void* dm = nullptr;
+        SMK_CUDA(cudaHostGetDevicePointer(&dm, pin + px, 0), "cudaHostGetDevicePointer");
+        dy = static_cast<float*>(dm);
+    }
     st = run_q(c, fmt, M, N, K, dx, K, dw, dy, N, s, nullptr);
     if (st != SMK_OK) return st;
-    if (yh) SMK_CUDA(cudaMemcpyAsync(y, dy, yb, cudaMemcpyDeviceToHost, s), "cudaMemcpyAsync (y)");
     SMK_CUDA(cudaStreamSynchronize(s), "cudaStreamSynchronize");
+    if (yk == Mem::kPageable) std::memcpy(y, pin + px, yb);
     return SMK_OK;
 }
 

@@ -131,12 +131,69 @@ def _set_device_of(*arrays) -> None:
             return
 
 
-def _gemv(core_fn, x, Wq, N, K, out, out_shape):
-    """x on the device: a device call queued on torch's current stream, CUDA
-    tensor result. x in host memory: the reference's synchronous contract
-    (weights may be device-resident), NumPy result."""
+_raw_stream = None
+
+
+def _current_stream(index):
+    """The raw cudaStream_t of torch's current stream on a device."""
+    global _raw_stream
+    t = _torch()
+    if _raw_stream is None:
+        _raw_stream = getattr(t._C, "_cuda_getCurrentRawStream", False)
+    if _raw_stream:
+        return _raw_stream(index)
+    return t.cuda.current_stream(index).cuda_stream
+
+
+def _check_dev_gemv(fmt, x, Wq, N, K, out, batched):
+    """The reference's argument checks (pybind_entry.cpp:944-971), for CUDA tensors."""
+    t = _torch()
+    if x.dtype != t.float32:
+        raise DTypeError("x must be float32 (dtype=np.float32). Call arr.astype(np.float32) before passing.")
+    if not x.is_contiguous():
+        raise ArgumentError("x must be C-contiguous. Call numpy.ascontiguousarray(arr) before passing.")
+    if Wq.dtype != t.uint8:
+        raise DTypeError(f"Wq must be uint8 (blocks from quantize_{fmt}; dtype=np.uint8)")
+    if not Wq.is_contiguous():
+        raise ArgumentError("Wq must be C-contiguous. Call numpy.ascontiguousarray(arr) before passing.")
+    if N < 0 or K < 0:
+        raise ArgumentError("N and K must be >= 0")
+    if K % 32:
+        raise ArgumentError(f"K must be a multiple of 32 (got {K})")
+    if not batched:
+        if x.dim() != 1 or x.shape[0] != K:
+            raise ArgumentError(f"x must be 1-D with K = {K} elements")
+        M = 1
+    else:
+        if x.dim() != 2 or x.shape[1] != K:
+            raise ArgumentError(f"x must be 2-D [M, K] with K = {K}")
+        M = x.shape[0]
+        if M > 8:
+            raise ArgumentError(f"at most 8 rows of x per call (got {M})")
+    bpb = 18 if fmt == "q4_0" else 34
+    if Wq.numel() != N * (K // 32) * bpb:
+        raise ArgumentError(f"Wq must hold N*K/32*{bpb} = {N * (K // 32) * bpb} bytes (got {Wq.numel()})")
+    if Wq.device != x.device:
+        raise ArgumentError("x and Wq must be on the same device")
+    if out is not None and (out.dtype != t.float32 or not out.is_contiguous() or out.numel() != M * N
+                            or out.device != x.device):
+        raise ArgumentError("out must be a contiguous float32 CUDA tensor of M*N values on x's device")
+    return M
+
+
+def _gemv(fmt, core_fn, x, Wq, N, K, out, batched):
+    """x a CUDA tensor: validated here, then queued on torch's current stream;
+    returns a CUDA tensor. x in host memory: the reference's synchronous
+    contract (weights may be device-resident); returns NumPy."""
     if _is_cuda_tensor(x):
-        return _device_call(core_fn, (x, Wq), out_shape, _torch().float32, _wrap(x), _wrap(Wq), N, K, out=out)
+        t = _torch()
+        M = _check_dev_gemv(fmt, x, Wq, N, K, out, batched)
+        if out is None:
+            out = t.empty((M, N) if batched else (N,), dtype=t.float32, device=x.device)
+        index = x.device.index if x.device.index is not None else t.cuda.current_device()
+        _core._gemv_q_dev(0 if fmt == "q4_0" else 1, M, N, K, x.data_ptr(), K, Wq.data_ptr(), out.data_ptr(), N,
+                          _current_stream(index), index)
+        return out
     _set_device_of(Wq, out)
     return core_fn(x, _wrap(Wq), N, K, out=_wrap(out) if out is not None else None)
 
@@ -144,21 +201,21 @@ def _gemv(core_fn, x, Wq, N, K, out, out_shape):
 def gemv_q4_0(x, Wq, N, K, *, out=None):
     """y = x @ W.T [N] float32 for one row x [K], W given as quantize_q4_0 blocks
     (N rows of K/32 blocks of 18 bytes); x is quantized to Q8 blocks inside."""
-    return _gemv(_core.gemv_q4_0, x, Wq, N, K, out, (N,))
+    return _gemv("q4_0", _core.gemv_q4_0, x, Wq, N, K, out, False)
 
 
 def gemv_q8_0(x, Wq, N, K, *, out=None):
     """y = x @ W.T [N] float32, W given as quantize_q8_0 blocks (34 bytes per 32 values)."""
-    return _gemv(_core.gemv_q8_0, x, Wq, N, K, out, (N,))
+    return _gemv("q8_0", _core.gemv_q8_0, x, Wq, N, K, out, False)
 
 
 def gemv_q4_0_batch(x, Wq, N, K, *, out=None):
     """Y = X @ W.T [M, N] for up to 8 rows of X [M, K]; row m equals gemv_q4_0(X[m], Wq, N, K)."""
-    return _gemv(_core.gemv_q4_0_batch, x, Wq, N, K, out, (x.shape[0], N))
+    return _gemv("q4_0", _core.gemv_q4_0_batch, x, Wq, N, K, out, True)
 
 
 def gemv_q8_0_batch(x, Wq, N, K, *, out=None):
-    return _gemv(_core.gemv_q8_0_batch, x, Wq, N, K, out, (x.shape[0], N))
+    return _gemv("q8_0", _core.gemv_q8_0_batch, x, Wq, N, K, out, True)
 
 
 def _quantize(core_fn, W, bpb, out):

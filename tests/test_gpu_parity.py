@@ -339,6 +339,30 @@ def test_dependent_chain_under_pdl(sk, torch, fmt):
         sk.set_pdl(False)
 
 
+@pytest.mark.parametrize("fmt", ["q4_0", "q8_0"])
+def test_host_io_paths_bitwise_equal(sk, torch, fmt):
+    """The synchronous host-memory contract in every combination — x pageable
+    or page-locked (read by the device in place), weights in host or device
+    memory, y returned or written into a given pageable / page-locked array —
+    gives bitwise the result of the all-device path."""
+    N, K = 3000, 2048
+    x, Wq = make_case(31, N, K, fmt)
+    fn = sk.gemv_q4_0 if fmt == "q4_0" else sk.gemv_q8_0
+    wd = torch.from_numpy(Wq.ravel()).cuda()
+    want = fn(torch.from_numpy(x).cuda(), wd, N, K).cpu().numpy()
+    x_pinned = torch.from_numpy(x).pin_memory().numpy()
+    y_pinned = torch.empty(N).pin_memory().numpy()
+    for xs in (x, x_pinned):
+        for ws in (Wq.ravel(), wd):
+            np.testing.assert_array_equal(fn(xs, ws, N, K).view(np.uint32), want.view(np.uint32))
+            y_page = np.empty(N, np.float32)
+            fn(xs, ws, N, K, out=y_page)
+            np.testing.assert_array_equal(y_page.view(np.uint32), want.view(np.uint32))
+            y_pinned[:] = np.nan
+            fn(xs, ws, N, K, out=y_pinned)
+            np.testing.assert_array_equal(y_pinned.view(np.uint32), want.view(np.uint32))
+
+
 def test_row_shards_bitwise_equal_full(sk, torch):
     """Row-sharding (the multi-GPU plan, 8-row groups as the reference's
     gemv_slice): every shard's outputs bitwise equal the unsharded call."""
