@@ -88,11 +88,18 @@ Arr as_arr(const py::handle& h) {
         auto arr = py::reinterpret_borrow<py::array>(h);
         a.ptr = const_cast<void*>(arr.data());
         for (int i = 0; i < arr.ndim(); ++i) a.shape.push_back(arr.shape(i));
-        a.kind = arr.dtype().kind();
-        a.itemsize = (int)arr.dtype().itemsize();
-        a.name = py::str(arr.dtype().attr("name"));
-        a.contiguous = arr.attr("flags").attr("c_contiguous").cast<bool>();
-        a.writeable = arr.attr("flags").attr("writeable").cast<bool>();
+        const py::dtype dt = arr.dtype();
+        a.kind = dt.kind();
+        a.itemsize = (int)dt.itemsize();
+        // The dtype's name is only read to tell ml_dtypes.bfloat16 apart and
+        // for error messages: fetched for 2-byte types that are not plain
+        // numbers, not on every call.
+        if (a.itemsize == 2 && a.kind != 'f' && a.kind != 'i' && a.kind != 'u')
+            a.name = py::str(dt.attr("name"));
+        else
+            a.name = std::string(1, a.kind) + std::to_string(a.itemsize);
+        a.contiguous = (arr.flags() & py::array::c_style) != 0;
+        a.writeable = arr.writeable();
         return a;
     }
     if (py::hasattr(h, "__cuda_array_interface__")) {
@@ -145,12 +152,11 @@ void check_writeable(const Arr& a, const char* name) {
 
 // ---- GEMV on ggml blocks (pybind_entry.cpp:944-995) -------------------------
 
-py::object gemv_blocks(const py::handle& xh, const py::handle& wh, py::ssize_t N, py::ssize_t K, int block_bytes,
+py::object gemv_blocks(const py::handle& xh, const Arr& w, py::ssize_t N, py::ssize_t K, int block_bytes,
                        const char* fmt_name, smk_qformat fmt, const py::object& out, const py::object& stream,
                        bool batched) {
     const Arr x = as_arr(xh);
     validate_array(x, "x");
-    const Arr w = as_arr(wh);
     if (w.kind != 'u' || w.itemsize != 1)
         throw DTypeError(std::string("Wq must be uint8 (blocks from quantize_") + fmt_name + "; dtype=np.uint8)");
     check_contiguous(w, "Wq");
@@ -458,21 +464,21 @@ PYBIND11_MODULE(_core, m) {
 
     m.def("gemv_q4_0",
           [](py::handle x, py::handle Wq, py::ssize_t N, py::ssize_t K, py::object out, py::object stream) {
-              return gemv_blocks(x, Wq, N, K, 18, "q4_0", SMK_Q4_0, out, stream, false);
+              return gemv_blocks(x, as_arr(Wq), N, K, 18, "q4_0", SMK_Q4_0, out, stream, false);
           },
           py::arg("x"), py::arg("Wq"), py::arg("N"), py::arg("K"), py::kw_only(), py::arg("out") = py::none(),
           py::arg("stream") = py::none(),
           "gemv_q4_0(x, Wq, N, K) -> float32 [N]: y = x @ W.T, W as quantize_q4_0 blocks; x quantized to Q8 inside.");
     m.def("gemv_q8_0",
           [](py::handle x, py::handle Wq, py::ssize_t N, py::ssize_t K, py::object out, py::object stream) {
-              return gemv_blocks(x, Wq, N, K, 34, "q8_0", SMK_Q8_0, out, stream, false);
+              return gemv_blocks(x, as_arr(Wq), N, K, 34, "q8_0", SMK_Q8_0, out, stream, false);
           },
           py::arg("x"), py::arg("Wq"), py::arg("N"), py::arg("K"), py::kw_only(), py::arg("out") = py::none(),
           py::arg("stream") = py::none(),
           "gemv_q8_0(x, Wq, N, K) -> float32 [N]: y = x @ W.T, W as quantize_q8_0 blocks.");
     m.def("gemv_q4_0_batch",
           [](py::handle x, py::handle Wq, py::ssize_t N, py::ssize_t K, py::object out, py::object stream) {
-              return gemv_blocks(x, Wq, N, K, 18, "q4_0", SMK_Q4_0, out, stream, true);
+              return gemv_blocks(x, as_arr(Wq), N, K, 18, "q4_0", SMK_Q4_0, out, stream, true);
           },
           py::arg("x"), py::arg("Wq"), py::arg("N"), py::arg("K"), py::kw_only(), py::arg("out") = py::none(),
           py::arg("stream") = py::none(),
@@ -480,7 +486,7 @@ PYBIND11_MODULE(_core, m) {
           "as one gemv_q4_0 call.");
     m.def("gemv_q8_0_batch",
           [](py::handle x, py::handle Wq, py::ssize_t N, py::ssize_t K, py::object out, py::object stream) {
-              return gemv_blocks(x, Wq, N, K, 34, "q8_0", SMK_Q8_0, out, stream, true);
+              return gemv_blocks(x, as_arr(Wq), N, K, 34, "q8_0", SMK_Q8_0, out, stream, true);
           },
           py::arg("x"), py::arg("Wq"), py::arg("N"), py::arg("K"), py::kw_only(), py::arg("out") = py::none(),
           py::arg("stream") = py::none());
@@ -529,6 +535,24 @@ PYBIND11_MODULE(_core, m) {
                                   reinterpret_cast<void*>(stream));
               }
               check(st);
+          });
+    // Host activations against weights already resident on a device (a
+    // torch CUDA tensor the package checked: uint8, contiguous): the
+    // reference's synchronous NumPy contract without describing W through
+    // __cuda_array_interface__ on every call.
+    m.def("_gemv_q_host_dw",
+          [](int fmt, py::handle x, uintptr_t w, long long wbytes, py::ssize_t N, py::ssize_t K, bool batched,
+             int device) {
+              Arr wa;
+              wa.ptr = reinterpret_cast<void*>(w);
+              wa.shape = {wbytes};
+              wa.kind = 'u';
+              wa.itemsize = 1;
+              wa.device = true;
+              wa.device_id = device;
+              const bool q4 = fmt == 0;
+              return gemv_blocks(x, wa, N, K, q4 ? 18 : 34, q4 ? "q4_0" : "q8_0", q4 ? SMK_Q4_0 : SMK_Q8_0,
+                                 py::none(), py::none(), batched);
           });
     m.def("version", []() { return std::string(smk_version()); });
     m.def("_set_device", [](int d) { current_device_hint = d; });

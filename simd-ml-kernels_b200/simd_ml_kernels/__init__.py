@@ -194,6 +194,15 @@ def _gemv(fmt, core_fn, x, Wq, N, K, out, batched):
         _core._gemv_q_dev(0 if fmt == "q4_0" else 1, M, N, K, x.data_ptr(), K, Wq.data_ptr(), out.data_ptr(), N,
                           _current_stream(index), index)
         return out
+    if out is None and _is_cuda_tensor(Wq):
+        # Host x, device-resident weights: checked here, passed as a pointer.
+        t = _torch()
+        if Wq.dtype != t.uint8:
+            raise DTypeError(f"Wq must be uint8 (blocks from quantize_{fmt}; dtype=np.uint8)")
+        if not Wq.is_contiguous():
+            raise ArgumentError("Wq must be C-contiguous. Call numpy.ascontiguousarray(arr) before passing.")
+        return _core._gemv_q_host_dw(0 if fmt == "q4_0" else 1, x, Wq.data_ptr(), Wq.numel(), N, K, batched,
+                                     Wq.get_device())
     _set_device_of(Wq, out)
     return core_fn(x, _wrap(Wq), N, K, out=_wrap(out) if out is not None else None)
 

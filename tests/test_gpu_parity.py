@@ -342,9 +342,10 @@ def test_dependent_chain_under_pdl(sk, torch, fmt):
 @pytest.mark.parametrize("fmt", ["q4_0", "q8_0"])
 def test_host_io_paths_bitwise_equal(sk, torch, fmt):
     """The synchronous host-memory contract in every combination — x pageable
-    or page-locked (read by the device in place), weights in host or device
-    memory, y returned or written into a given pageable / page-locked array —
-    gives bitwise the result of the all-device path."""
+    or page-locked, weights in host or device memory, y returned or written
+    into a given pageable / page-locked array — gives bitwise the result of
+    the all-device path; so does the batched call with device weights, and
+    its argument errors are the reference's."""
     N, K = 3000, 2048
     x, Wq = make_case(31, N, K, fmt)
     fn = sk.gemv_q4_0 if fmt == "q4_0" else sk.gemv_q8_0
@@ -361,6 +362,18 @@ def test_host_io_paths_bitwise_equal(sk, torch, fmt):
             y_pinned[:] = np.nan
             fn(xs, ws, N, K, out=y_pinned)
             np.testing.assert_array_equal(y_pinned.view(np.uint32), want.view(np.uint32))
+    batch = sk.gemv_q4_0_batch if fmt == "q4_0" else sk.gemv_q8_0_batch
+    X = np.stack([x, -x, 0.5 * x])
+    wantM = batch(torch.from_numpy(X).cuda(), wd, N, K).cpu().numpy()
+    np.testing.assert_array_equal(batch(X, wd, N, K).view(np.uint32), wantM.view(np.uint32))
+    with pytest.raises(sk.DTypeError, match="x must be float32"):
+        fn(x.astype(np.float64), wd, N, K)
+    with pytest.raises(sk.DTypeError, match="Wq must be uint8"):
+        fn(x, wd.view(torch.int8), N, K)
+    with pytest.raises(sk.ArgumentError, match="Wq must hold"):
+        fn(x, wd[:-1], N, K)
+    with pytest.raises(sk.ArgumentError, match="x must be 1-D"):
+        fn(x[:-32], wd, N, K)
 
 
 def test_row_shards_bitwise_equal_full(sk, torch):
