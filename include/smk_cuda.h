@@ -84,6 +84,11 @@ smk_status smk_ctx_set(smk_ctx* ctx, int option, long long value);
 smk_status smk_ctx_get(smk_ctx* ctx, int option, long long* value);
 /* The CUDA device that owns `ptr` (device or managed memory), or -1 for host memory. */
 smk_status smk_pointer_device(const void* ptr, int* device);
+/* Page-locked host memory, mapped into every device's address space (an
+ * addition; no reference counterpart). Results written here by a *_host call
+ * need no copy back: the kernel stores into them directly. */
+smk_status smk_host_alloc(size_t bytes, void** out);
+smk_status smk_host_free(void* ptr);
 /* Reads and clears the device error word (0: no kernel error since the last read). */
 smk_status smk_device_error(smk_ctx* ctx, unsigned* code, void* stream);
 

@@ -52,6 +52,73 @@ smk_ctx* ctx_for(int device) {
     return g_ctx[device];
 }
 
+// ---- page-locked result arrays -------------------------------------------------
+//
+// GEMV results returned as new NumPy arrays live in page-locked memory, so the
+// kernel stores y straight into the array the caller receives (no staging
+// buffer, no copy after the synchronise). Blocks are recycled by byte size when
+// their arrays die; a result larger than kMaxBlock, or any result while
+// page-locked memory cannot be had, is an ordinary NumPy array.
+
+struct PinnedPool {
+    static constexpr size_t kMaxBlock = size_t(4) << 20;   // per result array
+    static constexpr size_t kMaxFree = size_t(64) << 20;   // kept for reuse
+    std::mutex mu;
+    std::vector<std::pair<size_t, void*>> free_list;
+    size_t free_bytes = 0;
+
+    void* get(size_t bytes) {
+        {
+            std::lock_guard<std::mutex> g(mu);
+            for (size_t i = 0; i < free_list.size(); ++i) {
+                if (free_list[i].first == bytes) {
+                    void* p = free_list[i].second;
+                    free_list[i] = free_list.back();
+                    free_list.pop_back();
+                    free_bytes -= bytes;
+                    return p;
+                }
+            }
+        }
+        void* p = nullptr;
+        return smk_host_alloc(bytes, &p) == SMK_OK ? p : nullptr;
+    }
+    void put(void* p, size_t bytes) {
+        {
+            std::lock_guard<std::mutex> g(mu);
+            if (free_bytes + bytes <= kMaxFree) {
+                free_list.emplace_back(bytes, p);
+                free_bytes += bytes;
+                return;
+            }
+        }
+        smk_host_free(p);
+    }
+};
+
+PinnedPool* g_pool = new PinnedPool();   // never destroyed: result arrays may outlive the module
+
+struct PinnedBlock {
+    void* ptr;
+    size_t bytes;
+};
+
+py::array_t<float> result_array(const std::vector<py::ssize_t>& shape) {
+    size_t n = 1;
+    for (py::ssize_t d : shape) n *= (size_t)d;
+    const size_t bytes = n * sizeof(float);
+    if (bytes == 0 || bytes > PinnedPool::kMaxBlock) return py::array_t<float>(shape);
+    void* p = g_pool->get(bytes);
+    if (!p) return py::array_t<float>(shape);
+    auto* blk = new PinnedBlock{p, bytes};
+    py::capsule base(blk, [](void* v) {
+        auto* b = static_cast<PinnedBlock*>(v);
+        g_pool->put(b->ptr, b->bytes);
+        delete b;
+    });
+    return py::array_t<float>(shape, static_cast<float*>(p), base);
+}
+
 void check(smk_status st) {
     if (st == SMK_OK) return;
     const std::string msg = smk_last_error();
@@ -188,7 +255,7 @@ py::object gemv_blocks(const py::handle& xh, const Arr& w, py::ssize_t N, py::ss
         if (x.device) throw ArgumentError("out= is required when x is a CUDA array");
         std::vector<py::ssize_t> shp = batched ? std::vector<py::ssize_t>{M, (py::ssize_t)N}
                                                : std::vector<py::ssize_t>{(py::ssize_t)N};
-        py::array_t<float> y(shp);
+        py::array_t<float> y = result_array(shp);
         yp = y.mutable_data();
         result = y;
     } else {
@@ -284,7 +351,7 @@ py::object dense_call(smk_dtype wt, smk_dtype xt, const Arr& A, const Arr& B, in
     bool c_device = false;
     if (C.is_none()) {
         if (A.device) throw ArgumentError("C is required when A is a CUDA array");
-        py::array_t<float> out({(py::ssize_t)M, (py::ssize_t)N});
+        py::array_t<float> out = result_array({(py::ssize_t)M, (py::ssize_t)N});
         cp = out.mutable_data();
         if (M * (int64_t)N) std::memset(cp, 0, sizeof(float) * (size_t)M * N);
         result = out;

@@ -348,6 +348,19 @@ smk_status smk_ctx_get(smk_ctx* c, int option, long long* v) {
     }
 }
 
+smk_status smk_host_alloc(size_t bytes, void** out) {
+    if (!out) return fail(SMK_ERR_ARGUMENT, "out must not be NULL");
+    *out = nullptr;
+    if (bytes == 0) return SMK_OK;
+    SMK_CUDA(cudaHostAlloc(out, bytes, cudaHostAllocMapped | cudaHostAllocPortable), "cudaHostAlloc");
+    return SMK_OK;
+}
+
+smk_status smk_host_free(void* ptr) {
+    if (ptr) SMK_CUDA(cudaFreeHost(ptr), "cudaFreeHost");
+    return SMK_OK;
+}
+
 smk_status smk_pointer_device(const void* ptr, int* device) {
     if (!device) return fail(SMK_ERR_ARGUMENT, "device must not be NULL");
     *device = -1;

@@ -362,6 +362,16 @@ def test_host_io_paths_bitwise_equal(sk, torch, fmt):
             y_pinned[:] = np.nan
             fn(xs, ws, N, K, out=y_pinned)
             np.testing.assert_array_equal(y_pinned.view(np.uint32), want.view(np.uint32))
+    # Results come back in page-locked arrays recycled from a pool: live
+    # results never share memory, and a recycled block holds the new result.
+    ya, yb = fn(x_pinned, wd, N, K), fn(-x_pinned, wd, N, K)
+    assert torch.from_numpy(ya).is_pinned() and not np.shares_memory(ya, yb)
+    np.testing.assert_array_equal(ya.view(np.uint32), want.view(np.uint32))
+    np.testing.assert_array_equal(yb, -want)
+    del ya
+    yc = fn(x_pinned, wd, N, K)
+    np.testing.assert_array_equal(yc.view(np.uint32), want.view(np.uint32))
+    np.testing.assert_array_equal(yb, -want)
     batch = sk.gemv_q4_0_batch if fmt == "q4_0" else sk.gemv_q8_0_batch
     X = np.stack([x, -x, 0.5 * x])
     wantM = batch(torch.from_numpy(X).cuda(), wd, N, K).cpu().numpy()
