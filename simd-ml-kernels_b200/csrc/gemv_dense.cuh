@@ -22,6 +22,7 @@ struct DenseParams {
     long long ldy;
     int M, N, K;
     float alpha, beta;
+    unsigned* err;     // device error word (bounded waits), may be null
 };
 
 cudaError_t launch_gemv_dense(cudaStream_t s, bool pdl, int num_sms, int w_kind, int x_kind, const DenseParams& p);

@@ -482,6 +482,7 @@ smk_status smk_gemv_dense(smk_ctx* c, smk_dtype wt, smk_dtype xt, int M, int N, 
     smk::DenseParams p;
     p.x = X; p.ldx = ldx; p.w = W; p.ldw = ldw; p.y = C; p.ldy = ldc;
     p.M = M; p.N = N; p.K = K; p.alpha = alpha; p.beta = beta;
+    p.err = c->d_err;
     SMK_CUDA(smk::launch_gemv_dense(static_cast<cudaStream_t>(stream), c->pdl, c->num_sms, (int)wt, (int)xt, p),
              "dense gemv launch");
     return SMK_OK;

@@ -448,6 +448,30 @@ def test_dense_fp32_x(sk, torch, wtype, M, N, K):
     assert (np.abs(Y - y64) <= bound).all(), f"max err/bound {np.max(np.abs(Y - y64) / bound):.3g}"
 
 
+@pytest.mark.parametrize("kind", ["f32", "f16", "bf16"])
+@pytest.mark.parametrize("M,N,K", [(1, 1001, 1000), (5, 7, 8), (7, 33, 2056), (2, 3, 16), (8, 13, 520)])
+def test_dense_streaming_edges(sk, kind, M, N, K):
+    """The TMA-streaming dense kernel's edges: rows not a multiple of the
+    4-row item, a last K chunk shorter than 1 KB, K below one chunk, every M,
+    and the alpha/beta epilogue."""
+    rng = np.random.default_rng(7 * M + N + K)
+    A = rng.uniform(-1, 1, (M, K)).astype(np.float32)
+    B = rng.uniform(-1, 1, (N, K)).astype(np.float32)
+    C0 = rng.uniform(-1, 1, (M, N)).astype(np.float32)
+    a, b = _dense_operands(kind, A, B)
+    fn = {"f32": sk.sgemm, "f16": sk.sgemm_f16, "bf16": sk.sgemm_bf16}[kind]
+    if kind == "f16":
+        a, b = a.view(np.float16), b.view(np.float16)
+    for alpha, beta in ((1.0, 0.0), (-1.5, 0.5)):
+        C = C0.copy()
+        fn(a, b, C=C, alpha=alpha, beta=beta, trans_b=True)
+        y64, mag = O.dense_ref64(a.view(np.uint16) if kind != "f32" else a, kind,
+                                 b.view(np.uint16) if kind != "f32" else b, kind)
+        want = alpha * y64 + beta * C0.astype(np.float64)
+        bound = 2 * (K + 2) * U * (abs(alpha) * mag + abs(beta) * np.abs(C0)) + 1e-300
+        assert (np.abs(C - want) <= bound).all(), f"{kind} alpha={alpha}: max err/bound {np.max(np.abs(C - want) / bound):.3g}"
+
+
 def test_dense_rejects_non_decode(sk):
     A = np.ones((9, 16), np.float32)
     B = np.ones((4, 16), np.float32)
