@@ -289,9 +289,12 @@ def gpu_bench(args, rank: int, world: int, local_rank: int) -> dict | None:
 
     if args.only_gemv:
         if rank == 0:
-            return {"metric": METRIC, "value": round(STEP_BYTES * world * steps / (ms_max * 1e-3) / 1e9, 2),
-                    "unit": "GB/s", "n_gpus": world, "steps": steps, "ms_per_step": ms_max / steps,
-                    "only_gemv": True}
+            out = {"metric": METRIC, "value": round(STEP_BYTES * world * steps / (ms_max * 1e-3) / 1e9, 2),
+                   "unit": "GB/s", "n_gpus": world, "steps": steps, "ms_per_step": ms_max / steps,
+                   "only_gemv": True}
+            if args.case and world == 1:
+                out["configs"] = other_configs(sk, torch, dev, stream, args.case)
+            return out
         return None
 
     # End to end through the public API: x from pinned host memory, y back to
@@ -331,8 +334,8 @@ def gpu_bench(args, rank: int, world: int, local_rank: int) -> dict | None:
     extra = {}
     if rank == 0 and world == 1:
         extra["llama_stack"] = llama_stack(sk, torch, dev, stream, args)
-        if args.all:
-            extra["configs"] = other_configs(sk, torch, dev, stream)
+        if args.all or args.case:
+            extra["configs"] = other_configs(sk, torch, dev, stream, args.case)
 
     if rank != 0:
         return None
@@ -426,8 +429,9 @@ def llama_stack(sk, torch, dev, stream, args) -> dict:
             "launch": "one CUDA graph of 128 decode steps, PDL; q/k/v and gate/up as fused row groups"}
 
 
-def other_configs(sk, torch, dev, stream) -> dict:
-    """Configs 1 (Q8_0), 3 (dense fp32/bf16/fp16, M in 1,4,8) and 4 (large Q4_0, M 1/8) on one GPU."""
+def other_configs(sk, torch, dev, stream, only: str | None = None) -> dict:
+    """Configs 1 (Q8_0), 3 (dense fp32/bf16/fp16, M in 1,4,8) and 4 (large Q4_0, M 1/8) on one GPU;
+    `only`: time just the cases whose label contains it (for profilers)."""
     res = {}
     l2 = getattr(torch.cuda.get_device_properties(dev), "L2_cache_size", 126 << 20)
 
@@ -436,6 +440,8 @@ def other_configs(sk, torch, dev, stream) -> dict:
         return copies_needed, fn, reps
 
     def run(label, make_w, call, nbytes):
+        if only is not None and only not in label:
+            return
         copies = max(2, -(-2 * l2 // nbytes) + 1)
         ws = [make_w()] + []
         for _ in range(copies - 1):
@@ -504,6 +510,8 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--all", action="store_true", help="also time configs 1, 3 and 4 (one GPU)")
     ap.add_argument("--cpu-baseline-seconds", type=float, default=8.0)
+    ap.add_argument("--case", default=None,
+                    help="time only the config 1/3/4 cases whose label contains this text (after the config-0 line)")
     ap.add_argument("--only-gemv", action="store_true",
                     help="time the config-0 GEMV only (no e2e, Llama stack or CPU baseline): for profilers")
     args = ap.parse_args()

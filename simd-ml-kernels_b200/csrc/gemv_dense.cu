@@ -197,7 +197,7 @@ struct DenseGeom {
 // x [M, K] into shared memory as FP32 (row stride kp), every thread keeping
 // kXInFlight 16-byte loads in flight per round, so staging costs a few L2 round
 // trips rather than one per element.
-constexpr int kXInFlight = 4;
+constexpr int kXInFlight = 8;
 
 template <int XK, int M>
 __device__ __forceinline__ void stage_x(const DenseParams& p, const DenseGeom& g, float* xs) {
@@ -254,8 +254,8 @@ __device__ __forceinline__ void dense_issue(const DenseParams& p, const DenseGeo
     }
 }
 
-template <int WK, int XK, int M>
-__global__ void __launch_bounds__(kDWarps * 32, 1) gemv_dense_tma(const DenseParams p, const DenseGeom g) {
+template <int WK, int XK, int M, int WARPS>
+__global__ void __launch_bounds__(WARPS * 32, 1) gemv_dense_tma(const DenseParams p, const DenseGeom g) {
     constexpr int ES = WK == kF32 ? 4 : 2;
     constexpr int EPV = 16 / ES;                 // elements per 16-byte vector
     constexpr int HALF = kDRowBytes / 2 / ES;    // elements per half row chunk
@@ -263,7 +263,8 @@ __global__ void __launch_bounds__(kDWarps * 32, 1) gemv_dense_tma(const DensePar
     extern __shared__ __align__(128) uint8_t smem[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem) + warp * g.stages;
-    size_t off = ((size_t)nwarps * g.stages * 8 + 127) & ~(size_t)127;
+    uint64_t* xbar = reinterpret_cast<uint64_t*>(smem) + nwarps * g.stages;   // x copies (FP32 x)
+    size_t off = ((size_t)(nwarps * g.stages + 1) * 8 + 127) & ~(size_t)127;
     float* xs = reinterpret_cast<float*>(smem + off);
     off += ((size_t)M * g.kp * 4 + 127) & ~(size_t)127;
     uint8_t* ring = smem + off + (size_t)warp * g.stages * ITEM;
@@ -273,11 +274,14 @@ __global__ void __launch_bounds__(kDWarps * 32, 1) gemv_dense_tma(const DensePar
     const int gw = warp * gridDim.x + blockIdx.x;
     const int my_tiles = gw < g.ntiles ? (g.ntiles - 1 - gw) / GW + 1 : 0;
     const int nitems = my_tiles * g.ksteps;
+    constexpr bool kXBulk = XK == kF32;   // FP32 x rows go to shared memory by bulk copies
     if (lane == 0) {
         for (int i = 0; i < g.stages; ++i) mbar_init(&bars[i], 1);
+        if (kXBulk && threadIdx.x == 0) mbar_init(xbar, 1);
         fence_mbar_init();
     }
-    __syncwarp();
+    if (kXBulk) __syncthreads();   // xbar initialised before any thread waits on it
+    else __syncwarp();
     int c_tile = gw, c_ks = 0, c_slot = 0, i_tile = gw, i_ks = 0, i_slot = 0;
     uint32_t c_phase = 0;
     int issued = 0;
@@ -288,8 +292,23 @@ __global__ void __launch_bounds__(kDWarps * 32, 1) gemv_dense_tma(const DensePar
     }
 
     pdl_wait_primary();   // x and C may come from the previous kernel
-    stage_x<XK, M>(p, g, xs);
-    __syncthreads();
+    if (kXBulk && g.xvec) {
+        // One bulk copy per row of x (K·4 bytes, 16-byte aligned on both sides).
+        if (threadIdx.x == 0) {
+            mbar_arrive_expect_tx(xbar, (uint32_t)M * (uint32_t)p.K * 4u);
+            for (int m = 0; m < M; ++m)
+                tma_load_1d(xs + (size_t)m * g.kp, reinterpret_cast<const float*>(p.x) + (size_t)m * p.ldx,
+                            (uint32_t)p.K * 4u, xbar);
+        }
+        if (!mbar_wait_bounded(xbar, 0u, p.err)) {
+            // x never arrived: drain this warp's weight copies (bounded) and stop.
+            for (int k = 0; k < issued; ++k) mbar_wait_bounded(&bars[k], 0u, nullptr);
+            return;
+        }
+    } else {
+        stage_x<XK, M>(p, g, xs);
+        __syncthreads();
+    }
 
     float2 acc[kDTR][M];
 #pragma unroll
@@ -397,22 +416,25 @@ cudaError_t launch_tma(cudaStream_t s, bool pdl, int num_sms, const DenseParams&
     }
     const int optin = smem_optin_of_current_device();
     const size_t xbytes = ((size_t)M * g.kp * 4 + 127) & ~(size_t)127;
-    const size_t per_stage = (size_t)kDWarps * kDTR * kDRowBytes;
-    const size_t fixed = xbytes + 128 + 1024;   // x, barriers (rounded), slack
+    // More warps hide the shared-memory and FMA latency of the larger M;
+    // 12 warps of the M = 8 kernel still fit the register file.
+    constexpr int WARPS = M <= 2 ? kDWarps : 12;
+    const size_t per_stage = (size_t)WARPS * kDTR * kDRowBytes;
+    const size_t fixed = xbytes + 256 + 1024;   // x, barriers (rounded), slack
     if (optin <= 0 || (size_t)optin < fixed + 2 * per_stage) return cudaErrorNotSupported;
     g.stages = (int)std::min<size_t>(6, ((size_t)optin - fixed) / per_stage);
-    const size_t smem = (((size_t)kDWarps * g.stages * 8 + 127) & ~(size_t)127) + xbytes + g.stages * per_stage;
-    auto k = gemv_dense_tma<WK, XK, M>;
+    const size_t smem = (((size_t)(WARPS * g.stages + 1) * 8 + 127) & ~(size_t)127) + xbytes + g.stages * per_stage;
+    auto k = gemv_dense_tma<WK, XK, M, WARPS>;
     int per_sm = 0;
-    cudaError_t e = occupancy((const void*)k, kDWarps * 32, smem, &per_sm);
+    cudaError_t e = occupancy((const void*)k, WARPS * 32, smem, &per_sm);
     if (e != cudaSuccess) return e;
     if (per_sm < 1) return cudaErrorNotSupported;
-    const long long want = std::max<long long>(((long long)g.ntiles + kDWarps - 1) / kDWarps,
+    const long long want = std::max<long long>(((long long)g.ntiles + WARPS - 1) / WARPS,
                                                std::min<long long>(g.ntiles, num_sms));
     const long long grid = std::max<long long>(1, std::min<long long>(want, num_sms));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)grid);
-    cfg.blockDim = dim3(kDWarps * 32);
+    cfg.blockDim = dim3(WARPS * 32);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
