@@ -27,6 +27,8 @@
 #include "gemv_quant.cuh"
 #include "smk_device.cuh"
 
+#include <cudaTypedefs.h>
+
 #include <algorithm>
 #include <cfloat>
 #include <map>
@@ -57,11 +59,16 @@ struct XGeom {
     int M, nb, log2G, ksteps;
 };
 
-// All 32 lanes of the warp call this together (full-mask shuffles; the xor
-// offsets stay inside each 8-lane group); lanes with valid == false compute
-// on their (zero) values and store nothing.
-__device__ __forceinline__ void quantize_x_block(float4 v, int gq, bool valid, const XGeom& xg, int m, int b,
-                                                 uint8_t* xb) {
+// One thread's 4 values of a 32-value block, quantized to Q8: all 32 lanes of
+// the warp call this together (full-mask shuffles; the xor offsets stay inside
+// each 8-lane group of one block).
+struct Q8Quad {
+    uint32_t word;   // the 4 int8 quants, value 0 in the low byte
+    float dx;        // the block's scale; NaN when a value of the block is not finite
+    int s;           // Σ of the block's 32 quants
+};
+
+__device__ __forceinline__ Q8Quad quantize_quad(float4 v) {
     constexpr unsigned gmask = 0xffffffffu;
     unsigned fin = finite_bits(v.x) & finite_bits(v.y) & finite_bits(v.z) & finite_bits(v.w);
     float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
@@ -78,21 +85,32 @@ __device__ __forceinline__ void quantize_x_block(float4 v, int gq, bool valid, c
     const int q1 = fin ? (int)roundf(__fmul_rn(v.y, id)) : 0;
     const int q2 = fin ? (int)roundf(__fmul_rn(v.z, id)) : 0;
     const int q3 = fin ? (int)roundf(__fmul_rn(v.w, id)) : 0;
-    const uint32_t word = (uint32_t)(q0 & 0xff) | ((uint32_t)(q1 & 0xff) << 8) | ((uint32_t)(q2 & 0xff) << 16) |
-                          ((uint32_t)(q3 & 0xff) << 24);
+    Q8Quad r;
+    r.word = (uint32_t)(q0 & 0xff) | ((uint32_t)(q1 & 0xff) << 8) | ((uint32_t)(q2 & 0xff) << 16) |
+             ((uint32_t)(q3 & 0xff) << 24);
     int s = q0 + q1 + q2 + q3;
 #pragma unroll
     for (int o = 4; o > 0; o >>= 1) s += __shfl_xor_sync(gmask, s, o);
+    r.s = s;
+    r.dx = fin ? d : __int_as_float(0x7fc00000);
+    return r;
+}
+
+// quantize_quad, stored in the lane-major layout; lanes with valid == false
+// compute on their (zero) values and store nothing.
+__device__ __forceinline__ void quantize_x_block(float4 v, int gq, bool valid, const XGeom& xg, int m, int b,
+                                                 uint8_t* xb) {
+    const Q8Quad q = quantize_quad(v);
     // Offsets in 32 bits (the layout stays far below 4 GiB), no division.
     const unsigned sb = (unsigned)b >> 3, j = (unsigned)b & 7u;
     const unsigned ks = sb >> xg.log2G, g = sb & ((1u << xg.log2G) - 1u);
     const unsigned mk = (unsigned)m * (unsigned)xg.ksteps + ks;
     if (!valid) return;
-    *reinterpret_cast<uint32_t*>(xb + ((mk * 16u + 2u * j + (unsigned)(gq >> 2)) * 32u + g) * 16u + (gq & 3) * 4) = word;
+    *reinterpret_cast<uint32_t*>(xb + ((mk * 16u + 2u * j + (unsigned)(gq >> 2)) * 32u + g) * 16u + (gq & 3) * 4) =
+        q.word;
     if (gq == 0) {
-        const float dxv = fin ? d : __int_as_float(0x7fc00000);
         *reinterpret_cast<float2*>(xb + (unsigned)xg.M * (unsigned)xg.ksteps * 8192u + ((mk * 8u + j) * 32u + g) * 8u) =
-            make_float2(dxv, __int_as_float(-8 * s));
+            make_float2(q.dx, __int_as_float(-8 * q.s));
     }
 }
 
@@ -376,6 +394,267 @@ __global__ void __launch_bounds__(512) gemv_q_fast(const QGemvParams p) {
     }
 }
 
+// ---- tensor-core kernel for 3..8 rows of x -------------------------------------------
+//
+// With several rows of x, the block dots are an integer matrix product per
+// 32-value block: W [16 rows × 32] · Xᵀ [32 × 8 rows of x] on the
+// mma.sync m16n8k32 integer shape (u8 × s8 for Q4_0 nibbles, s8 × s8 for Q8_0),
+// one MMA per (16 rows, block), exact int32 per-block sums. The A fragment
+// of lane (g = lane/4, t = lane%4) is the words t of rows g and g+8, plus
+// (k + 16): a Q4_0 block's quant word t holds elements 4t..4t+3 in its low
+// nibbles and 16+4t..16+4t+3 in its high nibbles, so a0 = q & 0x0F0F0F0F and
+// a2 = (q >> 4) & 0x0F0F0F0F. The B fragment is words t and 4+t of the Q8
+// quants of x row g (rows ≥ M are zero). The result lands as rows g, g+8 ×
+// x rows 2t, 2t+1 in the lane that keeps them: each lane walks every block of
+// its two rows in order and accumulates
+//     acc = fl(acc + fl(float(isum) · fl(dw · dx)))
+// exactly as the reference's scalar kernel (q4_0_scalar.cpp:82-99,
+// q8_0_scalar.cpp:170-192, no contraction), so the outputs equal the scalar
+// reference's bit for bit. Weights stream as in the fast kernel: per-warp
+// rings of TMA stages (16 rows × 16 (Q4_0) or 8 (Q8_0) blocks each, rows
+// padded so the 8 row groups of a fragment load hit distinct banks), issued
+// before griddepcontrol.wait.
+
+// Q8 activations for the MMA path, written by quantize_x_mma_kernel: per
+// block b the B-fragment words of row m (0..7) for lane t, (word t, word 4+t)
+// side by side at ((b·8 + m)·4 + t)·8 bytes; after nb·256 bytes, the pair
+// (dx, bits of kIntToFloatMagic − 8·Σq) of (b, m) at (b·8 + m)·8.
+//
+// int → float without a conversion instruction: for |v| < 2^22 the float with
+// bits 0x4B400000 + v is 1.5·2^23 + v exactly (ulp 1 in [2^23, 2^24)), so
+// subtracting 1.5·2^23 leaves float(v) exactly. The Q4_0 bias −8·Σq rides in
+// the same integer add: float(isum) = bits(c + magic − 8Σq) − 1.5·2^23, with
+// |isum| ≤ 32·15·127 + 8·32·127 far below 2^22 (Q8_0: ≤ 32·127·127).
+constexpr int kIntToFloatMagic = 0x4B400000;
+constexpr int kMmaWarps = 16;
+// A warp item is 16 rows × 8 blocks, fetched as one box of a 2-D tensor map
+// over the weights (rows of nb·block bytes; Q4_0 as bytes, Q8_0 as 16-bit
+// elements so that the 272-byte box row fits the 256-element box limit).
+// In shared memory the box rows lie densely at 144 / 272 bytes: 36 / 68
+// words, 4 (mod 32), so the 8 row groups of a fragment load fall on
+// distinct banks.
+template <int F> __host__ __device__ constexpr int mma_kb() { return 8; }
+template <int F> __host__ __device__ constexpr int mma_rs() { return 8 * block_bytes(F); }
+
+__global__ void __launch_bounds__(kThreadsQuantX) quantize_x_mma_kernel(const float* __restrict__ x, long long ldx,
+                                                                         int M, int nb, uint8_t* xq) {
+    pdl_launch_dependents();
+    pdl_wait_primary();   // x comes from the previous kernel; xq may still be read by it
+    const int gq = threadIdx.x & 7;
+    const long long groups = (long long)nb * 8;   // (block, row) pairs, rows padded to 8
+    const long long stride = (long long)gridDim.x * (blockDim.x >> 3);
+    for (long long base = ((long long)blockIdx.x * blockDim.x + (threadIdx.x & ~31)) >> 3; base < groups;
+         base += stride) {   // warp-uniform
+        const long long grp = base + ((threadIdx.x & 31) >> 3);
+        const bool valid = grp < groups;
+        const int b = (int)(grp >> 3), m = (int)(grp & 7);
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (valid && m < M) v = load_x4(x + (size_t)m * ldx + (size_t)b * kQK + gq * 4);
+        const Q8Quad q = quantize_quad(v);
+        if (!valid) continue;
+        reinterpret_cast<uint32_t*>(xq)[((size_t)(b * 8 + m) * 4 + (gq & 3)) * 2 + (gq >> 2)] = m < M ? q.word : 0u;
+        if (gq == 0)
+            reinterpret_cast<float2*>(xq + (size_t)nb * 256)[(size_t)b * 8 + m] =
+                m < M ? make_float2(q.dx, __int_as_float(kIntToFloatMagic - 8 * q.s))
+                      : make_float2(0.0f, __int_as_float(kIntToFloatMagic));
+    }
+}
+
+template <int F>
+__device__ __forceinline__ void mma_q(const uint32_t (&a)[4], uint2 b, int (&c)[4]) {
+    if constexpr (F == kQ4_0)
+        asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                     "{%10,%10,%10,%10};"
+                     : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
+                     : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b.x), "r"(b.y), "r"(0));
+    else
+        asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                     "{%10,%10,%10,%10};"
+                     : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
+                     : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b.x), "r"(b.y), "r"(0));
+}
+
+template <int F>
+__device__ __forceinline__ void mma_issue(const CUtensorMap* wmap, int tile, int ks, uint8_t* slot, uint64_t* bar,
+                                          int lane) {
+    constexpr int RS = mma_rs<F>();
+    if (lane == 0) {
+        mbar_arrive_expect_tx(bar, 16u * RS);   // the whole box, rows past N zero-filled
+        tma_load_2d(slot, wmap, ks * (F == kQ4_0 ? RS : RS / 2), tile * 16, bar);
+    }
+}
+
+// The fragment words of one pair of blocks (2i, 2i+1) of a 16-row item for
+// lane (g, t): A of both blocks, and the rows' fp16 scales.
+template <int F>
+__device__ __forceinline__ void mma_frag_pair(const uint8_t* st, int pair, int g, int t, uint32_t (&ae)[4],
+                                              uint32_t (&ao)[4], uint32_t (&sc)[2][2]) {
+    constexpr int BB = block_bytes(F), RS = mma_rs<F>();
+#pragma unroll
+    for (int rr = 0; rr < 2; ++rr) {
+        const uint32_t* w = reinterpret_cast<const uint32_t*>(st + (g + 8 * rr) * RS + pair * 2 * BB);
+        if constexpr (F == kQ4_0) {
+            // even block: scale in bytes 0-1, quant word t at byte 2 + 4t; odd block:
+            // scale in bytes 18-19 (high half of word 4), quant word t is word 5 + t.
+            const uint32_t qe = funnel(w[t], w[t + 1], 16), qo = w[5 + t];
+            ae[rr] = qe & 0x0F0F0F0Fu;
+            ae[2 + rr] = (qe >> 4) & 0x0F0F0F0Fu;
+            ao[rr] = qo & 0x0F0F0F0Fu;
+            ao[2 + rr] = (qo >> 4) & 0x0F0F0F0Fu;
+            sc[0][rr] = w[0] & 0xffffu;
+            sc[1][rr] = w[4] >> 16;
+        } else {
+            // even block: quant word u at byte 2 + 4u; odd block (byte 34 on): scale in
+            // the high half of word 8, quant word u is word 9 + u.
+            ae[rr] = funnel(w[t], w[t + 1], 16);
+            ae[2 + rr] = funnel(w[4 + t], w[5 + t], 16);
+            ao[rr] = w[9 + t];
+            ao[2 + rr] = w[13 + t];
+            sc[0][rr] = w[0] & 0xffffu;
+            sc[1][rr] = w[8] >> 16;
+        }
+    }
+}
+
+// acc[rr] += isum · (dw · dx) for rows g + 8·rr and x rows (2t, 2t+1), in the
+// reference's order and roundings: __fmul_rn / __fadd_rn, never contracted.
+// float(isum) comes exactly from the magic-number add (see kIntToFloatMagic).
+template <int F>
+__device__ __forceinline__ void mma_accumulate(const int (&c)[4], const uint32_t (&sc)[2], float4 db,
+                                               float2 (&acc)[2]) {
+    const int m0 = F == kQ4_0 ? __float_as_int(db.y) : kIntToFloatMagic;
+    const int m1 = F == kQ4_0 ? __float_as_int(db.w) : kIntToFloatMagic;
+#pragma unroll
+    for (int rr = 0; rr < 2; ++rr) {
+        const float dw = half_bits_to_float(sc[rr]);
+        const float i0 = __fadd_rn(__int_as_float(c[2 * rr] + m0), -12582912.0f);
+        const float i1 = __fadd_rn(__int_as_float(c[2 * rr + 1] + m1), -12582912.0f);
+        acc[rr].x = __fadd_rn(acc[rr].x, __fmul_rn(i0, __fmul_rn(dw, db.x)));
+        acc[rr].y = __fadd_rn(acc[rr].y, __fmul_rn(i1, __fmul_rn(dw, db.z)));
+    }
+}
+
+// Shared-memory layout of gemv_q_mma: barriers (one per stage per warp, then
+// one for x), the MMA-layout x when kXS, then the per-warp rings.
+__host__ __device__ inline size_t mma_x_offset(int warps, int stages) {
+    return ((size_t)(warps * stages + 1) * 8 + 127) & ~(size_t)127;
+}
+__host__ __device__ inline size_t mma_ring_offset(int warps, int stages, int nb, bool xs) {
+    return mma_x_offset(warps, stages) + (xs ? (((size_t)nb * 320 + 127) & ~(size_t)127) : 0);
+}
+
+template <bool kXS, typename T>
+__device__ __forceinline__ T ld_xfrag(const T* p) {
+    if constexpr (kXS) return *p;
+    else return __ldg(p);
+}
+
+// kXS: the quantized x (xmma_bytes(nb)) is copied into shared memory once per
+// CTA by one bulk copy; otherwise its fragments are read from global memory.
+template <int F, bool kXS>
+__global__ void __launch_bounds__(kMmaWarps * 32) gemv_q_mma(const QGemvParams p, const __grid_constant__ CUtensorMap wmap) {
+    constexpr int KB = mma_kb<F>(), RS = mma_rs<F>(), ITEM = 16 * RS;
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem) + warp * p.stages;
+    uint64_t* xbar = reinterpret_cast<uint64_t*>(smem) + nwarps * p.stages;
+    uint8_t* xsm = smem + mma_x_offset(nwarps, p.stages);
+    uint8_t* ring = smem + mma_ring_offset(nwarps, p.stages, p.nb, kXS) + (size_t)warp * p.stages * ITEM;
+
+    pdl_launch_dependents();
+    const int ntiles = (p.N + 15) / 16, ksteps = (p.nb + KB - 1) / KB;
+    const int GW = gridDim.x * nwarps;
+    const int gw = warp * gridDim.x + blockIdx.x;
+    const int my_tiles = gw < ntiles ? (ntiles - 1 - gw) / GW + 1 : 0;
+    const int nitems = my_tiles * ksteps;
+    if (lane == 0) {
+        for (int i = 0; i < p.stages; ++i) mbar_init(&bars[i], 1);
+        if (kXS && threadIdx.x == 0) mbar_init(xbar, 1);
+        fence_mbar_init();
+    }
+    if (kXS) __syncthreads();   // xbar initialised before any thread waits on it
+    else __syncwarp();
+    int c_tile = gw, c_ks = 0, c_slot = 0, i_tile = gw, i_ks = 0, i_slot = 0;
+    uint32_t c_phase = 0;
+    int issued = 0;
+    for (; issued < min(p.stages, nitems); ++issued) {
+        mma_issue<F>(&wmap, i_tile, i_ks, ring + (size_t)i_slot * ITEM, &bars[i_slot], lane);
+        if (++i_ks == ksteps) { i_ks = 0; i_tile += GW; }
+        if (++i_slot == p.stages) i_slot = 0;
+    }
+
+    pdl_wait_primary();   // x was quantized by the previous kernel
+    const uint8_t* xbase = p.xq;
+    if constexpr (kXS) {
+        if (threadIdx.x == 0) {
+            const uint32_t bytes = (uint32_t)p.nb * 320u;
+            mbar_arrive_expect_tx(xbar, bytes);
+            tma_load_1d(xsm, p.xq, bytes, xbar);
+        }
+        if (!mbar_wait_bounded(xbar, 0u, p.err)) {
+            for (int k = 0; k < issued; ++k) mbar_wait_bounded(&bars[k], 0u, nullptr);
+            return;
+        }
+        xbase = xsm;
+    }
+    const uint2* xf = reinterpret_cast<const uint2*>(xbase);
+    const float4* xd = reinterpret_cast<const float4*>(xbase + (size_t)p.nb * 256);
+    float2 acc[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
+
+    for (int it = 0; it < nitems; ++it) {
+        if (!mbar_wait_bounded(&bars[c_slot], c_phase, p.err)) {
+            for (int k = it + 1; k < issued; ++k) {   // let the copies in flight land, then stop
+                const int s2 = (c_slot + (k - it)) % p.stages;
+                const uint32_t ph = c_phase ^ (uint32_t)(((c_slot + (k - it)) / p.stages) & 1);
+                mbar_wait_bounded(&bars[s2], ph, nullptr);
+            }
+            return;
+        }
+        const uint8_t* st = ring + (size_t)c_slot * ITEM;
+        const int b0 = c_ks * KB;   // every item holds KB = 8 whole blocks (K % 256 == 0)
+        // All MMAs of the item first, then the scaling in block order.
+        int c[KB][4];
+        uint32_t sc[KB][2];
+#pragma unroll
+        for (int pr = 0; pr < KB / 2; ++pr) {
+            const int b = b0 + 2 * pr;
+            const uint2 xe = ld_xfrag<kXS>(xf + ((size_t)b * 8 + g) * 4 + t);
+            const uint2 xo = ld_xfrag<kXS>(xf + ((size_t)(b + 1) * 8 + g) * 4 + t);
+            uint32_t ae[4], ao[4], s2[2][2];
+            mma_frag_pair<F>(st, pr, g, t, ae, ao, s2);
+            mma_q<F>(ae, xe, c[2 * pr]);
+            mma_q<F>(ao, xo, c[2 * pr + 1]);
+            sc[2 * pr][0] = s2[0][0];
+            sc[2 * pr][1] = s2[0][1];
+            sc[2 * pr + 1][0] = s2[1][0];
+            sc[2 * pr + 1][1] = s2[1][1];
+        }
+#pragma unroll
+        for (int j = 0; j < KB; ++j)
+            mma_accumulate<F>(c[j], sc[j], ld_xfrag<kXS>(xd + (size_t)(b0 + j) * 4 + t), acc);
+        if (c_ks == ksteps - 1) {
+#pragma unroll
+            for (int rr = 0; rr < 2; ++rr) {
+                const int row = c_tile * 16 + g + 8 * rr;
+                if (row < p.N && 2 * t < p.M) p.y[(size_t)(2 * t) * p.ldy + row] = acc[rr].x;
+                if (row < p.N && 2 * t + 1 < p.M) p.y[(size_t)(2 * t + 1) * p.ldy + row] = acc[rr].y;
+                acc[rr] = make_float2(0.0f, 0.0f);
+            }
+        }
+        __syncwarp();
+        if (issued < nitems) {
+            fence_proxy_async_smem();
+            mma_issue<F>(&wmap, i_tile, i_ks, ring + (size_t)i_slot * ITEM, &bars[i_slot], lane);
+            if (++i_ks == ksteps) { i_ks = 0; i_tile += GW; }
+            if (++i_slot == p.stages) i_slot = 0;
+            ++issued;
+        }
+        if (++c_ks == ksteps) { c_ks = 0; c_tile += GW; }
+        if (++c_slot == p.stages) { c_slot = 0; c_phase ^= 1u; }
+    }
+}
+
 // ---- the generic kernel --------------------------------------------------------------
 
 // Any K % 32 == 0 and any weight alignment. One warp per row, lanes over
@@ -635,6 +914,71 @@ cudaError_t launch_gemv_q(const LaunchCfg& c, int fmt, QGemvParams p, bool fast,
     if (fast) smem = gemv_q_smem(fmt, p.M, p.ksteps, c.warps, p.stages, p.xq == nullptr);
     if (smem_used) *smem_used = smem;
     return fmt == kQ4_0 ? dispatch_m<kQ4_0>(c, p, fast, smem, dump) : dispatch_m<kQ8_0>(c, p, fast, smem, dump);
+}
+
+size_t xmma_bytes(int nb) { return (size_t)nb * 320; }
+
+cudaError_t launch_quantize_x_mma(const LaunchCfg& c, const QGemvParams& p, uint8_t* xq) {
+    const long long groups = (long long)p.nb * 8;
+    const long long grid = std::min<long long>((groups + kThreadsQuantX / 8 - 1) / (kThreadsQuantX / 8),
+                                               (long long)c.num_sms * 4);
+    return launch(quantize_x_mma_kernel, dim3((unsigned)std::max<long long>(grid, 1)), dim3(kThreadsQuantX), 0, c,
+                  p.x, p.ldx, p.M, p.nb, xq);
+}
+
+size_t gemv_q_mma_smem(int fmt, int stages, int nb, bool x_in_smem) {
+    const int rs = fmt == kQ4_0 ? mma_rs<kQ4_0>() : mma_rs<kQ8_0>();
+    return mma_ring_offset(kMmaWarps, stages, nb, x_in_smem) + (size_t)kMmaWarps * stages * 16 * rs;
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link
+// against the driver library); null when the driver does not offer it.
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return (PFN_cuTensorMapEncodeTiled_v12000) nullptr;
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    }();
+    return fn;
+}
+
+// The weights as a 2-D tensor: N rows of nb·block bytes (16-byte multiple,
+// since nb % 8 == 0), boxes of 16 rows × 8 blocks.
+cudaError_t encode_weight_map(int fmt, const QGemvParams& p, CUtensorMap* map) {
+    PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+    if (!enc) return cudaErrorNotSupported;
+    const bool q4 = fmt == kQ4_0;
+    const cuuint64_t row_bytes = (cuuint64_t)p.nb * block_bytes(fmt);
+    const cuuint64_t dims[2] = {q4 ? row_bytes : row_bytes / 2, (cuuint64_t)p.N};
+    const cuuint64_t strides[1] = {row_bytes};
+    const cuuint32_t box[2] = {q4 ? (cuuint32_t)mma_rs<kQ4_0>() : (cuuint32_t)mma_rs<kQ8_0>() / 2, 16u};
+    const cuuint32_t estr[2] = {1u, 1u};
+    const CUresult r = enc(map, q4 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT16, 2,
+                           const_cast<uint8_t*>(p.w), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+cudaError_t launch_gemv_q_mma(const LaunchCfg& c, int fmt, const QGemvParams& p, bool x_in_smem) {
+    CUtensorMap wmap;
+    cudaError_t me = encode_weight_map(fmt, p, &wmap);
+    if (me != cudaSuccess) return me;
+    void (*k)(QGemvParams, CUtensorMap);
+    if (fmt == kQ4_0) k = x_in_smem ? gemv_q_mma<kQ4_0, true> : gemv_q_mma<kQ4_0, false>;
+    else k = x_in_smem ? gemv_q_mma<kQ8_0, true> : gemv_q_mma<kQ8_0, false>;
+    const size_t smem = gemv_q_mma_smem(fmt, p.stages, p.nb, x_in_smem);
+    int per_sm = 0;
+    cudaError_t e = occupancy_cached((const void*)k, kMmaWarps * 32, smem, &per_sm);
+    if (e != cudaSuccess) return e;
+    if (per_sm < 1) return cudaErrorInvalidConfiguration;
+    const long long ntiles = ((long long)p.N + 15) / 16;
+    const long long want = std::max<long long>((ntiles + kMmaWarps - 1) / kMmaWarps, std::min<long long>(ntiles, c.num_sms));
+    const long long grid = std::min<long long>(want, (long long)std::min(per_sm, std::max(c.ctas_per_sm, 1)) * c.num_sms);
+    return launch(k, dim3((unsigned)std::max<long long>(grid, 1)), dim3(kMmaWarps * 32), smem, c, p, wmap);
 }
 
 cudaError_t launch_quantize_w(cudaStream_t s, int fmt, const float* W, long long rows, int K, uint8_t* out,

@@ -84,6 +84,16 @@ cudaError_t launch_gemv_q(const LaunchCfg& c, int fmt, QGemvParams p, bool fast,
 // Size of the fast kernel's dynamic shared memory for this launch.
 size_t gemv_q_smem(int fmt, int M, int ksteps, int warps, int stages, bool x_in_smem);
 
+// Tensor-core path for kMmaMinRows..8 rows of x (fast-kernel conditions):
+// x quantized by launch_quantize_x_mma into xmma_bytes(nb) bytes at p.xq,
+// then launch_gemv_q_mma with p.stages stages per warp.
+constexpr int kMmaMinRows = 3;
+size_t xmma_bytes(int nb);
+size_t gemv_q_mma_smem(int fmt, int stages, int nb, bool x_in_smem);
+cudaError_t launch_quantize_x_mma(const LaunchCfg& c, const QGemvParams& p, uint8_t* xq);
+// x_in_smem: each CTA copies the quantized x into shared memory first.
+cudaError_t launch_gemv_q_mma(const LaunchCfg& c, int fmt, const QGemvParams& p, bool x_in_smem);
+
 // Weight quantizers (ggml quantize_row_q4_0_ref / q8_0_ref, bit-exact).
 // *reject gets 1 when a value is NaN/Inf or a scale overflows binary16.
 cudaError_t launch_quantize_w(cudaStream_t s, int fmt, const float* W, long long rows, int K, uint8_t* out,

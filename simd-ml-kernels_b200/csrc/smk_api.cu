@@ -242,6 +242,38 @@ smk_status run_q(smk_ctx* c, smk_qformat fmt, int M, int N, int K, const float* 
         return SMK_OK;
     }
     smk::LaunchCfg l = cfg_for(c, s);
+    if (M >= smk::kMmaMinRows && !dump && K % 256 == 0 && (reinterpret_cast<uintptr_t>(Wq) & 15) == 0) {
+        // Several rows of x: integer tensor-core kernel (bitwise the reference's
+        // scalar order), x quantized once into scratch by its own kernel.
+        smk::QGemvParams p = {};
+        p.x = x; p.ldx = ldx; p.w = Wq; p.y = y; p.ldy = ldy;
+        p.M = M; p.N = N; p.K = K; p.nb = K / 32;
+        p.err = c->d_err;
+        // x in shared memory when it fits beside at least 2 stages (K up to ~9K).
+        bool xs = false;
+        for (int st = c->stages > 0 ? c->stages : 4; st >= 2 && !xs; --st)
+            if (smk::gemv_q_mma_smem((int)fmt, st, p.nb, true) <= c->smem_optin) {
+                xs = true;
+                p.stages = st;
+            }
+        if (!xs) {
+            p.stages = c->stages > 0 ? c->stages : 4;
+            while (p.stages > 1 && smk::gemv_q_mma_smem((int)fmt, p.stages, p.nb, false) > c->smem_optin) --p.stages;
+        }
+        l.warps = 16;
+        l.ctas_per_sm = c->ctas_per_sm > 0 ? c->ctas_per_sm : 1;
+        uint8_t* xq;
+        {
+            std::lock_guard<std::mutex> g(c->mu_scratch);
+            DevBuf& b = c->scratch[s];
+            SMK_CUDA(b.reserve(smk::xmma_bytes(p.nb)), "cudaMalloc (scratch)");
+            xq = static_cast<uint8_t*>(b.ptr);
+        }
+        SMK_CUDA(smk::launch_quantize_x_mma(l, p, xq), "quantize_x launch");
+        p.xq = xq;
+        SMK_CUDA(smk::launch_gemv_q_mma(l, (int)fmt, p, xs), "gemv launch");
+        return SMK_OK;
+    }
     QPlan q = plan_q(c, &l, fmt, M, N, K, x, ldx, Wq, y, ldy, dump != nullptr);
     q.p.dump = dump;
     if (x_read_once && q.x_in_smem && !dump) {

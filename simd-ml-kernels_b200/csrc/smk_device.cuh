@@ -6,6 +6,7 @@
 #pragma once
 
 #include <cstdint>
+#include <cuda.h>
 #include <cuda_fp16.h>
 
 namespace smk {
@@ -90,6 +91,19 @@ __device__ __forceinline__ void tma_load_1d(void* dst, const void* src, uint32_t
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
             smem_addr(dst)),
         "l"(src), "r"(bytes), "r"(smem_addr(bar))
+        : "memory");
+}
+
+// 2-D tiled bulk copy of one box of the tensor described by *map (a kernel
+// parameter) at element coordinates (x, y) into this CTA's shared memory,
+// completion counted on *bar in bytes (the whole box, out-of-range rows
+// zero-filled). dst 128-byte aligned; x·element size a multiple of 16.
+// Never multicast.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
         : "memory");
 }
 

@@ -222,6 +222,27 @@ def test_gemv_batch_nan_row_only(sk):
 
 
 @pytest.mark.parametrize("fmt", ["q4_0", "q8_0"])
+@pytest.mark.parametrize("M,N,K", [(3, 1000, 2048), (8, 4099, 256), (5, 17, 8192), (8, 16, 512), (4, 2048, 28672),
+                                   (6, 31, 768)])
+def test_mma_rows_bitwise_equal_reference_scalar(sk, torch, fmt, M, N, K):
+    """3..8 rows of x take the integer tensor-core kernel, which accumulates
+    each row's blocks in order with the reference scalar kernel's roundings:
+    every output equals the reference's scalar GEMV (the oracle, pinned to
+    it bitwise) bit for bit; a non-finite value makes only its row NaN."""
+    rng = np.random.default_rng(M * 100003 + N + K)
+    W = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    X = (rng.standard_normal((M, K)) * 3).astype(np.float32)
+    X[M - 1, K // 3] = np.nan
+    Wq = O.quantize(fmt, W)
+    batch = sk.gemv_q4_0_batch if fmt == "q4_0" else sk.gemv_q8_0_batch
+    Y = batch(torch.from_numpy(X).cuda(), torch.from_numpy(Wq.ravel()).cuda(), N, K).cpu().numpy()
+    for m in range(M - 1):
+        want = O.gemv_scalar(fmt, X[m], Wq, N, K)
+        np.testing.assert_array_equal(Y[m].view(np.uint32), want.view(np.uint32), err_msg=f"row {m}")
+    assert np.isnan(Y[M - 1]).all()
+
+
+@pytest.mark.parametrize("fmt", ["q4_0", "q8_0"])
 def test_gemv_k0_and_n0(sk, fmt):
     fn = sk.gemv_q4_0 if fmt == "q4_0" else sk.gemv_q8_0
     assert (fn(np.ones(0, np.float32), np.zeros(0, np.uint8), 5, 0) == 0).all()
