@@ -317,7 +317,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1) gemv_dense_tma(const DenseParam
         for (int m = 0; m < M; ++m) acc[r][m] = make_float2(0.0f, 0.0f);
 
     for (int it = 0; it < nitems; ++it) {
-        if (!mbar_wait_bounded(&bars[c_slot], c_phase, p.err)) {
+        if (__any_sync(0xffffffffu, !mbar_wait_bounded(&bars[c_slot], c_phase, p.err))) {   // warp-uniform
             for (int k = it + 1; k < issued; ++k) {   // let the copies in flight land, then stop
                 const int s2 = (c_slot + (k - it)) % g.stages;
                 const uint32_t ph = c_phase ^ (uint32_t)(((c_slot + (k - it)) / g.stages) & 1);

@@ -353,7 +353,7 @@ __global__ void __launch_bounds__(512) gemv_q_fast(const QGemvParams p) {
     for (int m = 0; m < M; ++m) acc[m] = 0.0f;
 
     for (int it = 0; it < nitems; ++it) {
-        if (!mbar_wait_bounded(&bars[cur.slot], cur.phase, p.err)) {
+        if (__any_sync(0xffffffffu, !mbar_wait_bounded(&bars[cur.slot], cur.phase, p.err))) {   // warp-uniform
             // Give the copies still in flight a bounded chance to land before
             // the CTA's shared memory is released, then stop.
             ItemCursor c2 = cur;
@@ -535,12 +535,16 @@ __device__ __forceinline__ void mma_accumulate(const int (&c)[4], const uint32_t
 }
 
 // Shared-memory layout of gemv_q_mma: barriers (one per stage per warp, then
-// one for x), the MMA-layout x when kXS, then the per-warp rings.
+// one for x), the MMA-layout x when kXS, the partial sums of split tiles
+// (a float4 per lane per warp), then the per-warp rings.
 __host__ __device__ inline size_t mma_x_offset(int warps, int stages) {
     return ((size_t)(warps * stages + 1) * 8 + 127) & ~(size_t)127;
 }
-__host__ __device__ inline size_t mma_ring_offset(int warps, int stages, int nb, bool xs) {
+__host__ __device__ inline size_t mma_part_offset(int warps, int stages, int nb, bool xs) {
     return mma_x_offset(warps, stages) + (xs ? (((size_t)nb * 320 + 127) & ~(size_t)127) : 0);
+}
+__host__ __device__ inline size_t mma_ring_offset(int warps, int stages, int nb, bool xs) {
+    return mma_part_offset(warps, stages, nb, xs) + (size_t)warps * 32 * 16;
 }
 
 template <bool kXS, typename T>
@@ -551,6 +555,14 @@ __device__ __forceinline__ T ld_xfrag(const T* p) {
 
 // kXS: the quantized x (xmma_bytes(nb)) is copied into shared memory once per
 // CTA by one bulk copy; otherwise its fragments are read from global memory.
+//
+// Work split: a CTA takes groups of T = warps / S consecutive 16-row tiles;
+// warp w works on tile w / S of the group over the K part w % S (p.split = S
+// parts of the k-steps). With S = 1 every row's blocks are summed by one lane
+// in block order (the reference's order); with S > 1 each part's sum is kept
+// in shared memory and part 0 adds the S partial sums in order, so the result
+// is deterministic but rounded differently. The launcher splits K only when
+// the tiles alone cannot fill the GPU.
 template <int F, bool kXS>
 __global__ void __launch_bounds__(kMmaWarps * 32) gemv_q_mma(const QGemvParams p, const __grid_constant__ CUtensorMap wmap) {
     constexpr int KB = mma_kb<F>(), RS = mma_rs<F>(), ITEM = 16 * RS;
@@ -560,98 +572,134 @@ __global__ void __launch_bounds__(kMmaWarps * 32) gemv_q_mma(const QGemvParams p
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem) + warp * p.stages;
     uint64_t* xbar = reinterpret_cast<uint64_t*>(smem) + nwarps * p.stages;
     uint8_t* xsm = smem + mma_x_offset(nwarps, p.stages);
+    float4* parts = reinterpret_cast<float4*>(smem + mma_part_offset(nwarps, p.stages, p.nb, kXS));
     uint8_t* ring = smem + mma_ring_offset(nwarps, p.stages, p.nb, kXS) + (size_t)warp * p.stages * ITEM;
 
     pdl_launch_dependents();
-    const int ntiles = (p.N + 15) / 16, ksteps = (p.nb + KB - 1) / KB;
-    const int GW = gridDim.x * nwarps;
-    const int gw = warp * gridDim.x + blockIdx.x;
-    const int my_tiles = gw < ntiles ? (ntiles - 1 - gw) / GW + 1 : 0;
-    const int nitems = my_tiles * ksteps;
+    const int ntiles = (p.N + 15) / 16, ksteps = p.nb / KB;   // K % 256 == 0: whole items
+    const int S = p.split, T = nwarps / S, part = warp % S, tl = warp / S;
+    const int ks_lo = part * ksteps / S, nks = (part + 1) * ksteps / S - ks_lo;
+    const int ngroups = (ntiles + T - 1) / T;
+    const int my_groups = (int)blockIdx.x < ngroups ? (ngroups - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+    // Only the last group can hold a tile past N.
+    const int last_tile = my_groups > 0 ? ((int)blockIdx.x + (my_groups - 1) * (int)gridDim.x) * T + tl : 0;
+    const int valid_groups = my_groups > 0 && last_tile >= ntiles ? my_groups - 1 : my_groups;
+    const int nitems = valid_groups * nks;
     if (lane == 0) {
         for (int i = 0; i < p.stages; ++i) mbar_init(&bars[i], 1);
         if (kXS && threadIdx.x == 0) mbar_init(xbar, 1);
         fence_mbar_init();
     }
-    if (kXS) __syncthreads();   // xbar initialised before any thread waits on it
-    else __syncwarp();
-    int c_tile = gw, c_ks = 0, c_slot = 0, i_tile = gw, i_ks = 0, i_slot = 0;
-    uint32_t c_phase = 0;
-    int issued = 0;
-    for (; issued < min(p.stages, nitems); ++issued) {
-        mma_issue<F>(&wmap, i_tile, i_ks, ring + (size_t)i_slot * ITEM, &bars[i_slot], lane);
-        if (++i_ks == ksteps) { i_ks = 0; i_tile += GW; }
+    __syncthreads();
+    // Issue cursor over (group round, k-step); items are consumed in the same order.
+    int i_r = 0, i_ks = 0, i_slot = 0, issued = 0;
+    auto issue_next = [&]() {
+        const int tile = ((int)blockIdx.x + i_r * (int)gridDim.x) * T + tl;
+        mma_issue<F>(&wmap, tile, ks_lo + i_ks, ring + (size_t)i_slot * ITEM, &bars[i_slot], lane);
+        if (++i_ks == nks) { i_ks = 0; ++i_r; }
         if (++i_slot == p.stages) i_slot = 0;
-    }
+        ++issued;
+    };
+    while (issued < min(p.stages, nitems)) issue_next();
 
     pdl_wait_primary();   // x was quantized by the previous kernel
     const uint8_t* xbase = p.xq;
+    int failed = 0;
     if constexpr (kXS) {
         if (threadIdx.x == 0) {
             const uint32_t bytes = (uint32_t)p.nb * 320u;
             mbar_arrive_expect_tx(xbar, bytes);
             tma_load_1d(xsm, p.xq, bytes, xbar);
         }
-        if (!mbar_wait_bounded(xbar, 0u, p.err)) {
-            for (int k = 0; k < issued; ++k) mbar_wait_bounded(&bars[k], 0u, nullptr);
-            return;
-        }
+        failed = !mbar_wait_bounded(xbar, 0u, p.err);
         xbase = xsm;
     }
+    failed = __syncthreads_or(failed);
     const uint2* xf = reinterpret_cast<const uint2*>(xbase);
     const float4* xd = reinterpret_cast<const float4*>(xbase + (size_t)p.nb * 256);
-    float2 acc[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
 
-    for (int it = 0; it < nitems; ++it) {
-        if (!mbar_wait_bounded(&bars[c_slot], c_phase, p.err)) {
-            for (int k = it + 1; k < issued; ++k) {   // let the copies in flight land, then stop
-                const int s2 = (c_slot + (k - it)) % p.stages;
-                const uint32_t ph = c_phase ^ (uint32_t)(((c_slot + (k - it)) / p.stages) & 1);
-                mbar_wait_bounded(&bars[s2], ph, nullptr);
+    int c_slot = 0, consumed = 0;
+    uint32_t c_phase = 0;
+    for (int r = 0; r < my_groups; ++r) {   // CTA-uniform: every warp meets every barrier
+        const int tile = ((int)blockIdx.x + r * (int)gridDim.x) * T + tl;
+        float2 acc[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
+        if (r < valid_groups) {
+            for (int k = 0; k < nks && !failed; ++k) {
+                // Warp-uniform verdict: every lane leaves together or none does.
+                if (__any_sync(0xffffffffu, !mbar_wait_bounded(&bars[c_slot], c_phase, p.err))) {
+                    failed = 1;
+                    break;
+                }
+                const uint8_t* st = ring + (size_t)c_slot * ITEM;
+                const int b0 = (ks_lo + k) * KB;
+                // All MMAs of the item first, then the scaling in block order.
+                int c[KB][4];
+                uint32_t sc[KB][2];
+#pragma unroll
+                for (int pr = 0; pr < KB / 2; ++pr) {
+                    const int b = b0 + 2 * pr;
+                    const uint2 xe = ld_xfrag<kXS>(xf + ((size_t)b * 8 + g) * 4 + t);
+                    const uint2 xo = ld_xfrag<kXS>(xf + ((size_t)(b + 1) * 8 + g) * 4 + t);
+                    uint32_t ae[4], ao[4], s2[2][2];
+                    mma_frag_pair<F>(st, pr, g, t, ae, ao, s2);
+                    mma_q<F>(ae, xe, c[2 * pr]);
+                    mma_q<F>(ao, xo, c[2 * pr + 1]);
+                    sc[2 * pr][0] = s2[0][0];
+                    sc[2 * pr][1] = s2[0][1];
+                    sc[2 * pr + 1][0] = s2[1][0];
+                    sc[2 * pr + 1][1] = s2[1][1];
+                }
+#pragma unroll
+                for (int j = 0; j < KB; ++j)
+                    mma_accumulate<F>(c[j], sc[j], ld_xfrag<kXS>(xd + (size_t)(b0 + j) * 4 + t), acc);
+                __syncwarp();
+                if (issued < nitems) {
+                    fence_proxy_async_smem();
+                    issue_next();
+                }
+                ++consumed;
+                if (++c_slot == p.stages) { c_slot = 0; c_phase ^= 1u; }
             }
-            return;
         }
-        const uint8_t* st = ring + (size_t)c_slot * ITEM;
-        const int b0 = c_ks * KB;   // every item holds KB = 8 whole blocks (K % 256 == 0)
-        // All MMAs of the item first, then the scaling in block order.
-        int c[KB][4];
-        uint32_t sc[KB][2];
+        if (S == 1) {
+            if (r < valid_groups && !failed) {
 #pragma unroll
-        for (int pr = 0; pr < KB / 2; ++pr) {
-            const int b = b0 + 2 * pr;
-            const uint2 xe = ld_xfrag<kXS>(xf + ((size_t)b * 8 + g) * 4 + t);
-            const uint2 xo = ld_xfrag<kXS>(xf + ((size_t)(b + 1) * 8 + g) * 4 + t);
-            uint32_t ae[4], ao[4], s2[2][2];
-            mma_frag_pair<F>(st, pr, g, t, ae, ao, s2);
-            mma_q<F>(ae, xe, c[2 * pr]);
-            mma_q<F>(ao, xo, c[2 * pr + 1]);
-            sc[2 * pr][0] = s2[0][0];
-            sc[2 * pr][1] = s2[0][1];
-            sc[2 * pr + 1][0] = s2[1][0];
-            sc[2 * pr + 1][1] = s2[1][1];
-        }
-#pragma unroll
-        for (int j = 0; j < KB; ++j)
-            mma_accumulate<F>(c[j], sc[j], ld_xfrag<kXS>(xd + (size_t)(b0 + j) * 4 + t), acc);
-        if (c_ks == ksteps - 1) {
-#pragma unroll
-            for (int rr = 0; rr < 2; ++rr) {
-                const int row = c_tile * 16 + g + 8 * rr;
-                if (row < p.N && 2 * t < p.M) p.y[(size_t)(2 * t) * p.ldy + row] = acc[rr].x;
-                if (row < p.N && 2 * t + 1 < p.M) p.y[(size_t)(2 * t + 1) * p.ldy + row] = acc[rr].y;
-                acc[rr] = make_float2(0.0f, 0.0f);
+                for (int rr = 0; rr < 2; ++rr) {
+                    const int row = tile * 16 + g + 8 * rr;
+                    if (row < p.N && 2 * t < p.M) p.y[(size_t)(2 * t) * p.ldy + row] = acc[rr].x;
+                    if (row < p.N && 2 * t + 1 < p.M) p.y[(size_t)(2 * t + 1) * p.ldy + row] = acc[rr].y;
+                }
             }
+        } else {
+            parts[warp * 32 + lane] = make_float4(acc[0].x, acc[0].y, acc[1].x, acc[1].y);
+            __syncthreads();
+            if (part == 0 && r < valid_groups && !failed) {
+                float4 sum = parts[warp * 32 + lane];
+                for (int q = 1; q < S; ++q) {   // the parts of the tile in K order
+                    const float4 v = parts[(warp + q) * 32 + lane];
+                    sum.x = __fadd_rn(sum.x, v.x);
+                    sum.y = __fadd_rn(sum.y, v.y);
+                    sum.z = __fadd_rn(sum.z, v.z);
+                    sum.w = __fadd_rn(sum.w, v.w);
+                }
+                const float vals[4] = {sum.x, sum.y, sum.z, sum.w};
+#pragma unroll
+                for (int rr = 0; rr < 2; ++rr) {
+                    const int row = tile * 16 + g + 8 * rr;
+#pragma unroll
+                    for (int j = 0; j < 2; ++j)
+                        if (row < p.N && 2 * t + j < p.M) p.y[(size_t)(2 * t + j) * p.ldy + row] = vals[2 * rr + j];
+                }
+            }
+            __syncthreads();
         }
-        __syncwarp();
-        if (issued < nitems) {
-            fence_proxy_async_smem();
-            mma_issue<F>(&wmap, i_tile, i_ks, ring + (size_t)i_slot * ITEM, &bars[i_slot], lane);
-            if (++i_ks == ksteps) { i_ks = 0; i_tile += GW; }
-            if (++i_slot == p.stages) i_slot = 0;
-            ++issued;
+    }
+    if (failed) {
+        // Let this warp's copies still in flight land (bounded) before the CTA exits.
+        for (int k = consumed; k < issued; ++k) {
+            const int s2 = k % p.stages;
+            mbar_wait_bounded(&bars[s2], (uint32_t)((k / p.stages) & 1), nullptr);
         }
-        if (++c_ks == ksteps) { c_ks = 0; c_tile += GW; }
-        if (++c_slot == p.stages) { c_slot = 0; c_phase ^= 1u; }
     }
 }
 
@@ -975,10 +1023,17 @@ cudaError_t launch_gemv_q_mma(const LaunchCfg& c, int fmt, const QGemvParams& p,
     cudaError_t e = occupancy_cached((const void*)k, kMmaWarps * 32, smem, &per_sm);
     if (e != cudaSuccess) return e;
     if (per_sm < 1) return cudaErrorInvalidConfiguration;
-    const long long ntiles = ((long long)p.N + 15) / 16;
-    const long long want = std::max<long long>((ntiles + kMmaWarps - 1) / kMmaWarps, std::min<long long>(ntiles, c.num_sms));
-    const long long grid = std::min<long long>(want, (long long)std::min(per_sm, std::max(c.ctas_per_sm, 1)) * c.num_sms);
-    return launch(k, dim3((unsigned)std::max<long long>(grid, 1)), dim3(kMmaWarps * 32), smem, c, p, wmap);
+    // Split K (S parts per tile, a power of two up to the warps of a CTA and the
+    // k-steps) until the tiles' parts fill about 3/4 of the GPU's warps.
+    const long long ntiles = ((long long)p.N + 15) / 16, ksteps = p.nb / 8;
+    const long long cap = (long long)std::min(per_sm, std::max(c.ctas_per_sm, 1)) * c.num_sms;
+    QGemvParams q = p;
+    q.split = 1;
+    while (q.split < kMmaWarps && 2LL * q.split <= ksteps && ntiles * q.split * 4 < cap * kMmaWarps * 3) q.split *= 2;
+    const long long T = kMmaWarps / q.split;
+    const long long ngroups = (ntiles + T - 1) / T;
+    const long long grid = std::min(ngroups, cap);
+    return launch(k, dim3((unsigned)std::max<long long>(grid, 1)), dim3(kMmaWarps * 32), smem, c, q, wmap);
 }
 
 cudaError_t launch_quantize_w(cudaStream_t s, int fmt, const float* W, long long rows, int K, uint8_t* out,

@@ -51,6 +51,7 @@ struct QGemvParams {
     int nsbp;              // ceil(nb / 8)
     int G, log2G, TR, ksteps, ntiles;
     int stages;            // shared-memory stages per warp (fast kernel)
+    int split;             // tensor-core kernel: K parts per 16-row tile (set by its launcher)
     const uint8_t* xq;     // quantized x in global memory (nullptr: each CTA quantizes into shared memory)
     int32_t* dump;         // test-only: per-block integer sums [M, N, nb], or nullptr
     unsigned* err;         // device error word

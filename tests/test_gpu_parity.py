@@ -221,24 +221,46 @@ def test_gemv_batch_nan_row_only(sk):
     assert np.isnan(Y[1]).all() and np.isfinite(Y[0]).all() and np.isfinite(Y[2]).all()
 
 
-@pytest.mark.parametrize("fmt", ["q4_0", "q8_0"])
-@pytest.mark.parametrize("M,N,K", [(3, 1000, 2048), (8, 4099, 256), (5, 17, 8192), (8, 16, 512), (4, 2048, 28672),
-                                   (6, 31, 768)])
-def test_mma_rows_bitwise_equal_reference_scalar(sk, torch, fmt, M, N, K):
-    """3..8 rows of x take the integer tensor-core kernel, which accumulates
-    each row's blocks in order with the reference scalar kernel's roundings:
-    every output equals the reference's scalar GEMV (the oracle, pinned to
-    it bitwise) bit for bit; a non-finite value makes only its row NaN."""
+def _mma_case(fmt, M, N, K):
     rng = np.random.default_rng(M * 100003 + N + K)
     W = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
     X = (rng.standard_normal((M, K)) * 3).astype(np.float32)
     X[M - 1, K // 3] = np.nan
-    Wq = O.quantize(fmt, W)
+    return X, O.quantize(fmt, W)
+
+
+@pytest.mark.parametrize("fmt", ["q4_0", "q8_0"])
+@pytest.mark.parametrize("M,N,K", [(3, 28500, 256), (8, 30000, 512), (5, 29001, 2048)])
+def test_mma_rows_bitwise_equal_reference_scalar(sk, torch, fmt, M, N, K):
+    """3..8 rows of x take the integer tensor-core kernel. When its 16-row
+    tiles alone fill the GPU (N >= ~28.4K on 148 SMs), each row's blocks are
+    accumulated in order with the reference scalar kernel's roundings: every
+    output equals the reference's scalar GEMV (the oracle, pinned to it
+    bitwise) bit for bit; a non-finite value makes only its row NaN."""
+    X, Wq = _mma_case(fmt, M, N, K)
     batch = sk.gemv_q4_0_batch if fmt == "q4_0" else sk.gemv_q8_0_batch
     Y = batch(torch.from_numpy(X).cuda(), torch.from_numpy(Wq.ravel()).cuda(), N, K).cpu().numpy()
     for m in range(M - 1):
         want = O.gemv_scalar(fmt, X[m], Wq, N, K)
         np.testing.assert_array_equal(Y[m].view(np.uint32), want.view(np.uint32), err_msg=f"row {m}")
+    assert np.isnan(Y[M - 1]).all()
+
+
+@pytest.mark.parametrize("fmt", ["q4_0", "q8_0"])
+@pytest.mark.parametrize("M,N,K", [(3, 1000, 2048), (8, 4099, 256), (5, 17, 8192), (8, 16, 512), (4, 2048, 28672),
+                                   (6, 31, 768), (8, 8192, 28672)])
+def test_mma_rows_split_k(sk, torch, fmt, M, N, K):
+    """Fewer tiles than the GPU holds: K is split into parts whose sums are
+    added in order: within the reference's bound of the float64 sums,
+    identical from call to call, NaN rows as the reference."""
+    X, Wq = _mma_case(fmt, M, N, K)
+    batch = sk.gemv_q4_0_batch if fmt == "q4_0" else sk.gemv_q8_0_batch
+    xd, wd = torch.from_numpy(X).cuda(), torch.from_numpy(Wq.ravel()).cuda()
+    Y = batch(xd, wd, N, K).cpu().numpy()
+    np.testing.assert_array_equal(batch(xd, wd, N, K).cpu().numpy().view(np.uint32), Y.view(np.uint32))
+    for m in range(M - 1):
+        y64, mag = O.ref64(fmt, X[m], Wq, N, K)
+        assert_gemv_close(Y[m], y64, mag, K, f"{fmt} row {m}")
     assert np.isnan(Y[M - 1]).all()
 
 
