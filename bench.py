@@ -14,8 +14,10 @@ max-over-ranks device time.
 
 N > 1 (torchrun): weak scaling. Each rank holds its 8192-row slice of a
 [8192*N, 2048] matrix (the reference's row slicing, gemv_slice), and every
-step all-gathers the y slices over NVLink with NCCL, so every rank ends the
-step with all 8192*N outputs.
+step all-gathers the y slices over NVLink, so every rank ends the step with
+all 8192*N outputs: by default inside the GEMV kernel (it stores its slice
+into every rank's buffer through CUDA IPC mappings; a one-warp kernel then
+waits for the peers' signals), or with NCCL (--gather nccl).
 
 --impl reference: the reference's own CPU kernel (Mattral/simd-ml-kernels
 compiled from its sources, oracle/_ref) on the same workload with every host
@@ -215,12 +217,19 @@ def gpu_bench(args, rank: int, world: int, local_rank: int) -> dict | None:
     x = torch.randn(K_COLS, generator=g, device=dev)
     y = torch.empty(N_ROWS, device=dev)
     Ntot = N_ROWS * world
-    gathered = torch.empty((world, N_ROWS), device=dev) if world > 1 else None
+    nvlink = world > 1 and args.gather == "nvlink"
+    gathered = torch.empty((world, N_ROWS), device=dev) if world > 1 and not nvlink else None
+    sg = shard.ShardedGemv("q4_0", Wq0, Ntot, K_COLS, gather="nvlink") if nvlink else None
 
     stream = torch.cuda.Stream(device=dev)
-    launches_per_step = 1
+    launches_per_step = 2 if nvlink else 1
+    from simd_ml_kernels import _core
 
     def one_step(i):
+        if nvlink:   # GEMV storing its slice into every rank's y over NVLink, then the peers' signals
+            _core._gemv_q_gather(sg._g, 0, 1, N_ROWS, K_COLS, x.data_ptr(), K_COLS, ws[i % copies].data_ptr(),
+                                 stream.cuda_stream, local_rank)
+            return
         sk.gemv_q4_0(x, ws[i % copies], N_ROWS, K_COLS, out=y)
         if world > 1:
             dist.all_gather_into_tensor(gathered, y)
@@ -314,7 +323,8 @@ def gpu_bench(args, rank: int, world: int, local_rank: int) -> dict | None:
         assert yh.shape == (N_ROWS,)
         e2e_bytes_out = 4 * N_ROWS
     else:
-        sg = shard.ShardedGemv("q4_0", ws[0], Ntot, K_COLS)
+        if sg is None:
+            sg = shard.ShardedGemv("q4_0", ws[0], Ntot, K_COLS)
         yfull_h = torch.empty(Ntot).pin_memory()
         for _ in range(20):
             yfull_h.copy_(sg.forward(xh.to(dev, non_blocking=True)))
@@ -330,6 +340,8 @@ def gpu_bench(args, rank: int, world: int, local_rank: int) -> dict | None:
         e2e_s = float(tt.item())
         e2e_bytes_out = 4 * Ntot
     sk.set_pdl(True, local_rank)
+    if sg is not None:
+        sg.close()   # release the gather buffers before the process group goes
 
     extra = {}
     if rank == 0 and world == 1:
@@ -348,7 +360,10 @@ def gpu_bench(args, rank: int, world: int, local_rank: int) -> dict | None:
         "vs_baseline": None, "dtype": "q4_0 weights x int8 activations (dp4a int32, fp32 accumulate)",
         "data": "synthetic: W ~ N(0, 0.02) seed 0 quantized ggml Q4_0 on device, x ~ N(0, 1)",
         "config": {"workload": "config 0: Q4_0 decode GEMV M=1 K=2048 N=8192 per GPU"
-                               + (f", rows sharded over {world} GPUs + NCCL all-gather of y" if world > 1 else ""),
+                               + ((f", rows sharded over {world} GPUs, all-gather of y fused into the GEMV "
+                                   "(stores into every rank's y over NVLink, then a wait on the peers' signals)"
+                                   if nvlink else f", rows sharded over {world} GPUs + NCCL all-gather of y")
+                                  if world > 1 else ""),
                    "M": 1, "K": K_COLS, "N_per_gpu": N_ROWS, "N_total": Ntot,
                    "bytes_per_step_per_gpu": STEP_BYTES,
                    "l2_policy": f"{copies} rotated weight copies ({copies * W_BYTES / 2**20:.0f} MiB > 2x L2 "
@@ -510,6 +525,8 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--all", action="store_true", help="also time configs 1, 3 and 4 (one GPU)")
     ap.add_argument("--cpu-baseline-seconds", type=float, default=8.0)
+    ap.add_argument("--gather", choices=["nvlink", "nccl"], default="nvlink",
+                    help="N > 1: all-gather of y fused into the GEMV over NVLink, or NCCL's all-gather")
     ap.add_argument("--case", default=None,
                     help="time only the config 1/3/4 cases whose label contains this text (after the config-0 line)")
     ap.add_argument("--only-gemv", action="store_true",

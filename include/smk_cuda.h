@@ -155,6 +155,29 @@ smk_status smk_block_sums(smk_ctx* ctx, smk_qformat fmt, int M, int N, int K, co
 smk_status smk_gemv_q_noalloc(smk_qformat fmt, int M, int N, int K, const float* x, int64_t ldx, const uint8_t* Wq,
                               float* y, int64_t ldy, void* stream);
 
+/* ---- row-sharded GEMV with the all-gather of y fused in (one process per GPU) ----
+ * Replaces the row slicing of gemv_slice (src/dispatch/dispatch.cpp:373-379)
+ * across GPUs, plus an all-gather of the y slices; an addition with no
+ * reference counterpart beyond that slicing. Each rank creates one gather
+ * object (a device buffer holding two full-y areas [m_max][world * npad] and
+ * a control block), passes its 64-byte IPC handle to every peer (any host
+ * channel: torch.distributed, MPI, ...), and connects with all ranks'
+ * handles in rank order. Every rank then makes the same sequence of
+ * smk_gemv_q_gather calls on the same shapes: each computes this rank's
+ * npad-row slice (N_local <= npad valid rows), stores it into every rank's
+ * area over NVLink, and, on the same stream, waits (bounded, about 1 s;
+ * smk_device_error reports a timeout) until every peer's slice of the step
+ * has arrived. *y_full receives this step's area: [M][world * npad] floats,
+ * rank r's rows at r * npad; it stays valid until the call after next. */
+typedef struct smk_gather smk_gather;
+#define SMK_IPC_HANDLE_BYTES 64
+smk_status smk_gather_create(smk_ctx* ctx, int world, int rank, int npad, int m_max, smk_gather** out,
+                             void* ipc_handle /* SMK_IPC_HANDLE_BYTES */);
+smk_status smk_gather_connect(smk_gather* g, const void* ipc_handles /* world * SMK_IPC_HANDLE_BYTES, by rank */);
+smk_status smk_gather_destroy(smk_gather* g);
+smk_status smk_gemv_q_gather(smk_ctx* ctx, smk_gather* g, smk_qformat fmt, int M, int N_local, int K, const float* x,
+                             int64_t ldx, const uint8_t* Wq, float** y_full, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -621,6 +621,33 @@ PYBIND11_MODULE(_core, m) {
               return gemv_blocks(x, wa, N, K, q4 ? 18 : 34, q4 ? "q4_0" : "q8_0", q4 ? SMK_Q4_0 : SMK_Q8_0,
                                  py::none(), py::none(), batched);
           });
+    // Row-sharded GEMV with the all-gather of y fused in (simd_ml_kernels.shard).
+    m.def("_gather_create", [](int world, int rank, int npad, int m_max, int device) {
+        smk_ctx* c = ctx_for(device);
+        smk_gather* g = nullptr;
+        char h[SMK_IPC_HANDLE_BYTES];
+        check(smk_gather_create(c, world, rank, npad, m_max, &g, h));
+        return py::make_tuple(reinterpret_cast<uintptr_t>(g), py::bytes(h, SMK_IPC_HANDLE_BYTES));
+    });
+    m.def("_gather_connect", [](uintptr_t g, py::bytes handles) {
+        const std::string hs = handles;
+        check(smk_gather_connect(reinterpret_cast<smk_gather*>(g), hs.data()));
+    });
+    m.def("_gather_destroy", [](uintptr_t g) { check(smk_gather_destroy(reinterpret_cast<smk_gather*>(g))); });
+    m.def("_gemv_q_gather", [](uintptr_t g, int fmt, int M, int N, int K, uintptr_t x, long long ldx, uintptr_t w,
+                               uintptr_t stream, int device) {
+        smk_ctx* c = ctx_for(device);
+        float* y = nullptr;
+        smk_status st;
+        {
+            py::gil_scoped_release release;
+            st = smk_gemv_q_gather(c, reinterpret_cast<smk_gather*>(g), (smk_qformat)fmt, M, N, K,
+                                   reinterpret_cast<const float*>(x), ldx, reinterpret_cast<const uint8_t*>(w), &y,
+                                   reinterpret_cast<void*>(stream));
+        }
+        check(st);
+        return reinterpret_cast<uintptr_t>(y);
+    });
     m.def("version", []() { return std::string(smk_version()); });
     m.def("_set_device", [](int d) { current_device_hint = d; });
     m.def("_ctx_set", [](int option, long long value) { check(smk_ctx_set(ctx_for(current_device_hint), option, value)); });

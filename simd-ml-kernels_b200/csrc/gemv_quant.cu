@@ -344,6 +344,15 @@ __global__ void __launch_bounds__(512) gemv_q_fast(const QGemvParams p) {
     const uint8_t* xb = kXGlobal ? p.xq : xs;
 
     const int r = lane >> p.log2G, g = lane & (p.G - 1);
+    // Fused all-gather: this step's y goes into full-y area (epoch & 1) of
+    // every rank, at this rank's slice. The previous kernel (the gather wait)
+    // completed before griddepcontrol.wait returned, so the epoch is settled.
+    long long gather_off = 0;
+    if (p.gather) {
+        const GatherArgs* ga = p.gather;
+        const unsigned epoch = *reinterpret_cast<volatile const unsigned*>(ga->ctrl[ga->rank]);
+        gather_off = (long long)(epoch & 1u) * ga->area + (long long)ga->rank * ga->npad;
+    }
     XPtr xp;
     xp.mstride_q = (size_t)p.ksteps * 8192;
     xp.mstride_d = (size_t)p.ksteps * 2048;
@@ -379,7 +388,22 @@ __global__ void __launch_bounds__(512) gemv_q_fast(const QGemvParams p) {
             for (int m = 0; m < M; ++m) {
                 float v = acc[m];
                 for (int o = p.G >> 1; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-                if (g == 0 && row < p.N) p.y[(size_t)m * p.ldy + row] = v;
+                if (p.gather) {   // this rank's slice in the local area and every peer's, over NVLink
+                    const GatherArgs* ga = p.gather;
+                    const long long o0 = gather_off + (long long)m * ga->world * ga->npad + (long long)cur.tile * p.TR;
+                    if (p.TR == 4 && (cur.tile + 1) * 4 <= p.N && (o0 & 3) == 0) {
+                        // The 4 rows of the tile (lanes 0, 8, 16, 24) as one 16-byte store per rank.
+                        const float v1 = __shfl_sync(0xffffffffu, v, 8), v2 = __shfl_sync(0xffffffffu, v, 16);
+                        const float v3 = __shfl_sync(0xffffffffu, v, 24);
+                        if (lane == 0)
+                            for (int rk = 0; rk < ga->world; ++rk)
+                                *reinterpret_cast<float4*>(ga->y[rk] + o0) = make_float4(v, v1, v2, v3);
+                    } else if (g == 0 && row < p.N) {
+                        for (int rk = 0; rk < ga->world; ++rk) ga->y[rk][o0 + r] = v;
+                    }
+                } else if (g == 0 && row < p.N) {
+                    p.y[(size_t)m * p.ldy + row] = v;
+                }
                 acc[m] = 0.0f;
             }
         }
@@ -391,6 +415,42 @@ __global__ void __launch_bounds__(512) gemv_q_fast(const QGemvParams p) {
             ++issued;
         }
         cur.next(p, GW);
+    }
+}
+
+// One warp, after this rank's GEMV of the step: tell every peer that this
+// rank's slice has landed in its buffer, wait (bounded) until every peer's
+// counter for this rank shows the step, then advance the epoch, so the next
+// GEMV writes the other full-y area. The GEMV's stores to the peers were
+// performed when it completed (griddepcontrol.wait returns after that), so
+// one system-scope release per peer publishes them. On a timeout the epoch
+// still advances and the error word gets kErrPeerTimeout (the gathered y of
+// that step is then incomplete).
+__global__ void __launch_bounds__(32) gather_wait_kernel(const GatherArgs* __restrict__ ga, unsigned* err) {
+    pdl_launch_dependents();
+    pdl_wait_primary();   // this rank's GEMV of the step has completed
+    const int lane = threadIdx.x;
+    unsigned* ctrl = ga->ctrl[ga->rank];
+    const unsigned epoch = *reinterpret_cast<volatile unsigned*>(ctrl);
+    if (lane < ga->world && lane != ga->rank) {
+        __threadfence_system();
+        red_release_sys_add(ga->ctrl[lane] + kGatherCounters + ga->rank, 1u);
+    }
+    bool ok = true;
+    if (lane < ga->world && lane != ga->rank) {
+        const unsigned* cnt = ctrl + kGatherCounters + lane;
+        const unsigned long long t0 = globaltimer();
+        for (uint32_t i = 0; ld_acquire_sys(cnt) < epoch + 1u; ++i) {
+            if ((i & 63u) == 0 && globaltimer() - t0 > kWaitLimitNs) {
+                ok = false;
+                break;
+            }
+        }
+    }
+    ok = __all_sync(0xffffffffu, ok);
+    if (lane == 0) {
+        if (!ok && err) atomicOr(err, kErrPeerTimeout);
+        *reinterpret_cast<volatile unsigned*>(ctrl) = epoch + 1u;
     }
 }
 
@@ -962,6 +1022,10 @@ cudaError_t launch_gemv_q(const LaunchCfg& c, int fmt, QGemvParams p, bool fast,
     if (fast) smem = gemv_q_smem(fmt, p.M, p.ksteps, c.warps, p.stages, p.xq == nullptr);
     if (smem_used) *smem_used = smem;
     return fmt == kQ4_0 ? dispatch_m<kQ4_0>(c, p, fast, smem, dump) : dispatch_m<kQ8_0>(c, p, fast, smem, dump);
+}
+
+cudaError_t launch_gather_wait(const LaunchCfg& c, const GatherArgs* g_dev, unsigned* err) {
+    return launch(gather_wait_kernel, dim3(1), dim3(32), 0, c, g_dev, err);
 }
 
 size_t xmma_bytes(int nb) { return (size_t)nb * 320; }

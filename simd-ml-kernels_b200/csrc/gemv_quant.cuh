@@ -52,9 +52,24 @@ struct QGemvParams {
     int G, log2G, TR, ksteps, ntiles;
     int stages;            // shared-memory stages per warp (fast kernel)
     int split;             // tensor-core kernel: K parts per 16-row tile (set by its launcher)
+    const struct GatherArgs* gather;   // fused all-gather of y over peer GPUs, or nullptr (device copy)
     const uint8_t* xq;     // quantized x in global memory (nullptr: each CTA quantizes into shared memory)
     int32_t* dump;         // test-only: per-block integer sums [M, N, nb], or nullptr
     unsigned* err;         // device error word
+};
+
+// All-gather of y fused into the fast kernel's epilogue (row-sharded GEMV,
+// one process per GPU). Every rank owns one buffer, mapped into its peers'
+// address spaces: two full-y areas [M][world·npad] (alternate steps) and a
+// control block of 32-bit words: [0] epoch (completed gathers),
+// [kGatherCounters + s] steps whose slice rank s has delivered here.
+constexpr int kMaxRanks = 8;
+constexpr int kGatherCounters = 8;
+struct GatherArgs {
+    float* y[kMaxRanks];         // rank r's full-y areas (this rank's own at [rank])
+    unsigned* ctrl[kMaxRanks];   // rank r's control block
+    long long area;              // floats per full-y area (M_max · world · npad)
+    int world, rank, npad;
 };
 
 // Fill the tiling of p (p.M, p.N, p.K set): the fast kernel's G = the
@@ -84,6 +99,11 @@ cudaError_t launch_quantize_x(const LaunchCfg& c, const QGemvParams& p, uint8_t*
 cudaError_t launch_gemv_q(const LaunchCfg& c, int fmt, QGemvParams p, bool fast, size_t* smem_used);
 // Size of the fast kernel's dynamic shared memory for this launch.
 size_t gemv_q_smem(int fmt, int M, int ksteps, int warps, int stages, bool x_in_smem);
+
+// Wait until every peer delivered this step's slice, then advance the epoch
+// (one warp; bounded wait, kErrPeerTimeout on err). Launched after a fused
+// GEMV on the same stream.
+cudaError_t launch_gather_wait(const LaunchCfg& c, const GatherArgs* g_dev, unsigned* err);
 
 // Tensor-core path for kMmaMinRows..8 rows of x (fast-kernel conditions):
 // x quantized by launch_quantize_x_mma into xmma_bytes(nb) bytes at p.xq,

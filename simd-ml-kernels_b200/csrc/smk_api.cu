@@ -235,14 +235,15 @@ QPlan plan_q(smk_ctx* c, smk::LaunchCfg* l, smk_qformat fmt, int M, int N, int K
 }
 
 smk_status run_q(smk_ctx* c, smk_qformat fmt, int M, int N, int K, const float* x, int64_t ldx, const uint8_t* Wq,
-                 float* y, int64_t ldy, cudaStream_t s, int32_t* dump, bool x_read_once = false) {
+                 float* y, int64_t ldy, cudaStream_t s, int32_t* dump, bool x_read_once = false,
+                 const smk::GatherArgs* gather = nullptr) {
     if (M == 0 || N == 0) return SMK_OK;
     if (K == 0) {
         for (int m = 0; m < M; ++m) SMK_CUDA(cudaMemsetAsync(y + (size_t)m * ldy, 0, (size_t)N * 4, s), "cudaMemsetAsync");
         return SMK_OK;
     }
     smk::LaunchCfg l = cfg_for(c, s);
-    if (M >= smk::kMmaMinRows && !dump && K % 256 == 0 && (reinterpret_cast<uintptr_t>(Wq) & 15) == 0) {
+    if (!gather && M >= smk::kMmaMinRows && !dump && K % 256 == 0 && (reinterpret_cast<uintptr_t>(Wq) & 15) == 0) {
         // Several rows of x: integer tensor-core kernel (bitwise the reference's
         // scalar order), x quantized once into scratch by its own kernel.
         smk::QGemvParams p = {};
@@ -276,6 +277,8 @@ smk_status run_q(smk_ctx* c, smk_qformat fmt, int M, int N, int K, const float* 
     }
     QPlan q = plan_q(c, &l, fmt, M, N, K, x, ldx, Wq, y, ldy, dump != nullptr);
     q.p.dump = dump;
+    q.p.gather = gather;
+    if (gather && !q.fast) return fail(SMK_ERR_ARGUMENT, "the fused gather needs K %% 256 == 0 and 16-byte aligned Wq");
     if (x_read_once && q.x_in_smem && !dump) {
         // x lives in host memory mapped into the device: one quantize kernel
         // reads it once, instead of every CTA reading it over the bus.
@@ -429,6 +432,124 @@ smk_status smk_gemv_q(smk_ctx* c, smk_qformat fmt, int M, int N, int K, const fl
     DeviceGuard g(c->device);
     if (!g.ok) return fail(SMK_ERR_CUDA, "cudaSetDevice(%d) failed", c->device);
     return run_q(c, fmt, M, N, K, x, ldx, Wq, y, ldy, static_cast<cudaStream_t>(stream), nullptr);
+}
+
+}  // extern "C"
+
+struct smk_gather {
+    smk_ctx* c = nullptr;
+    int world = 0, rank = 0, npad = 0, m_max = 0;
+    void* base = nullptr;                      // this rank's buffer: two full-y areas, control block
+    size_t area_bytes = 0;
+    void* peer[smk::kMaxRanks] = {};           // mapped peer buffers (peer[rank] = base)
+    smk::GatherArgs host = {};
+    smk::GatherArgs* dev = nullptr;            // the same, in device memory (kernel argument)
+    unsigned long long steps = 0;              // calls so far: which area the next one writes
+    bool connected = false;
+};
+
+namespace {
+constexpr size_t kGatherCtrlBytes = 256;
+}
+
+extern "C" {
+
+smk_status smk_gather_create(smk_ctx* c, int world, int rank, int npad, int m_max, smk_gather** out,
+                             void* ipc_handle) {
+    if (!c || !out || !ipc_handle) return fail(SMK_ERR_ARGUMENT, "ctx, out and ipc_handle must not be NULL");
+    *out = nullptr;
+    if (world < 1 || world > smk::kMaxRanks || rank < 0 || rank >= world)
+        return fail(SMK_ERR_ARGUMENT, "need 1 <= world <= %d and 0 <= rank < world", smk::kMaxRanks);
+    if (npad < 1 || m_max < 1 || m_max > smk::kMaxRows) return fail(SMK_ERR_ARGUMENT, "need npad >= 1, 1 <= m_max <= 8");
+    static_assert(sizeof(cudaIpcMemHandle_t) == SMK_IPC_HANDLE_BYTES, "IPC handle size");
+    DeviceGuard dg(c->device);
+    if (!dg.ok) return fail(SMK_ERR_CUDA, "cudaSetDevice(%d) failed", c->device);
+    auto* g = new smk_gather();
+    g->c = c;
+    g->world = world;
+    g->rank = rank;
+    g->npad = npad;
+    g->m_max = m_max;
+    g->area_bytes = align256((size_t)m_max * world * npad * sizeof(float));
+    const size_t bytes = 2 * g->area_bytes + kGatherCtrlBytes;
+    cudaError_t e = cudaMalloc(&g->base, bytes);
+    if (e == cudaSuccess) e = cudaMemset(g->base, 0, bytes);
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(ipc_handle), g->base);
+    if (e != cudaSuccess) {
+        if (g->base) cudaFree(g->base);
+        delete g;
+        return cuda_fail(e, "gather buffer");
+    }
+    *out = g;
+    return SMK_OK;
+}
+
+smk_status smk_gather_connect(smk_gather* g, const void* ipc_handles) {
+    if (!g || !ipc_handles) return fail(SMK_ERR_ARGUMENT, "gather and ipc_handles must not be NULL");
+    if (g->connected) return fail(SMK_ERR_ARGUMENT, "gather already connected");
+    DeviceGuard dg(g->c->device);
+    if (!dg.ok) return fail(SMK_ERR_CUDA, "cudaSetDevice(%d) failed", g->c->device);
+    const auto* hs = static_cast<const cudaIpcMemHandle_t*>(ipc_handles);
+    for (int r = 0; r < g->world; ++r) {
+        if (r == g->rank) {
+            g->peer[r] = g->base;
+            continue;
+        }
+        void* p = nullptr;
+        const cudaError_t e = cudaIpcOpenMemHandle(&p, hs[r], cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            for (int q = 0; q < r; ++q)
+                if (q != g->rank && g->peer[q]) cudaIpcCloseMemHandle(g->peer[q]);
+            return cuda_fail(e, "cudaIpcOpenMemHandle (peer gather buffer)");
+        }
+        g->peer[r] = p;
+    }
+    smk::GatherArgs& a = g->host;
+    for (int r = 0; r < g->world; ++r) {
+        a.y[r] = static_cast<float*>(g->peer[r]);
+        a.ctrl[r] = reinterpret_cast<unsigned*>(static_cast<char*>(g->peer[r]) + 2 * g->area_bytes);
+    }
+    a.area = (long long)(g->area_bytes / sizeof(float));
+    a.world = g->world;
+    a.rank = g->rank;
+    a.npad = g->npad;
+    SMK_CUDA(cudaMalloc(&g->dev, sizeof(smk::GatherArgs)), "cudaMalloc (gather args)");
+    SMK_CUDA(cudaMemcpy(g->dev, &a, sizeof a, cudaMemcpyHostToDevice), "cudaMemcpy (gather args)");
+    g->connected = true;
+    return SMK_OK;
+}
+
+smk_status smk_gather_destroy(smk_gather* g) {
+    if (!g) return SMK_OK;
+    DeviceGuard dg(g->c->device);
+    cudaDeviceSynchronize();
+    for (int r = 0; r < g->world; ++r)
+        if (r != g->rank && g->peer[r]) cudaIpcCloseMemHandle(g->peer[r]);
+    if (g->dev) cudaFree(g->dev);
+    if (g->base) cudaFree(g->base);
+    delete g;
+    return SMK_OK;
+}
+
+smk_status smk_gemv_q_gather(smk_ctx* c, smk_gather* g, smk_qformat fmt, int M, int N_local, int K, const float* x,
+                             int64_t ldx, const uint8_t* Wq, float** y_full, void* stream) {
+    if (!c || !g || !y_full) return fail(SMK_ERR_ARGUMENT, "ctx, gather and y_full must not be NULL");
+    if (!g->connected) return fail(SMK_ERR_ARGUMENT, "gather not connected");
+    smk_status st = check_q_args(fmt, M, N_local, K);
+    if (st != SMK_OK) return st;
+    if (M < 1 || M > g->m_max || N_local < 1 || N_local > g->npad || K < 256)
+        return fail(SMK_ERR_ARGUMENT, "need 1 <= M <= m_max, 1 <= N_local <= npad and K >= 256");
+    if (!x || !Wq || ldx < K) return fail(SMK_ERR_ARGUMENT, "x and Wq must not be NULL; ldx >= K");
+    DeviceGuard dg(c->device);
+    if (!dg.ok) return fail(SMK_ERR_CUDA, "cudaSetDevice(%d) failed", c->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    st = run_q(c, fmt, M, N_local, K, x, ldx, Wq, nullptr, 0, s, nullptr, false, g->dev);
+    if (st != SMK_OK) return st;
+    smk::LaunchCfg l = cfg_for(c, s);
+    SMK_CUDA(smk::launch_gather_wait(l, g->dev, c->d_err), "gather wait launch");
+    *y_full = reinterpret_cast<float*>(static_cast<char*>(g->base) + (g->steps & 1) * g->area_bytes);
+    ++g->steps;
+    return SMK_OK;
 }
 
 smk_status smk_gemv_q4_0(smk_ctx* c, int N, int K, const float* x, const uint8_t* Wq, float* y, void* stream) {

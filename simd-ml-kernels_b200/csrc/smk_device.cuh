@@ -16,6 +16,7 @@ namespace smk {
 enum : unsigned {
     kErrWaitTimeout = 1u,   // an mbarrier wait ran past its deadline
     kErrBadLaunch = 2u,     // a kernel saw parameters its launch code should have rejected
+    kErrPeerTimeout = 4u,   // a peer GPU's gather signal did not arrive in time
 };
 
 // A wait on an mbarrier gives up after this long (ns of %globaltimer): far
@@ -105,6 +106,18 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
             smem_addr(dst)),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
         : "memory");
+}
+
+// System-scope release increment of a (possibly peer GPU's) counter, and the
+// matching acquire load: the writer's earlier stores are visible to a reader
+// that observes the new value.
+__device__ __forceinline__ void red_release_sys_add(unsigned* p, unsigned v) {
+    asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
 }
 
 // Programmatic dependent launch. Both are no-ops when the kernel was not

@@ -1,0 +1,86 @@
+"""Row-sharded GEMV with the all-gather fused into the kernel (gather="nvlink"):
+2 GPUs, one spawned process each, NCCL only for the set-up handshake. Every
+step's gathered y equals the unsharded GEMV on one GPU (bitwise for one and
+two rows of x, which take the same kernel; within the reference's bound of the
+float64 sums for four rows), a step's result stays intact through the next
+step, and no device error is raised. Needs two GPUs; skipped otherwise."""
+
+from __future__ import annotations
+
+import os
+import socket
+import sys
+
+import numpy as np
+import pytest
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(HERE)
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank(rank, world, port, out_dir):
+    for p in (os.path.join(REPO, "simd-ml-kernels_b200"), os.path.join(REPO, "oracle"), HERE):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    from datetime import timedelta
+
+    import torch
+    import torch.distributed as dist
+
+    import simd_ml_kernels as sk
+    from simd_ml_kernels import _core, shard
+
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    status = "ok"
+    try:
+        N, K = 1003, 2048
+        g = torch.Generator(device="cuda").manual_seed(11)
+        W = torch.randn((N, K), generator=g, device="cuda") * 0.02
+        Wq = sk.quantize_q4_0(W).reshape(-1)
+        rb = K // 32 * 18
+        lo, hi = shard.row_slice(N, rank, world)
+        sg = shard.ShardedGemv("q4_0", Wq[lo * rb:hi * rb].clone(), N, K, gather="nvlink")
+        prev = None
+        for step in range(6):
+            M = (1, 2, 4)[step % 3]
+            X = torch.randn((M, K), generator=torch.Generator(device="cuda").manual_seed(100 + step), device="cuda")
+            Y = sg.forward(X if M > 1 else X[0]).reshape(M, N)
+            want = sk.gemv_q4_0_batch(X, Wq, N, K)
+            torch.cuda.synchronize()
+            if M <= 2:
+                assert torch.equal(Y.view(torch.int32), want.view(torch.int32)), f"step {step}: not bitwise"
+            else:
+                assert (Y - want).abs().max().item() <= 1e-5 * want.abs().max().item(), f"step {step}"
+            if prev is not None:   # the previous step's result is still intact
+                assert torch.equal(prev[0], prev[1]), f"step {step}: previous result overwritten"
+            prev = (Y.clone(), Y) if M > 0 else None
+        torch.cuda.synchronize()
+        assert _core._device_error(torch.cuda.current_stream().cuda_stream) == 0
+        sg.close()
+    except Exception as exc:  # noqa: BLE001 - reported to the parent
+        status = f"error: {type(exc).__name__}: {exc}"
+    with open(os.path.join(out_dir, f"rank{rank}.txt"), "w") as f:
+        f.write(status)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_fused_gather_two_gpus(tmp_path):
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    mp.start_processes(_rank, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True, start_method="spawn")
+    for r in range(2):
+        assert (tmp_path / f"rank{r}.txt").read_text() == "ok", (tmp_path / f"rank{r}.txt").read_text()
