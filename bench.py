@@ -308,7 +308,7 @@ def gpu_bench(args, rank: int, world: int, local_rank: int) -> dict | None:
 
     # End to end through the public API: x from pinned host memory, y back to
     # host memory, weights resident on the device (uploaded once, as a model's).
-    e2e_steps = min(max(steps // 100, 200), 2000)
+    e2e_steps = min(max(steps // 10, 200), 2000)
     xh = torch.randn(K_COLS, generator=torch.Generator().manual_seed(1)).pin_memory()
     xh_np = xh.numpy()
     sk.set_pdl(False, local_rank)
@@ -344,6 +344,10 @@ def gpu_bench(args, rank: int, world: int, local_rank: int) -> dict | None:
         sg.close()   # release the gather buffers before the process group goes
 
     extra = {}
+    if not args.only_gemv:
+        sharded = sharded_configs(sk, torch, dev, stream, world, rank, local_rank)
+        if rank == 0:
+            extra["sharded_config4"] = sharded
     if rank == 0 and world == 1:
         extra["llama_stack"] = llama_stack(sk, torch, dev, stream, args)
         if args.all or args.case:
@@ -442,6 +446,75 @@ def llama_stack(sk, torch, dev, stream, args) -> dict:
             "bytes_per_token": tok_bytes, "gb_s": round(tok_bytes / (per_tok_ms * 1e-3) / 1e9, 1),
             "tokens": LLAMA_TOKENS,
             "launch": "one CUDA graph of 128 decode steps, PDL; q/k/v and gate/up as fused row groups"}
+
+
+SHARDED_SHAPES = [(28672, 8192), (8192, 28672), (128256, 8192)]   # config 4: 70B layers, LM head
+
+
+def sharded_configs(sk, torch, dev, stream, world: int, rank: int, local_rank: int) -> dict:
+    """Config 4 (Q4_0, M = 1, W ~ N(0, 0.015) from seed 4) split by rows over
+    the ranks: each step is this rank's GEMV plus the all-gather of y fused
+    into it (world > 1), timed in CUDA graphs as the max over ranks; aggregate
+    GB/s = the whole matrix's algorithmic bytes per step time (strong scaling).
+    Every rank calls this with the same shapes (collectives inside)."""
+    import torch.distributed as dist
+    from simd_ml_kernels import _core, shard
+    res = {}
+    l2 = getattr(torch.cuda.get_device_properties(dev), "L2_cache_size", 126 << 20)
+    for N, K in SHARDED_SHAPES:
+        lo, hi = shard.row_slice(N, rank, world)
+        n, rb = hi - lo, K // 32 * 18
+        g = torch.Generator(device=dev)
+        g.manual_seed(4 * 1000 + rank)
+        wq = torch.empty(n * rb, dtype=torch.uint8, device=dev)
+        for r0 in range(0, n, 8192):
+            rows = min(8192, n - r0)
+            wq[r0 * rb:(r0 + rows) * rb] = sk.quantize_q4_0(
+                torch.randn((rows, K), generator=g, device=dev) * 0.015).reshape(-1)
+        copies = max(2, -(-2 * l2 // (n * rb)) + 1)
+        ws = [wq] + [wq.clone() for _ in range(copies - 1)]
+        x = torch.randn(K, generator=g, device=dev)
+        y = torch.empty(n, device=dev)
+        sg = shard.ShardedGemv("q4_0", wq, N, K, gather="nvlink") if world > 1 else None
+
+        def step(i):
+            if sg is not None:
+                _core._gemv_q_gather(sg._g, 0, 1, n, K, x.data_ptr(), K, ws[i % copies].data_ptr(),
+                                     stream.cuda_stream, local_rank)
+            else:
+                sk.gemv_q4_0(x, ws[i % copies], n, K, out=y)
+
+        reps = copies * max(1, 64 // copies)
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            step(0)
+            torch.cuda.synchronize(dev)
+            with torch.cuda.graph(gr, stream=stream):
+                for i in range(reps):
+                    step(i)
+            gr.replay()
+            torch.cuda.synchronize(dev)
+            if world > 1:
+                dist.barrier()
+            s0, e0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s0.record(stream)
+            for _ in range(5):
+                gr.replay()
+            e0.record(stream)
+        torch.cuda.synchronize(dev)
+        t = torch.tensor([s0.elapsed_time(e0) * 1e3 / (5 * reps)], device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        us = float(t.item())
+        del gr
+        if sg is not None:
+            sg.close()
+        nbytes = N * K // 32 * 18 + 4 * K + 4 * N
+        res[f"q4_0 M=1 N={N} K={K} over {world} GPU(s)"] = {
+            "us_per_step": round(us, 3), "gb_s_aggregate": round(nbytes / (us * 1e-6) / 1e9, 1),
+            "rows_per_gpu": n, "gather": "fused NVLink" if world > 1 else None}
+        del ws, wq
+    return res
 
 
 def other_configs(sk, torch, dev, stream, only: str | None = None) -> dict:
