@@ -639,11 +639,25 @@ __global__ void __launch_bounds__(kMmaWarps * 32) gemv_q_mma(const QGemvParams p
     const int ntiles = (p.N + 15) / 16, ksteps = p.nb / KB;   // K % 256 == 0: whole items
     const int S = p.split, T = nwarps / S, part = warp % S, tl = warp / S;
     const int ks_lo = part * ksteps / S, nks = (part + 1) * ksteps / S - ks_lo;
-    const int ngroups = (ntiles + T - 1) / T;
-    const int my_groups = (int)blockIdx.x < ngroups ? (ngroups - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
-    // Only the last group can hold a tile past N.
-    const int last_tile = my_groups > 0 ? ((int)blockIdx.x + (my_groups - 1) * (int)gridDim.x) * T + tl : 0;
-    const int valid_groups = my_groups > 0 && last_tile >= ntiles ? my_groups - 1 : my_groups;
+    // Rounds of this warp. S == 1: the CTA owns a contiguous range of tiles
+    // (an even share, so every SM streams one region of W) and its warps
+    // take them in turn (no CTA barrier). S > 1: the CTA's groups of T tiles,
+    // CTA-uniform (a barrier per round); only the last group can hold a tile
+    // past N.
+    const int c_lo = (int)((long long)blockIdx.x * ntiles / gridDim.x);
+    const int c_hi = (int)((long long)(blockIdx.x + 1) * ntiles / gridDim.x);
+    int my_groups, valid_groups;
+    if (S == 1) {
+        my_groups = valid_groups = c_lo + warp < c_hi ? (c_hi - 1 - c_lo - warp) / nwarps + 1 : 0;
+    } else {
+        const int ngroups = (ntiles + T - 1) / T;
+        my_groups = (int)blockIdx.x < ngroups ? (ngroups - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+        const int last_tile = my_groups > 0 ? ((int)blockIdx.x + (my_groups - 1) * (int)gridDim.x) * T + tl : 0;
+        valid_groups = my_groups > 0 && last_tile >= ntiles ? my_groups - 1 : my_groups;
+    }
+    auto tile_of = [&](int r) {
+        return S == 1 ? c_lo + warp + r * nwarps : ((int)blockIdx.x + r * (int)gridDim.x) * T + tl;
+    };
     const int nitems = valid_groups * nks;
     if (lane == 0) {
         for (int i = 0; i < p.stages; ++i) mbar_init(&bars[i], 1);
@@ -654,7 +668,7 @@ __global__ void __launch_bounds__(kMmaWarps * 32) gemv_q_mma(const QGemvParams p
     // Issue cursor over (group round, k-step); items are consumed in the same order.
     int i_r = 0, i_ks = 0, i_slot = 0, issued = 0;
     auto issue_next = [&]() {
-        const int tile = ((int)blockIdx.x + i_r * (int)gridDim.x) * T + tl;
+        const int tile = tile_of(i_r);
         mma_issue<F>(&wmap, tile, ks_lo + i_ks, ring + (size_t)i_slot * ITEM, &bars[i_slot], lane);
         if (++i_ks == nks) { i_ks = 0; ++i_r; }
         if (++i_slot == p.stages) i_slot = 0;
@@ -680,8 +694,8 @@ __global__ void __launch_bounds__(kMmaWarps * 32) gemv_q_mma(const QGemvParams p
 
     int c_slot = 0, consumed = 0;
     uint32_t c_phase = 0;
-    for (int r = 0; r < my_groups; ++r) {   // CTA-uniform: every warp meets every barrier
-        const int tile = ((int)blockIdx.x + r * (int)gridDim.x) * T + tl;
+    for (int r = 0; r < my_groups; ++r) {   // S > 1: CTA-uniform, every warp meets every barrier
+        const int tile = tile_of(r);
         float2 acc[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
         if (r < valid_groups) {
             for (int k = 0; k < nks && !failed; ++k) {
@@ -1094,9 +1108,15 @@ cudaError_t launch_gemv_q_mma(const LaunchCfg& c, int fmt, const QGemvParams& p,
     QGemvParams q = p;
     q.split = 1;
     while (q.split < kMmaWarps && 2LL * q.split <= ksteps && ntiles * q.split * 4 < cap * kMmaWarps * 3) q.split *= 2;
-    const long long T = kMmaWarps / q.split;
-    const long long ngroups = (ntiles + T - 1) / T;
-    const long long grid = std::min(ngroups, cap);
+    long long grid;
+    if (q.split == 1) {   // tiles interleaved over every warp of the grid
+        grid = std::min(std::max((ntiles + kMmaWarps - 1) / kMmaWarps, std::min<long long>(ntiles, c.num_sms)), cap);
+    } else {              // groups of kMmaWarps / S tiles per CTA: enough groups for every CTA slot
+        while (q.split < kMmaWarps && 2LL * q.split <= ksteps && (ntiles * q.split + kMmaWarps - 1) / kMmaWarps < cap)
+            q.split *= 2;
+        const long long T = kMmaWarps / q.split;
+        grid = std::min((ntiles + T - 1) / T, cap);
+    }
     return launch(k, dim3((unsigned)std::max<long long>(grid, 1)), dim3(kMmaWarps * 32), smem, c, q, wmap);
 }
 
