@@ -315,11 +315,21 @@ __global__ void __launch_bounds__(512) gemv_q_fast(const QGemvParams p) {
 
     pdl_launch_dependents();
 
-    // Tiles of this warp: gw, gw + GW, ... (interleaved over CTAs so every SM
-    // gets a near-equal share); each tile is ksteps items.
-    const int GW = gridDim.x * nwarps;
-    const int gw = warp * gridDim.x + blockIdx.x;
-    const int my_tiles = gw < p.ntiles ? (p.ntiles - 1 - gw) / GW + 1 : 0;
+    // Tiles of this warp: gw, gw + GW, ...; each tile is ksteps items. With
+    // p.contiguous the CTA owns a contiguous, even share of the tiles (each SM
+    // streams one region of W) and its warps take them in turn; otherwise the
+    // tiles are interleaved over every warp of the grid.
+    int GW, gw, tiles_end;
+    if (p.contiguous) {
+        GW = nwarps;
+        gw = (int)((long long)blockIdx.x * p.ntiles / gridDim.x) + warp;
+        tiles_end = (int)((long long)(blockIdx.x + 1) * p.ntiles / gridDim.x);
+    } else {
+        GW = gridDim.x * nwarps;
+        gw = warp * gridDim.x + blockIdx.x;
+        tiles_end = p.ntiles;
+    }
+    const int my_tiles = gw < tiles_end ? (tiles_end - 1 - gw) / GW + 1 : 0;
     const int nitems = my_tiles * p.ksteps;
 
     if (lane == 0) {

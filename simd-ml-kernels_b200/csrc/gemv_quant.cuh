@@ -51,6 +51,7 @@ struct QGemvParams {
     int nsbp;              // ceil(nb / 8)
     int G, log2G, TR, ksteps, ntiles;
     int stages;            // shared-memory stages per warp (fast kernel)
+    int contiguous;        // fast kernel: 1 = each CTA takes a contiguous range of tiles, 0 = tiles interleaved over CTAs
     int split;             // tensor-core kernel: K parts per 16-row tile (set by its launcher)
     const struct GatherArgs* gather;   // fused all-gather of y over peer GPUs, or nullptr (device copy)
     const uint8_t* xq;     // quantized x in global memory (nullptr: each CTA quantizes into shared memory)

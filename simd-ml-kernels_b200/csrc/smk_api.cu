@@ -180,11 +180,15 @@ smk::LaunchCfg cfg_for(smk_ctx* c, cudaStream_t s) {
 // one stage each and one CTA per SM (the next GEMV's CTA fits beside it under
 // programmatic dependent launch); a larger one is bandwidth-bound, best with
 // 8 warps of two stages and two CTAs per SM.
-void auto_shape(smk_ctx* c, const smk::QGemvParams& p, smk::LaunchCfg* l, int* stages) {
+// The small, latency-bound shapes also take contiguous per-CTA tile ranges
+// (measured: config 0 3.04 vs 3.41 µs per chained step); the large ones keep
+// tiles interleaved over the CTAs.
+void auto_shape(smk_ctx* c, smk::QGemvParams& p, smk::LaunchCfg* l, int* stages) {
     const bool large = (long long)p.ntiles >= 64LL * c->num_sms;
     if (c->warps <= 0) l->warps = large ? 8 : 16;
     if (c->ctas_per_sm <= 0) l->ctas_per_sm = large ? 2 : 1;
     *stages = c->stages > 0 ? c->stages : (large ? 2 : 1);
+    p.contiguous = large ? 0 : 1;
 }
 
 smk_status check_q_args(smk_qformat fmt, int M, int N, int K) {
