@@ -239,7 +239,7 @@ QPlan plan_q(smk_ctx* c, smk::LaunchCfg* l, smk_qformat fmt, int M, int N, int K
 }
 
 smk_status run_q(smk_ctx* c, smk_qformat fmt, int M, int N, int K, const float* x, int64_t ldx, const uint8_t* Wq,
-                 float* y, int64_t ldy, cudaStream_t s, int32_t* dump, bool x_read_once = false,
+                 float* y, int64_t ldy, cudaStream_t s, int32_t* dump,
                  const smk::GatherArgs* gather = nullptr) {
     if (M == 0 || N == 0) return SMK_OK;
     if (K == 0) {
@@ -283,11 +283,6 @@ smk_status run_q(smk_ctx* c, smk_qformat fmt, int M, int N, int K, const float* 
     q.p.dump = dump;
     q.p.gather = gather;
     if (gather && !q.fast) return fail(SMK_ERR_ARGUMENT, "the fused gather needs K %% 256 == 0 and 16-byte aligned Wq");
-    if (x_read_once && q.x_in_smem && !dump) {
-        // x lives in host memory mapped into the device: one quantize kernel
-        // reads it once, instead of every CTA reading it over the bus.
-        q.x_in_smem = false;
-    }
     if (!q.x_in_smem) {
         uint8_t* xq;
         {
@@ -547,7 +542,7 @@ smk_status smk_gemv_q_gather(smk_ctx* c, smk_gather* g, smk_qformat fmt, int M, 
     DeviceGuard dg(c->device);
     if (!dg.ok) return fail(SMK_ERR_CUDA, "cudaSetDevice(%d) failed", c->device);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    st = run_q(c, fmt, M, N_local, K, x, ldx, Wq, nullptr, 0, s, nullptr, false, g->dev);
+    st = run_q(c, fmt, M, N_local, K, x, ldx, Wq, nullptr, 0, s, nullptr, g->dev);
     if (st != SMK_OK) return st;
     smk::LaunchCfg l = cfg_for(c, s);
     SMK_CUDA(smk::launch_gather_wait(l, g->dev, c->d_err), "gather wait launch");
