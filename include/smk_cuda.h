@@ -74,12 +74,14 @@ smk_status smk_ctx_destroy(smk_ctx* ctx);
  *   SMK_OPT_STAGES  shared-memory stages per warp of that kernel, each one
  *                   tile of weights (1..8).
  *   SMK_OPT_CTAS_PER_SM  resident CTAs per SM of that kernel (1..8).
- *                   For these three, 0 (the default) picks per call: 16 warps,
- *                   1 stage, 1 CTA per SM for GEMVs of up to 64 tiles per SM
- *                   (latency-bound; leaves room for the next GEMV's CTA under
- *                   programmatic dependent launch), else 8 warps, 2 stages,
- *                   2 CTAs per SM. */
-enum { SMK_OPT_PDL = 1, SMK_OPT_WARPS = 2, SMK_OPT_STAGES = 3, SMK_OPT_CTAS_PER_SM = 4 };
+ *                   For these three, 0 (the default) picks per call: 16 warps;
+ *                   1 stage and up to 2 CTAs per SM for GEMVs of up to 64
+ *                   tiles per SM (latency-bound), else 2 stages and 1 CTA
+ *                   per SM.
+ *   SMK_OPT_TILE_ORDER  how that kernel's row tiles are spread over its CTAs:
+ *                   1 interleaved, 2 or 0 (default) a contiguous range per
+ *                   CTA. */
+enum { SMK_OPT_PDL = 1, SMK_OPT_WARPS = 2, SMK_OPT_STAGES = 3, SMK_OPT_CTAS_PER_SM = 4, SMK_OPT_TILE_ORDER = 5 };
 smk_status smk_ctx_set(smk_ctx* ctx, int option, long long value);
 smk_status smk_ctx_get(smk_ctx* ctx, int option, long long* value);
 /* The CUDA device that owns `ptr` (device or managed memory), or -1 for host memory. */

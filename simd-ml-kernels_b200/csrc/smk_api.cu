@@ -153,6 +153,7 @@ struct smk_ctx {
     int warps = 0;
     int stages = 0;
     int ctas_per_sm = 0;
+    int tile_order = 0;             // 0 automatic, 1 interleaved, 2 contiguous
     unsigned* d_err = nullptr;      // device error word
     unsigned* d_reject = nullptr;   // quantizer rejection flag
     std::mutex mu_scratch;                    // guards scratch and test_buf
@@ -175,20 +176,18 @@ smk::LaunchCfg cfg_for(smk_ctx* c, cudaStream_t s) {
     return l;
 }
 
-// The automatic launch shape (measured on B200, config-0 to LM-head sizes):
-// a GEMV of up to ~64 tiles per SM is latency-bound, best with 16 warps of
-// one stage each and one CTA per SM (the next GEMV's CTA fits beside it under
-// programmatic dependent launch); a larger one is bandwidth-bound, best with
-// 8 warps of two stages and two CTAs per SM.
-// The small, latency-bound shapes also take contiguous per-CTA tile ranges
-// (measured: config 0 3.04 vs 3.41 µs per chained step); the large ones keep
-// tiles interleaved over the CTAs.
+// The automatic launch shape (measured on B200 in CUDA-graph chains, config-0
+// to LM-head sizes): 16 warps per CTA and contiguous per-CTA tile ranges
+// throughout; GEMVs of up to ~64 tiles per SM (latency-bound) take one stage
+// per warp with up to 2 CTAs per SM, larger ones two stages and one CTA per
+// SM (8192x28672: 29.7 µs against 34.1 for 8 warps x 2 stages x 2 CTAs with
+// interleaved tiles; 16384x2048: 5.24 against 5.58 µs for one CTA per SM).
 void auto_shape(smk_ctx* c, smk::QGemvParams& p, smk::LaunchCfg* l, int* stages) {
     const bool large = (long long)p.ntiles >= 64LL * c->num_sms;
-    if (c->warps <= 0) l->warps = large ? 8 : 16;
-    if (c->ctas_per_sm <= 0) l->ctas_per_sm = large ? 2 : 1;
+    if (c->warps <= 0) l->warps = 16;
+    if (c->ctas_per_sm <= 0) l->ctas_per_sm = large ? 1 : 2;
     *stages = c->stages > 0 ? c->stages : (large ? 2 : 1);
-    p.contiguous = large ? 0 : 1;
+    p.contiguous = c->tile_order == 1 ? 0 : 1;
 }
 
 smk_status check_q_args(smk_qformat fmt, int M, int N, int K) {
@@ -367,6 +366,10 @@ smk_status smk_ctx_set(smk_ctx* c, int option, long long v) {
             if (v < 0 || v > 8) return fail(SMK_ERR_ARGUMENT, "CTAs per SM must be in 0..8 (0: automatic)");
             c->ctas_per_sm = (int)v;
             return SMK_OK;
+        case SMK_OPT_TILE_ORDER:
+            if (v < 0 || v > 2) return fail(SMK_ERR_ARGUMENT, "tile order must be 0, 1 or 2");
+            c->tile_order = (int)v;
+            return SMK_OK;
         default: return fail(SMK_ERR_ARGUMENT, "unknown option %d", option);
     }
 }
@@ -378,6 +381,7 @@ smk_status smk_ctx_get(smk_ctx* c, int option, long long* v) {
         case SMK_OPT_WARPS: *v = c->warps; return SMK_OK;
         case SMK_OPT_STAGES: *v = c->stages; return SMK_OK;
         case SMK_OPT_CTAS_PER_SM: *v = c->ctas_per_sm; return SMK_OK;
+        case SMK_OPT_TILE_ORDER: *v = c->tile_order; return SMK_OK;
         default: return fail(SMK_ERR_ARGUMENT, "unknown option %d", option);
     }
 }
