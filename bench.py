@@ -350,6 +350,7 @@ def gpu_bench(args, rank: int, world: int, local_rank: int) -> dict | None:
             extra["sharded_config4"] = sharded
     if rank == 0 and world == 1:
         extra["llama_stack"] = llama_stack(sk, torch, dev, stream, args)
+        extra["llama_decode_swiglu"] = llama_stack(sk, torch, dev, stream, args, swiglu=True)
         if args.all or args.case:
             extra["configs"] = other_configs(sk, torch, dev, stream, args.case)
 
@@ -392,14 +393,17 @@ def gpu_bench(args, rank: int, world: int, local_rank: int) -> dict | None:
     return out
 
 
-def llama_stack(sk, torch, dev, stream, args) -> dict:
+def llama_stack(sk, torch, dev, stream, args, swiglu: bool = False) -> dict:
     """a Llama-3.2-1B decode step's GEMVs — 16 layers of
     q 2048->2048, k, v 2048->512, o 2048->2048, gate, up 2048->8192, down
     8192->2048, and the tied 2048->128256 LM head — on random-init Q4_0 weights
     (seed 2), fresh activations every step, 128 steps in one CUDA graph.
     q, k and v read the same activation row within a step, as do gate and up,
     so each group runs as one GEMV over its concatenated rows (the same bytes
-    and outputs as the separate GEMVs): 4 GEMVs per layer + the LM head."""
+    and outputs as the separate GEMVs): 4 GEMVs per layer + the LM head.
+    swiglu: the down projection reads silu(gate) * up of the layer's gate/up
+    GEMV instead of fresh activations, as the decoder does, with the SwiGLU
+    product formed inside it (more work than the GEMV-only stack)."""
     g = torch.Generator(device=dev)
     g.manual_seed(2)
     groups = []   # (rows N, K, logical GEMVs)
@@ -424,8 +428,17 @@ def llama_stack(sk, torch, dev, stream, args) -> dict:
         with torch.cuda.graph(gr, stream=stream):
             for t in range(LLAMA_TOKENS):
                 xo = yo = 0
+                gate_up = None
                 for (n, k, _), wq in zip(groups, weights):
-                    sk.gemv_q4_0(X[t, xo:xo + k], wq, n, k, out=Y[yo:yo + n])
+                    if swiglu and gate_up is not None and n == 2048 and k == 8192:
+                        # The down projection takes silu(gate) * up of the gate/up GEMV just
+                        # before it, formed while its activations are quantized.
+                        sk.gemv_q4_0_silu_mul(gate_up[:8192], gate_up[8192:], wq, n, k, out=Y[yo:yo + n])
+                        gate_up = None
+                    else:
+                        sk.gemv_q4_0(X[t, xo:xo + k], wq, n, k, out=Y[yo:yo + n])
+                        if n == 16384:
+                            gate_up = Y[yo:yo + n]
                     xo += k
                     yo += n
         for _ in range(3):
@@ -445,7 +458,9 @@ def llama_stack(sk, torch, dev, stream, args) -> dict:
             "gemvs_per_token": sum(c for _, _, c in groups), "launches_per_token": len(groups),
             "bytes_per_token": tok_bytes, "gb_s": round(tok_bytes / (per_tok_ms * 1e-3) / 1e9, 1),
             "tokens": LLAMA_TOKENS,
-            "launch": "one CUDA graph of 128 decode steps, PDL; q/k/v and gate/up as fused row groups"}
+            "launch": "one CUDA graph of 128 decode steps, PDL; q/k/v and gate/up as fused row groups"
+                      + ("; down projection fed by silu(gate)*up inside its activation quantization" if swiglu
+                         else "")}
 
 
 SHARDED_SHAPES = [(28672, 8192), (8192, 28672), (128256, 8192)]   # config 4: 70B layers, LM head

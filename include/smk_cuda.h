@@ -103,6 +103,16 @@ smk_status smk_gemv_q(smk_ctx* ctx, smk_qformat fmt, int M, int N, int K, const 
                       const uint8_t* Wq, float* y, int64_t ldy, void* stream);
 smk_status smk_gemv_q4_0(smk_ctx* ctx, int N, int K, const float* x, const uint8_t* Wq, float* y, void* stream);
 smk_status smk_gemv_q8_0(smk_ctx* ctx, int N, int K, const float* x, const uint8_t* Wq, float* y, void* stream);
+/* The decode step's down projection with its SwiGLU input formed on the fly:
+ * y = (silu(gate) * up) @ W.T, silu(g) = g / (1 + exp(-g)) as the reference
+ * (src/kernels/scalar_kernels.cpp:196-198), the product quantized to Q8 inside
+ * the GEMV; replaces w_down(silu(w_gate(h)) * w_up(h)) of the reference's
+ * examples/llama/llama.py:434 without the separate SiLU and product passes.
+ * Device pointers, asynchronous; gate [M, ldg], up [M, ldu]. An addition. */
+smk_status smk_gemv_q_silu_mul(smk_ctx* ctx, smk_qformat fmt, int M, int N, int K, const float* gate, int64_t ldg,
+                               const float* up, int64_t ldu, const uint8_t* Wq, float* y, int64_t ldy, void* stream);
+/* out[i] = silu(gate[i]) * up[i], i < n, the same arithmetic (device pointers). */
+smk_status smk_silu_mul(smk_ctx* ctx, int64_t n, const float* gate, const float* up, float* out, void* stream);
 /* Host-or-device pointers, synchronous. The exact contract of GemvQ4_0Fn / GemvQ8_0Fn. */
 smk_status smk_gemv_q_host(smk_ctx* ctx, smk_qformat fmt, int M, int N, int K, const float* x, const uint8_t* Wq,
                            float* y);

@@ -648,6 +648,23 @@ PYBIND11_MODULE(_core, m) {
         check(st);
         return reinterpret_cast<uintptr_t>(y);
     });
+    m.def("_gemv_q_silu_mul_dev", [](int fmt, int M, int N, int K, uintptr_t g, long long ldg, uintptr_t u,
+                                     long long ldu, uintptr_t w, uintptr_t y, long long ldy, uintptr_t stream,
+                                     int device) {
+        smk_ctx* c = ctx_for(device);
+        smk_status st;
+        {
+            py::gil_scoped_release release;
+            st = smk_gemv_q_silu_mul(c, (smk_qformat)fmt, M, N, K, reinterpret_cast<const float*>(g), ldg,
+                                     reinterpret_cast<const float*>(u), ldu, reinterpret_cast<const uint8_t*>(w),
+                                     reinterpret_cast<float*>(y), ldy, reinterpret_cast<void*>(stream));
+        }
+        check(st);
+    });
+    m.def("_silu_mul", [](long long n, uintptr_t g, uintptr_t u, uintptr_t out, uintptr_t stream, int device) {
+        check(smk_silu_mul(ctx_for(device), n, reinterpret_cast<const float*>(g), reinterpret_cast<const float*>(u),
+                           reinterpret_cast<float*>(out), reinterpret_cast<void*>(stream)));
+    });
     m.def("version", []() { return std::string(smk_version()); });
     m.def("_set_device", [](int d) { current_device_hint = d; });
     m.def("_ctx_set", [](int option, long long value) { check(smk_ctx_set(ctx_for(current_device_hint), option, value)); });

@@ -59,6 +59,25 @@ struct XGeom {
     int M, nb, log2G, ksteps;
 };
 
+// The decode step's SwiGLU input of the down projection, silu(g) * u, with
+// silu(g) = g / (1 + exp(−g)) as the reference defines it
+// (src/kernels/scalar_kernels.cpp:196-198; silu_avx2.cpp:1-26): IEEE divide
+// and product, CUDA's expf (a few ulp), so the value is within the reference's
+// own SiLU tolerance of 1e-35 + 1e-6·|SiLU(g)| before the product. For
+// g < −88.7, exp(−g) overflows, the denominator is +inf and the result −0;
+// silu(−inf) = NaN and silu(+inf) = +inf, as the reference's kernels.
+__device__ __forceinline__ float silu_mul1(float g, float u) {
+    return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+}
+__device__ __forceinline__ float4 silu_mul4(float4 g, float4 u) {
+    return make_float4(silu_mul1(g.x, u.x), silu_mul1(g.y, u.y), silu_mul1(g.z, u.z), silu_mul1(g.w, u.w));
+}
+
+// One row's 4 activation values at element offset k: x, or silu(x) * up.
+__device__ __forceinline__ float4 load_act4(const float* xr, const float* ur, size_t k) {
+    return ur ? silu_mul4(load_x4(xr + k), load_x4(ur + k)) : load_x4(xr + k);
+}
+
 // One thread's 4 values of a 32-value block, quantized to Q8: all 32 lanes of
 // the warp call this together (full-mask shuffles; the xor offsets stay inside
 // each 8-lane group of one block).
@@ -119,7 +138,8 @@ __device__ __forceinline__ void quantize_x_block(float4 v, int gq, bool valid, c
 // group), then the next 4·warps, so every lane of a warp runs every
 // iteration. MT: rows of x known at compile time (0: xg.M).
 template <int MT>
-__device__ __forceinline__ void quantize_x_rows(const float* __restrict__ x, long long ldx, const XGeom& xg,
+__device__ __forceinline__ void quantize_x_rows(const float* __restrict__ x, long long ldx,
+                                                const float* __restrict__ up, long long ldu, const XGeom& xg,
                                                 uint8_t* xb, int tid, int nthreads) {
     const int gq = tid & 7, grp = (tid & 31) >> 3;
     const int wstride = (nthreads >> 5) * 4, nb = xg.nb;
@@ -128,12 +148,13 @@ __device__ __forceinline__ void quantize_x_rows(const float* __restrict__ x, lon
     for (int m = 0; m < (MT > 0 ? MT : kMaxRows); ++m) {
         if (m >= rows) break;
         const float* xr = x + (size_t)m * ldx + gq * 4;
+        const float* ur = up ? up + (size_t)m * ldu + gq * 4 : nullptr;
         for (int wbase = (tid >> 5) * 4; wbase < nb; wbase += kXUnroll * wstride) {
             float4 v[kXUnroll];
 #pragma unroll
             for (int u = 0; u < kXUnroll; ++u) {
                 const int b = wbase + u * wstride + grp;
-                v[u] = b < nb ? load_x4(xr + (size_t)b * kQK) : make_float4(0.f, 0.f, 0.f, 0.f);
+                v[u] = b < nb ? load_act4(xr, ur, (size_t)b * kQK) : make_float4(0.f, 0.f, 0.f, 0.f);
             }
 #pragma unroll
             for (int u = 0; u < kXUnroll; ++u) {
@@ -146,10 +167,19 @@ __device__ __forceinline__ void quantize_x_rows(const float* __restrict__ x, lon
 }
 
 __global__ void __launch_bounds__(kThreadsQuantX) quantize_x_kernel(const float* __restrict__ x, long long ldx,
+                                                                     const float* __restrict__ up, long long ldu,
                                                                      XGeom xg, uint8_t* xq) {
     pdl_launch_dependents();
     pdl_wait_primary();   // x comes from the previous kernel; xq may still be read by it
-    quantize_x_rows<0>(x, ldx, xg, xq, blockIdx.x * blockDim.x + threadIdx.x, gridDim.x * blockDim.x);
+    quantize_x_rows<0>(x, ldx, up, ldu, xg, xq, blockIdx.x * blockDim.x + threadIdx.x, gridDim.x * blockDim.x);
+}
+
+__global__ void __launch_bounds__(256) silu_mul_kernel(long long n, const float* __restrict__ g,
+                                                       const float* __restrict__ u, float* __restrict__ out) {
+    pdl_launch_dependents();
+    pdl_wait_primary();
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+        out[i] = silu_mul1(g[i], u[i]);
 }
 
 // ---- integer block dots -----------------------------------------------------------
@@ -348,7 +378,7 @@ __global__ void __launch_bounds__(512) gemv_q_fast(const QGemvParams p) {
     pdl_wait_primary();
     if constexpr (!kXGlobal) {
         const XGeom xg{M, p.nb, p.log2G, p.ksteps};
-        quantize_x_rows<M>(p.x, p.ldx, xg, xs, threadIdx.x, blockDim.x);
+        quantize_x_rows<M>(p.x, p.ldx, p.up, p.ldu, xg, xs, threadIdx.x, blockDim.x);
         __syncthreads();
     }
     const uint8_t* xb = kXGlobal ? p.xq : xs;
@@ -507,6 +537,7 @@ template <int F> __host__ __device__ constexpr int mma_kb() { return 8; }
 template <int F> __host__ __device__ constexpr int mma_rs() { return 8 * block_bytes(F); }
 
 __global__ void __launch_bounds__(kThreadsQuantX) quantize_x_mma_kernel(const float* __restrict__ x, long long ldx,
+                                                                         const float* __restrict__ up, long long ldu,
                                                                          int M, int nb, uint8_t* xq) {
     pdl_launch_dependents();
     pdl_wait_primary();   // x comes from the previous kernel; xq may still be read by it
@@ -519,7 +550,8 @@ __global__ void __launch_bounds__(kThreadsQuantX) quantize_x_mma_kernel(const fl
         const bool valid = grp < groups;
         const int b = (int)(grp >> 3), m = (int)(grp & 7);
         float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (valid && m < M) v = load_x4(x + (size_t)m * ldx + (size_t)b * kQK + gq * 4);
+        if (valid && m < M)
+            v = load_act4(x + (size_t)m * ldx, up ? up + (size_t)m * ldu : nullptr, (size_t)b * kQK + gq * 4);
         const Q8Quad q = quantize_quad(v);
         if (!valid) continue;
         reinterpret_cast<uint32_t*>(xq)[((size_t)(b * 8 + m) * 4 + (gq & 3)) * 2 + (gq >> 2)] = m < M ? q.word : 0u;
@@ -1037,7 +1069,14 @@ cudaError_t launch_quantize_x(const LaunchCfg& c, const QGemvParams& p, uint8_t*
                                                (long long)c.num_sms * 4);
     const XGeom xg{p.M, p.nb, p.log2G, p.ksteps};
     return launch(quantize_x_kernel, dim3((unsigned)std::max<long long>(grid, 1)), dim3(kThreadsQuantX), 0, c, p.x,
-                  p.ldx, xg, xq);
+                  p.ldx, p.up, p.ldu, xg, xq);
+}
+
+cudaError_t launch_silu_mul(cudaStream_t s, long long n, const float* gate, const float* up, float* out) {
+    if (n <= 0) return cudaSuccess;
+    const long long grid = std::min<long long>((n + 255) / 256, 148LL * 8);
+    silu_mul_kernel<<<(unsigned)grid, 256, 0, s>>>(n, gate, up, out);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_gemv_q(const LaunchCfg& c, int fmt, QGemvParams p, bool fast, size_t* smem_used) {
@@ -1059,7 +1098,7 @@ cudaError_t launch_quantize_x_mma(const LaunchCfg& c, const QGemvParams& p, uint
     const long long grid = std::min<long long>((groups + kThreadsQuantX / 8 - 1) / (kThreadsQuantX / 8),
                                                (long long)c.num_sms * 4);
     return launch(quantize_x_mma_kernel, dim3((unsigned)std::max<long long>(grid, 1)), dim3(kThreadsQuantX), 0, c,
-                  p.x, p.ldx, p.M, p.nb, xq);
+                  p.x, p.ldx, p.up, p.ldu, p.M, p.nb, xq);
 }
 
 size_t gemv_q_mma_smem(int fmt, int stages, int nb, bool x_in_smem) {

@@ -41,8 +41,10 @@ __host__ __device__ inline size_t xd_off(int M, int ksteps, int m, int ks, int j
 }
 
 struct QGemvParams {
-    const float* x;        // [M, ldx] fp32 activations (device)
+    const float* x;        // [M, ldx] fp32 activations (device); with `up`, the gate
     long long ldx;
+    const float* up;       // nullptr, or [M, ldu]: the activations are silu(x) * up, formed while quantizing
+    long long ldu;
     const uint8_t* w;      // N rows of K/32 blocks (device)
     float* y;              // [M, ldy]
     long long ldy;
@@ -93,8 +95,12 @@ struct LaunchCfg {
     int ctas_per_sm = 1;   // cap on resident CTAs per SM of the fast kernel
 };
 
-// Quantize p.x into the layout above at xq (global memory, xq_total_bytes(M, ksteps)).
+// Quantize p.x (or silu(p.x) * p.up) into the layout above at xq (global
+// memory, xq_total_bytes(M, ksteps)).
 cudaError_t launch_quantize_x(const LaunchCfg& c, const QGemvParams& p, uint8_t* xq);
+// out[i] = silu(gate[i]) * up[i] for i < n, as the fused GEMV forms its
+// activations (test hook and unfused path).
+cudaError_t launch_silu_mul(cudaStream_t s, long long n, const float* gate, const float* up, float* out);
 // y = x · Wᵀ. fast: K % 256 == 0 and w 16-byte aligned (ggml superblocks
 // stream as whole 16-byte units); otherwise the generic kernel.
 cudaError_t launch_gemv_q(const LaunchCfg& c, int fmt, QGemvParams p, bool fast, size_t* smem_used);

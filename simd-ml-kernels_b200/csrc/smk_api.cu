@@ -239,7 +239,7 @@ QPlan plan_q(smk_ctx* c, smk::LaunchCfg* l, smk_qformat fmt, int M, int N, int K
 
 smk_status run_q(smk_ctx* c, smk_qformat fmt, int M, int N, int K, const float* x, int64_t ldx, const uint8_t* Wq,
                  float* y, int64_t ldy, cudaStream_t s, int32_t* dump,
-                 const smk::GatherArgs* gather = nullptr) {
+                 const smk::GatherArgs* gather = nullptr, const float* up = nullptr, int64_t ldu = 0) {
     if (M == 0 || N == 0) return SMK_OK;
     if (K == 0) {
         for (int m = 0; m < M; ++m) SMK_CUDA(cudaMemsetAsync(y + (size_t)m * ldy, 0, (size_t)N * 4, s), "cudaMemsetAsync");
@@ -251,6 +251,7 @@ smk_status run_q(smk_ctx* c, smk_qformat fmt, int M, int N, int K, const float* 
         // scalar order), x quantized once into scratch by its own kernel.
         smk::QGemvParams p = {};
         p.x = x; p.ldx = ldx; p.w = Wq; p.y = y; p.ldy = ldy;
+        p.up = up; p.ldu = ldu;
         p.M = M; p.N = N; p.K = K; p.nb = K / 32;
         p.err = c->d_err;
         // x in shared memory when it fits beside at least 2 stages (K up to ~9K).
@@ -281,6 +282,8 @@ smk_status run_q(smk_ctx* c, smk_qformat fmt, int M, int N, int K, const float* 
     QPlan q = plan_q(c, &l, fmt, M, N, K, x, ldx, Wq, y, ldy, dump != nullptr);
     q.p.dump = dump;
     q.p.gather = gather;
+    q.p.up = up;
+    q.p.ldu = ldu;
     if (gather && !q.fast) return fail(SMK_ERR_ARGUMENT, "the fused gather needs K %% 256 == 0 and 16-byte aligned Wq");
     if (!q.x_in_smem) {
         uint8_t* xq;
@@ -552,6 +555,30 @@ smk_status smk_gemv_q_gather(smk_ctx* c, smk_gather* g, smk_qformat fmt, int M, 
     SMK_CUDA(smk::launch_gather_wait(l, g->dev, c->d_err), "gather wait launch");
     *y_full = reinterpret_cast<float*>(static_cast<char*>(g->base) + (g->steps & 1) * g->area_bytes);
     ++g->steps;
+    return SMK_OK;
+}
+
+smk_status smk_gemv_q_silu_mul(smk_ctx* c, smk_qformat fmt, int M, int N, int K, const float* gate, int64_t ldg,
+                               const float* up, int64_t ldu, const uint8_t* Wq, float* y, int64_t ldy, void* stream) {
+    if (!c) return fail(SMK_ERR_ARGUMENT, "ctx must not be NULL");
+    smk_status st = check_q_args(fmt, M, N, K);
+    if (st != SMK_OK) return st;
+    if (M == 0 || N == 0) return SMK_OK;
+    if (!y || (K > 0 && (!gate || !up || !Wq))) return fail(SMK_ERR_ARGUMENT, "gate, up, Wq and y must not be NULL");
+    if (ldy < N || (K > 0 && (ldg < K || ldu < K))) return fail(SMK_ERR_ARGUMENT, "ldg, ldu >= K and ldy >= N required");
+    DeviceGuard g(c->device);
+    if (!g.ok) return fail(SMK_ERR_CUDA, "cudaSetDevice(%d) failed", c->device);
+    return run_q(c, fmt, M, N, K, gate, ldg, Wq, y, ldy, static_cast<cudaStream_t>(stream), nullptr, nullptr, up, ldu);
+}
+
+smk_status smk_silu_mul(smk_ctx* c, int64_t n, const float* gate, const float* up, float* out, void* stream) {
+    if (!c) return fail(SMK_ERR_ARGUMENT, "ctx must not be NULL");
+    if (n < 0) return fail(SMK_ERR_ARGUMENT, "n must be >= 0");
+    if (n == 0) return SMK_OK;
+    if (!gate || !up || !out) return fail(SMK_ERR_ARGUMENT, "gate, up and out must not be NULL");
+    DeviceGuard g(c->device);
+    if (!g.ok) return fail(SMK_ERR_CUDA, "cudaSetDevice(%d) failed", c->device);
+    SMK_CUDA(smk::launch_silu_mul(static_cast<cudaStream_t>(stream), n, gate, up, out), "silu_mul launch");
     return SMK_OK;
 }
 

@@ -36,6 +36,8 @@ __all__ = [
     "gemv_q4_0_batch",
     "gemv_q8_0",
     "gemv_q8_0_batch",
+    "gemv_q4_0_silu_mul",
+    "gemv_q8_0_silu_mul",
     "get_num_threads",
     "library_path",
     "quantize_q4_0",
@@ -45,6 +47,7 @@ __all__ = [
     "sgemm",
     "sgemm_bf16",
     "sgemm_f16",
+    "silu_mul",
 ]
 
 
@@ -225,6 +228,49 @@ def gemv_q4_0_batch(x, Wq, N, K, *, out=None):
 
 def gemv_q8_0_batch(x, Wq, N, K, *, out=None):
     return _gemv("q8_0", _core.gemv_q8_0_batch, x, Wq, N, K, out, True)
+
+
+def _silu_mul_gemv(fmt, gate, up, Wq, N, K, out):
+    """The decode step's down projection, y = (silu(gate) * up) @ W.T, with the
+    SwiGLU product formed while x is quantized (CUDA tensors; gate and up [K]
+    or [M, K], M <= 8; asynchronous on the current stream)."""
+    t = _torch()
+    if not (_is_cuda_tensor(gate) and _is_cuda_tensor(up)):
+        raise ArgumentError("gate and up must be CUDA tensors")
+    if up.shape != gate.shape or up.dtype != gate.dtype or not up.is_contiguous():
+        raise ArgumentError("up must be a contiguous tensor of gate's shape and dtype")
+    batched = gate.dim() == 2
+    M = _check_dev_gemv(fmt, gate, Wq, N, K, out, batched)
+    if out is None:
+        out = t.empty((M, N) if batched else (N,), dtype=t.float32, device=gate.device)
+    index = gate.device.index if gate.device.index is not None else t.cuda.current_device()
+    _core._gemv_q_silu_mul_dev(0 if fmt == "q4_0" else 1, M, N, K, gate.data_ptr(), K, up.data_ptr(), K,
+                               Wq.data_ptr(), out.data_ptr(), N, _current_stream(index), index)
+    return out
+
+
+def gemv_q4_0_silu_mul(gate, up, Wq, N, K, *, out=None):
+    """y = (silu(gate) * up) @ W.T, W as quantize_q4_0 blocks: the reference
+    decoder's w_down(silu(w_gate(h)) * w_up(h)) after the gate/up GEMV, in one
+    kernel (silu(g) = g / (1 + exp(-g)))."""
+    return _silu_mul_gemv("q4_0", gate, up, Wq, N, K, out)
+
+
+def gemv_q8_0_silu_mul(gate, up, Wq, N, K, *, out=None):
+    return _silu_mul_gemv("q8_0", gate, up, Wq, N, K, out)
+
+
+def silu_mul(gate, up, *, out=None):
+    """silu(gate) * up on the device, the arithmetic gemv_*_silu_mul uses."""
+    t = _torch()
+    if not (_is_cuda_tensor(gate) and _is_cuda_tensor(up)) or gate.dtype != t.float32 or up.shape != gate.shape \
+            or up.dtype != t.float32 or not gate.is_contiguous() or not up.is_contiguous():
+        raise ArgumentError("gate and up must be contiguous float32 CUDA tensors of one shape")
+    if out is None:
+        out = t.empty_like(gate)
+    index = gate.device.index if gate.device.index is not None else t.cuda.current_device()
+    _core._silu_mul(gate.numel(), gate.data_ptr(), up.data_ptr(), out.data_ptr(), _current_stream(index), index)
+    return out
 
 
 def _quantize(core_fn, W, bpb, out):

@@ -264,6 +264,45 @@ def test_mma_rows_split_k(sk, torch, fmt, M, N, K):
     assert np.isnan(Y[M - 1]).all()
 
 
+def test_silu_mul_values(sk, torch):
+    """silu(g) * u on the device against the float64 definition, within the
+    reference's own SiLU tolerance 1e-35 + 1e-6·|ref| (its tests hold every
+    SiLU table to it), plus one rounding of the product; and the reference's
+    special values: silu(-inf) = NaN, silu(+inf) = +inf, x < -88 gives -0."""
+    rng = np.random.default_rng(3)
+    g = np.concatenate([rng.standard_normal(100000).astype(np.float32) * 8,
+                        np.array([0.0, -0.0, 1e-30, -1e-30, 88.0, -88.0, -100.0, 100.0, -1e4, 3.4e38, -3.4e38],
+                                 np.float32)])
+    u = rng.standard_normal(g.size).astype(np.float32)
+    got = sk.silu_mul(torch.from_numpy(g).cuda(), torch.from_numpy(u).cuda()).cpu().numpy().astype(np.float64)
+    g64 = g.astype(np.float64)
+    with np.errstate(over="ignore"):
+        want = g64 / (1.0 + np.exp(-g64)) * u.astype(np.float64)
+    assert (np.abs(got - want) <= 1e-35 + 1.2e-6 * np.abs(want)).all()
+    sp = np.array([-np.inf, np.inf, -90.0], np.float32)
+    r = sk.silu_mul(torch.from_numpy(sp).cuda(), torch.ones(3, device="cuda")).cpu().numpy()
+    assert np.isnan(r[0]) and r[1] == np.inf and r[2] == 0.0 and np.signbit(r[2])
+
+
+@pytest.mark.parametrize("fmt", ["q4_0", "q8_0"])
+@pytest.mark.parametrize("M,N,K", [(1, 2048, 8192), (1, 1000, 2048), (3, 517, 4096), (8, 64, 256), (2, 33, 160)])
+def test_gemv_silu_mul_equals_unfused(sk, torch, fmt, M, N, K):
+    """The fused down projection (SwiGLU product formed while quantizing x)
+    equals silu_mul followed by the plain GEMV bit for bit — fast, tensor-core
+    and generic kernels alike."""
+    rng = np.random.default_rng(M + N + K)
+    W = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    Wq = torch.from_numpy(O.quantize(fmt, W).ravel()).cuda()
+    g = torch.from_numpy((rng.standard_normal((M, K)) * 3).astype(np.float32)).cuda()
+    u = torch.from_numpy(rng.standard_normal((M, K)).astype(np.float32)).cuda()
+    fused = (sk.gemv_q4_0_silu_mul if fmt == "q4_0" else sk.gemv_q8_0_silu_mul)(g, u, Wq, N, K)
+    plain = (sk.gemv_q4_0_batch if fmt == "q4_0" else sk.gemv_q8_0_batch)(sk.silu_mul(g, u), Wq, N, K)
+    assert torch.equal(fused.view(torch.int32), plain.view(torch.int32))
+    fused1 = (sk.gemv_q4_0_silu_mul if fmt == "q4_0" else sk.gemv_q8_0_silu_mul)(g[0], u[0], Wq, N, K)
+    plain1 = (sk.gemv_q4_0 if fmt == "q4_0" else sk.gemv_q8_0)(sk.silu_mul(g[0], u[0]), Wq, N, K)
+    assert torch.equal(fused1.view(torch.int32), plain1.view(torch.int32))
+
+
 @pytest.mark.parametrize("fmt", ["q4_0", "q8_0"])
 def test_gemv_k0_and_n0(sk, fmt):
     fn = sk.gemv_q4_0 if fmt == "q4_0" else sk.gemv_q8_0
@@ -314,8 +353,8 @@ def test_gemv_deterministic_pdl_and_streams(sk, torch, fmt):
 @pytest.mark.parametrize("fmt", ["q4_0", "q8_0"])
 def test_launch_settings_bitwise_equal(sk, torch, fmt):
     """Outputs do not depend on the launch shape of the fast kernel (warps per
-    CTA, shared-memory stages per warp, CTAs per SM, programmatic dependent
-    launch): bitwise identical."""
+    CTA, shared-memory stages per warp, CTAs per SM, tile order, programmatic
+    dependent launch): bitwise identical."""
     from simd_ml_kernels import _core
     cases = [(28672, 8192), (8192, 2048), (1000, 28672), (300, 256)]
     ref = {}
@@ -327,23 +366,25 @@ def test_launch_settings_bitwise_equal(sk, torch, fmt):
     for key, y in base.items():
         y64, mag = O.ref64(fmt, ref[key][2], ref[key][3], *key)
         assert_gemv_close(y, y64, mag, key[1], f"{fmt} {key}")
-    settings = [(16, 2, 1, False), (8, 3, 1, True), (2, 8, 1, False), (4, 2, 2, True), (12, 1, 3, False)]
+    settings = [(16, 2, 1, False, 1), (8, 3, 1, True, 2), (2, 8, 1, False, 1), (4, 2, 2, True, 1),
+                (12, 1, 3, False, 2), (16, 1, 2, True, 1)]
     try:
-        for warps, stages, ctas, pdl in settings:
+        for warps, stages, ctas, pdl, order in settings:
             _core._ctx_set(2, warps)
             _core._ctx_set(3, stages)
             _core._ctx_set(4, ctas)
+            _core._ctx_set(5, order)
             sk.set_pdl(pdl)
             for key, v in ref.items():
                 fn = sk.gemv_q4_0 if fmt == "q4_0" else sk.gemv_q8_0
                 for _ in range(2):
                     got = fn(v[0], v[1], *key).cpu().numpy()
                     np.testing.assert_array_equal(got.view(np.uint32), base[key].view(np.uint32),
-                                                  err_msg=f"{fmt} {key} warps={warps} stages={stages} ctas={ctas}")
+                                                  err_msg=f"{fmt} {key} warps={warps} stages={stages} ctas={ctas} "
+                                                          f"order={order}")
     finally:
-        _core._ctx_set(2, 0)
-        _core._ctx_set(3, 0)
-        _core._ctx_set(4, 0)
+        for opt in (2, 3, 4, 5):
+            _core._ctx_set(opt, 0)
         sk.set_pdl(False)
 
 
