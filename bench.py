@@ -378,7 +378,7 @@ def gpu_bench(args, rank: int, world: int, local_rank: int) -> dict | None:
                      "frac": round(achieved / peaks["hbm_gbs"], 4),
                      "traffic": committed_traffic("gemv_q4_0_cfg0_traffic.json"),
                      "peak_source": peaks["source"] + " (MEASURED_PEAKS.json hbm_gbs, burst copy)",
-                     "kernel": "gemv_q_fast<Q4_0, M=1>", "algorithmic_bytes_per_launch": STEP_BYTES},
+                     "kernel": "gemv_q_fast2<Q4_0, M=1>", "algorithmic_bytes_per_launch": STEP_BYTES},
         "e2e": {"value": round(STEP_BYTES * world * e2e_steps / e2e_s / 1e9, 2), "unit": "GB/s",
                 "h2d_bytes_per_step": 4 * K_COLS, "d2h_bytes_per_step": e2e_bytes_out,
                 "us_per_step": e2e_s / e2e_steps * 1e6, "steps": e2e_steps,

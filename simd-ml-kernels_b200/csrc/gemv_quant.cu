@@ -299,6 +299,38 @@ __device__ __forceinline__ void superblock(const uint8_t* sp, const XPtr& xp, fl
 
 // ---- the fast kernel -----------------------------------------------------------------
 
+// The CTA that finishes last copies y from device memory into the mapped
+// page-locked output. Every SM that writes host memory has its writes flushed
+// over the bus before the kernel can complete; measured on a B200, one CTA
+// copying 32 KB after the others stored y in device memory ends about 1.6 µs
+// sooner than 296 CTAs each storing their rows into host memory. Every thread
+// of the CTA calls this once, after its last store of y.
+__device__ __forceinline__ void copy_y_to_host(const QGemvParams& p) {
+    __shared__ unsigned last;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();   // this CTA's rows of y before its ticket
+        last = atomicAdd(p.ticket, 1u) == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (!last) return;
+    __threadfence();   // every other CTA's rows, seen through their tickets
+    const size_t n = (size_t)p.N;
+    const bool vec = (n & 3) == 0 && (p.ldy & 3) == 0 && ((reinterpret_cast<uintptr_t>(p.y) | reinterpret_cast<uintptr_t>(p.yhost)) & 15) == 0;
+    for (int m = 0; m < p.M; ++m) {
+        const float* src = p.y + (size_t)m * p.ldy;
+        float* dst = p.yhost + (size_t)m * p.ldy;
+        if (vec) {
+            const float4* s4 = reinterpret_cast<const float4*>(src);
+            float4* d4 = reinterpret_cast<float4*>(dst);
+            for (size_t i = threadIdx.x; i < (n >> 2); i += blockDim.x) d4[i] = __ldcg(s4 + i);
+        } else {
+            for (size_t i = threadIdx.x; i < n; i += blockDim.x) dst[i] = __ldcg(src + i);
+        }
+    }
+    if (threadIdx.x == 0) *p.ticket = 0u;   // for the next launch, which the stream orders after this one
+}
+
 // Issue the bulk copies of one work item (tile, k-step ks) of this warp into stage `slot`.
 template <int F>
 __device__ __forceinline__ void issue_item(const QGemvParams& p, int tile, int ks, int slot, uint8_t* stages,
@@ -332,7 +364,7 @@ struct ItemCursor {
 };
 
 template <int F, int M, bool kXGlobal, bool kDump>
-__global__ void __launch_bounds__(512) gemv_q_fast(const QGemvParams p) {
+__device__ __forceinline__ void gemv_q_fast_body(const QGemvParams& p) {
     constexpr int SBB = sb_bytes(F);
     extern __shared__ __align__(128) uint8_t smem[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
@@ -410,7 +442,7 @@ __global__ void __launch_bounds__(512) gemv_q_fast(const QGemvParams p) {
                 c2.next(p, GW);
                 mbar_wait_bounded(&bars[c2.slot], c2.phase, nullptr);
             }
-            return;
+            break;
         }
         const int row = cur.tile * p.TR + r, sb = cur.ks * p.G + g;
         xp.xq = xb + ((size_t)cur.ks * 16 * 32 + g) * 16;
@@ -456,6 +488,19 @@ __global__ void __launch_bounds__(512) gemv_q_fast(const QGemvParams p) {
         }
         cur.next(p, GW);
     }
+    if (p.yhost) copy_y_to_host(p);   // every warp gets here, the ones that gave up too
+}
+
+template <int F, int M, bool kXGlobal, bool kDump>
+__global__ void __launch_bounds__(512) gemv_q_fast(const QGemvParams p) {
+    gemv_q_fast_body<F, M, kXGlobal, kDump>(p);
+}
+
+// Q4_0 with one or two rows runs two 512-thread CTAs per SM on small
+// matrices (the launch tuning): at most 64 registers a thread.
+template <int F, int M, bool kXGlobal, bool kDump>
+__global__ void __launch_bounds__(512, 2) gemv_q_fast2(const QGemvParams p) {
+    gemv_q_fast_body<F, M, kXGlobal, kDump>(p);
 }
 
 // One warp, after this rank's GEMV of the step: tell every peer that this
@@ -997,9 +1042,15 @@ cudaError_t launch(Kern kernel, dim3 grid, dim3 block, size_t smem, const Launch
 template <int F, int M>
 cudaError_t launch_fast_m(const LaunchCfg& c, const QGemvParams& p, size_t smem, bool dump) {
     void (*k)(QGemvParams);
-    if (p.xq) k = gemv_q_fast<F, M, true, false>;
-    else if (dump) k = gemv_q_fast<F, M, false, true>;
-    else k = gemv_q_fast<F, M, false, false>;
+    if constexpr (F == 0 && M <= 2) {
+        if (p.xq) k = gemv_q_fast2<F, M, true, false>;
+        else if (dump) k = gemv_q_fast<F, M, false, true>;
+        else k = gemv_q_fast2<F, M, false, false>;
+    } else {
+        if (p.xq) k = gemv_q_fast<F, M, true, false>;
+        else if (dump) k = gemv_q_fast<F, M, false, true>;
+        else k = gemv_q_fast<F, M, false, false>;
+    }
     int per_sm = 0;
     cudaError_t e = occupancy_cached((const void*)k, c.warps * 32, smem, &per_sm);
     if (e != cudaSuccess) return e;

@@ -56,6 +56,12 @@ struct QGemvParams {
     int contiguous;        // fast kernel: 1 = each CTA takes a contiguous range of tiles, 0 = tiles interleaved over CTAs
     int split;             // tensor-core kernel: K parts per 16-row tile (set by its launcher)
     const struct GatherArgs* gather;   // fused all-gather of y over peer GPUs, or nullptr (device copy)
+    // Fast kernel, y wanted in page-locked host memory: y goes to device
+    // memory as usual, and the CTA that finishes last (counted on *ticket,
+    // zero between launches) copies the M rows of N values to yhost (the
+    // buffer's device-mapped address, rows ldy apart like y). nullptr: off.
+    float* yhost;
+    unsigned* ticket;
     const uint8_t* xq;     // quantized x in global memory (nullptr: each CTA quantizes into shared memory)
     int32_t* dump;         // test-only: per-block integer sums [M, N, nb], or nullptr
     unsigned* err;         // device error word

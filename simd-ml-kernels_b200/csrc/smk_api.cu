@@ -156,6 +156,7 @@ struct smk_ctx {
     int tile_order = 0;             // 0 automatic, 1 interleaved, 2 contiguous
     unsigned* d_err = nullptr;      // device error word
     unsigned* d_reject = nullptr;   // quantizer rejection flag
+    unsigned* d_ticket = nullptr;   // finished-CTA count of a GEMV that copies y to host memory (zero between launches)
     std::mutex mu_scratch;                    // guards scratch and test_buf
     std::map<cudaStream_t, DevBuf> scratch;   // per-stream quantized-x scratch
     DevBuf test_buf;                          // test hooks
@@ -239,9 +240,15 @@ QPlan plan_q(smk_ctx* c, smk::LaunchCfg* l, smk_qformat fmt, int M, int N, int K
 
 smk_status run_q(smk_ctx* c, smk_qformat fmt, int M, int N, int K, const float* x, int64_t ldx, const uint8_t* Wq,
                  float* y, int64_t ldy, cudaStream_t s, int32_t* dump,
-                 const smk::GatherArgs* gather = nullptr, const float* up = nullptr, int64_t ldu = 0) {
+                 const smk::GatherArgs* gather = nullptr, const float* up = nullptr, int64_t ldu = 0,
+                 float* yhost = nullptr) {
+    // yhost: the device-mapped address of a page-locked output. The fast
+    // kernel then writes y (device memory, same ldy) and copies it there at
+    // its end; the other kernels write yhost directly.
     if (M == 0 || N == 0) return SMK_OK;
+    if (yhost && (gather || dump)) return fail(SMK_ERR_ARGUMENT, "internal: host output with a gather or dump");
     if (K == 0) {
+        if (yhost) y = yhost;
         for (int m = 0; m < M; ++m) SMK_CUDA(cudaMemsetAsync(y + (size_t)m * ldy, 0, (size_t)N * 4, s), "cudaMemsetAsync");
         return SMK_OK;
     }
@@ -250,7 +257,7 @@ smk_status run_q(smk_ctx* c, smk_qformat fmt, int M, int N, int K, const float* 
         // Several rows of x: integer tensor-core kernel (bitwise the reference's
         // scalar order), x quantized once into scratch by its own kernel.
         smk::QGemvParams p = {};
-        p.x = x; p.ldx = ldx; p.w = Wq; p.y = y; p.ldy = ldy;
+        p.x = x; p.ldx = ldx; p.w = Wq; p.y = yhost ? yhost : y; p.ldy = ldy;
         p.up = up; p.ldu = ldu;
         p.M = M; p.N = N; p.K = K; p.nb = K / 32;
         p.err = c->d_err;
@@ -284,6 +291,14 @@ smk_status run_q(smk_ctx* c, smk_qformat fmt, int M, int N, int K, const float* 
     q.p.gather = gather;
     q.p.up = up;
     q.p.ldu = ldu;
+    if (yhost) {
+        if (q.fast) {
+            q.p.yhost = yhost;
+            q.p.ticket = c->d_ticket;
+        } else {
+            q.p.y = yhost;
+        }
+    }
     if (gather && !q.fast) return fail(SMK_ERR_ARGUMENT, "the fused gather needs K %% 256 == 0 and 16-byte aligned Wq");
     if (!q.x_in_smem) {
         uint8_t* xq;
@@ -324,13 +339,14 @@ smk_status smk_ctx_create(int device, smk_ctx** out) {
     c->device = device;
     c->num_sms = prop.multiProcessorCount;
     c->smem_optin = prop.sharedMemPerBlockOptin;
-    cudaError_t e = cudaMalloc(&c->d_err, 2 * sizeof(unsigned));
+    cudaError_t e = cudaMalloc(&c->d_err, 4 * sizeof(unsigned));
     if (e != cudaSuccess) {
         delete c;
         return cuda_fail(e, "cudaMalloc (error word)");
     }
     c->d_reject = c->d_err + 1;
-    e = cudaMemset(c->d_err, 0, 2 * sizeof(unsigned));
+    c->d_ticket = c->d_err + 2;
+    e = cudaMemset(c->d_err, 0, 4 * sizeof(unsigned));
     if (e != cudaSuccess) {
         cudaFree(c->d_err);
         delete c;
@@ -602,11 +618,12 @@ smk_status smk_gemv_q_host(smk_ctx* c, smk_qformat fmt, int M, int N, int K, con
     const size_t xb = (size_t)M * K * 4, wb = (size_t)N * (K / 32) * smk::block_bytes(fmt), yb = (size_t)M * N * 4;
     // Host activations reach the device by one DMA copy (from page-locked
     // memory: the caller's, or this context's page-locked buffer for a
-    // pageable array); reading them in place over the bus is slower. Host
-    // outputs are written by the GEMV straight into page-locked memory
-    // (mapped into the device's address space under unified addressing),
-    // which costs less than a copy back. Weights in host memory are copied
-    // to the device (device-resident weights are the fast path).
+    // pageable array); reading them in the kernel over the bus costs the same.
+    // Host outputs are written by the GEMV into page-locked memory (mapped
+    // into the device's address space under unified addressing), which costs
+    // less than a copy back; the fast kernel does it from one CTA at its end.
+    // Weights in host memory are copied to the device (device-resident
+    // weights are the fast path).
     void *xmap = nullptr, *wmap = nullptr, *ymap = nullptr;
     const Mem xk = K > 0 ? mem_kind(x, &xmap) : Mem::kDevice;
     const Mem wk = K > 0 ? mem_kind(Wq, &wmap) : Mem::kDevice;
@@ -617,8 +634,9 @@ smk_status smk_gemv_q_host(smk_ctx* c, smk_qformat fmt, int M, int N, int K, con
     if (px + py) SMK_CUDA(c->pinned.reserve(px + py), "cudaHostAlloc (staging)");
     char* pin = static_cast<char*>(c->pinned.ptr);
     const size_t dxo = 0, dwo = xk != Mem::kDevice ? align256(xb) : 0;
-    const size_t dev_bytes = dwo + (wk != Mem::kDevice ? wb : 0);
-    if (dev_bytes) SMK_CUDA(c->staging.reserve(dev_bytes), "cudaMalloc (staging)");
+    const size_t dyo = dwo + (wk != Mem::kDevice ? align256(wb) : 0);   // device copy of y (see run_q)
+    const size_t dev_bytes = dyo + align256(yb);
+    SMK_CUDA(c->staging.reserve(dev_bytes), "cudaMalloc (staging)");
     char* dst = static_cast<char*>(c->staging.ptr);
     const float* dx = x;
     if (xk != Mem::kDevice) {
@@ -636,13 +654,15 @@ smk_status smk_gemv_q_host(smk_ctx* c, smk_qformat fmt, int M, int N, int K, con
         dw = reinterpret_cast<const uint8_t*>(dst + dwo);
     }
     float* dy = y;
-    if (yk == Mem::kPinned) dy = static_cast<float*>(ymap);
+    float* yhost = nullptr;
+    if (yk == Mem::kPinned) yhost = static_cast<float*>(ymap);
     if (yk == Mem::kPageable) {
         void* dm = nullptr;
         SMK_CUDA(cudaHostGetDevicePointer(&dm, pin + px, 0), "cudaHostGetDevicePointer");
-        dy = static_cast<float*>(dm);
+        yhost = static_cast<float*>(dm);
     }
-    st = run_q(c, fmt, M, N, K, dx, K, dw, dy, N, s, nullptr);
+    if (yhost) dy = reinterpret_cast<float*>(dst + dyo);
+    st = run_q(c, fmt, M, N, K, dx, K, dw, dy, N, s, nullptr, nullptr, nullptr, 0, yhost);
     if (st != SMK_OK) return st;
     SMK_CUDA(cudaStreamSynchronize(s), "cudaStreamSynchronize");
     if (yk == Mem::kPageable) std::memcpy(y, pin + px, yb);

@@ -470,6 +470,33 @@ def test_host_io_paths_bitwise_equal(sk, torch, fmt):
         fn(x[:-32], wd, N, K)
 
 
+@pytest.mark.parametrize("N,K", [(1003, 2048), (8192, 2048), (517, 2080), (4096, 4096)])
+def test_host_output_copy_bitwise_equal(sk, torch, N, K):
+    """Host outputs from the fast kernel are copied to page-locked memory by
+    the CTA that finishes last: odd N and a page-locked output 4 bytes off a
+    16-byte boundary take its scalar copy, one and two rows the fast kernel,
+    three rows the tensor-core kernel and K % 256 != 0 the generic kernel
+    (both write host memory directly). Each agrees bitwise with the
+    all-device call, over repeated calls (the finish counter starts from zero
+    each launch)."""
+    x, Wq = make_case(77, N, K, "q4_0")
+    wd = torch.from_numpy(Wq.ravel()).cuda()
+    X = np.stack([x, -0.5 * x, 0.25 * x])
+    for M in (1, 2, 3):
+        want = sk.gemv_q4_0_batch(torch.from_numpy(X[:M]).cuda(), wd, N, K).cpu().numpy()
+        pool = torch.empty(M * N + 8).pin_memory().numpy()
+        for off in (0, 1, 4):
+            out = pool[off:off + M * N].reshape(M, N)
+            for rep in range(3):
+                out[:] = np.nan
+                sk.gemv_q4_0_batch(X[:M], wd, N, K, out=out)
+                np.testing.assert_array_equal(out.view(np.uint32), want.view(np.uint32))
+        y1 = sk.gemv_q4_0_batch(X[:M], wd, N, K)
+        np.testing.assert_array_equal(y1.view(np.uint32), want.view(np.uint32))
+    from simd_ml_kernels import _core
+    assert _core._device_error(0) == 0
+
+
 def test_row_shards_bitwise_equal_full(sk, torch):
     """Row-sharding (the multi-GPU plan, 8-row groups as the reference's
     gemv_slice): every shard's outputs bitwise equal the unsharded call."""
