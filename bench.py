@@ -350,7 +350,8 @@ def gpu_bench(args, rank: int, world: int, local_rank: int) -> dict | None:
             extra["sharded_config4"] = sharded
     if rank == 0 and world == 1:
         extra["llama_stack"] = llama_stack(sk, torch, dev, stream, args)
-        extra["llama_decode_swiglu"] = llama_stack(sk, torch, dev, stream, args, swiglu=True)
+        extra["llama_decode_swiglu"] = llama_stack(sk, torch, dev, stream, args, swiglu="fused")
+        extra["llama_decode_swiglu_unfused"] = llama_stack(sk, torch, dev, stream, args, swiglu="unfused")
         if args.all or args.case:
             extra["configs"] = other_configs(sk, torch, dev, stream, args.case)
 
@@ -393,7 +394,7 @@ def gpu_bench(args, rank: int, world: int, local_rank: int) -> dict | None:
     return out
 
 
-def llama_stack(sk, torch, dev, stream, args, swiglu: bool = False) -> dict:
+def llama_stack(sk, torch, dev, stream, args, swiglu: str = "") -> dict:
     """a Llama-3.2-1B decode step's GEMVs — 16 layers of
     q 2048->2048, k, v 2048->512, o 2048->2048, gate, up 2048->8192, down
     8192->2048, and the tied 2048->128256 LM head — on random-init Q4_0 weights
@@ -401,9 +402,11 @@ def llama_stack(sk, torch, dev, stream, args, swiglu: bool = False) -> dict:
     q, k and v read the same activation row within a step, as do gate and up,
     so each group runs as one GEMV over its concatenated rows (the same bytes
     and outputs as the separate GEMVs): 4 GEMVs per layer + the LM head.
-    swiglu: the down projection reads silu(gate) * up of the layer's gate/up
-    GEMV instead of fresh activations, as the decoder does, with the SwiGLU
-    product formed inside it (more work than the GEMV-only stack)."""
+    swiglu "fused": the down projection reads silu(gate) * up of the layer's
+    gate/up GEMV instead of fresh activations, as the decoder does, with the
+    SwiGLU product formed inside it (more work than the GEMV-only stack);
+    "unfused": the same step with silu_mul as its own kernel before a plain
+    down-projection GEMV."""
     g = torch.Generator(device=dev)
     g.manual_seed(2)
     groups = []   # (rows N, K, logical GEMVs)
@@ -423,6 +426,7 @@ def llama_stack(sk, torch, dev, stream, args, swiglu: bool = False) -> dict:
     ys_per_tok = sum(n for n, _, _ in groups)
     X = torch.randn((LLAMA_TOKENS, xs_per_tok), generator=g, device=dev)
     Y = torch.empty((ys_per_tok,), device=dev)
+    act = torch.empty((8192,), device=dev)
     gr = torch.cuda.CUDAGraph()
     with torch.cuda.stream(stream):
         with torch.cuda.graph(gr, stream=stream):
@@ -433,7 +437,11 @@ def llama_stack(sk, torch, dev, stream, args, swiglu: bool = False) -> dict:
                     if swiglu and gate_up is not None and n == 2048 and k == 8192:
                         # The down projection takes silu(gate) * up of the gate/up GEMV just
                         # before it, formed while its activations are quantized.
-                        sk.gemv_q4_0_silu_mul(gate_up[:8192], gate_up[8192:], wq, n, k, out=Y[yo:yo + n])
+                        if swiglu == "fused":
+                            sk.gemv_q4_0_silu_mul(gate_up[:8192], gate_up[8192:], wq, n, k, out=Y[yo:yo + n])
+                        else:
+                            sk.silu_mul(gate_up[:8192], gate_up[8192:], out=act)
+                            sk.gemv_q4_0(act, wq, n, k, out=Y[yo:yo + n])
                         gate_up = None
                     else:
                         sk.gemv_q4_0(X[t, xo:xo + k], wq, n, k, out=Y[yo:yo + n])
@@ -455,12 +463,13 @@ def llama_stack(sk, torch, dev, stream, args, swiglu: bool = False) -> dict:
     tok_bytes = wbytes + 4 * (logical_x + ys_per_tok)
     del gr
     return {"tok_s": round(1e3 / per_tok_ms, 1), "ms_per_token": per_tok_ms,
-            "gemvs_per_token": sum(c for _, _, c in groups), "launches_per_token": len(groups),
+            "gemvs_per_token": sum(c for _, _, c in groups),
+            "launches_per_token": len(groups) + (LLAMA_LAYERS if swiglu == "unfused" else 0),
             "bytes_per_token": tok_bytes, "gb_s": round(tok_bytes / (per_tok_ms * 1e-3) / 1e9, 1),
             "tokens": LLAMA_TOKENS,
             "launch": "one CUDA graph of 128 decode steps, PDL; q/k/v and gate/up as fused row groups"
-                      + ("; down projection fed by silu(gate)*up inside its activation quantization" if swiglu
-                         else "")}
+                      + {"": "", "fused": "; down projection fed by silu(gate)*up inside its activation quantization",
+                         "unfused": "; silu(gate)*up as a separate kernel before the down projection"}[swiglu]}
 
 
 SHARDED_SHAPES = [(28672, 8192), (8192, 28672), (128256, 8192)]   # config 4: 70B layers, LM head
