@@ -398,7 +398,8 @@ def llama_stack(sk, torch, dev, stream, args, swiglu: str = "") -> dict:
     """a Llama-3.2-1B decode step's GEMVs — 16 layers of
     q 2048->2048, k, v 2048->512, o 2048->2048, gate, up 2048->8192, down
     8192->2048, and the tied 2048->128256 LM head — on random-init Q4_0 weights
-    (seed 2), fresh activations every step, 128 steps in one CUDA graph.
+    (seed 2), fresh activations every step, --llama-tokens (128) steps in one
+    CUDA graph.
     q, k and v read the same activation row within a step, as do gate and up,
     so each group runs as one GEMV over its concatenated rows (the same bytes
     and outputs as the separate GEMVs): 4 GEMVs per layer + the LM head.
@@ -424,13 +425,14 @@ def llama_stack(sk, torch, dev, stream, args, swiglu: str = "") -> dict:
         wbytes += wq.numel()
     xs_per_tok = sum(k for _, k, _ in groups)
     ys_per_tok = sum(n for n, _, _ in groups)
-    X = torch.randn((LLAMA_TOKENS, xs_per_tok), generator=g, device=dev)
+    tokens = args.llama_tokens
+    X = torch.randn((tokens, xs_per_tok), generator=g, device=dev)
     Y = torch.empty((ys_per_tok,), device=dev)
     act = torch.empty((8192,), device=dev)
     gr = torch.cuda.CUDAGraph()
     with torch.cuda.stream(stream):
         with torch.cuda.graph(gr, stream=stream):
-            for t in range(LLAMA_TOKENS):
+            for t in range(tokens):
                 xo = yo = 0
                 gate_up = None
                 for (n, k, _), wq in zip(groups, weights):
@@ -457,7 +459,7 @@ def llama_stack(sk, torch, dev, stream, args, swiglu: str = "") -> dict:
         e.record(stream)
     torch.cuda.synchronize(dev)
     ms = s.elapsed_time(e)
-    per_tok_ms = ms / LLAMA_TOKENS
+    per_tok_ms = ms / tokens
     # Algorithmic bytes of the 113 separate GEMVs: weights, x of each, y of each.
     logical_x = sum(k * c for _, k, c in groups)
     tok_bytes = wbytes + 4 * (logical_x + ys_per_tok)
@@ -466,8 +468,8 @@ def llama_stack(sk, torch, dev, stream, args, swiglu: str = "") -> dict:
             "gemvs_per_token": sum(c for _, _, c in groups),
             "launches_per_token": len(groups) + (LLAMA_LAYERS if swiglu == "unfused" else 0),
             "bytes_per_token": tok_bytes, "gb_s": round(tok_bytes / (per_tok_ms * 1e-3) / 1e9, 1),
-            "tokens": LLAMA_TOKENS,
-            "launch": "one CUDA graph of 128 decode steps, PDL; q/k/v and gate/up as fused row groups"
+            "tokens": tokens,
+            "launch": f"one CUDA graph of {tokens} decode steps, PDL; q/k/v and gate/up as fused row groups"
                       + {"": "", "fused": "; down projection fed by silu(gate)*up inside its activation quantization",
                          "unfused": "; silu(gate)*up as a separate kernel before the down projection"}[swiglu]}
 
@@ -596,6 +598,17 @@ def other_configs(sk, torch, dev, stream, only: str | None = None) -> dict:
                 run(f"dense {str(wt).split('.')[-1]} M={m} N={n} K={k}",
                     lambda: (torch.randn((n, k), generator=g, device=dev) * 0.02).to(wt),
                     lambda w: sk.gemv_dense(x, w, out=y), n * k * es + 4 * m * k + 4 * m * n)
+    g.manual_seed(5)
+    for m in (1, 4, 8):   # INT8 sgemm_u8s8 with trans_b: uint8 A, int8 W [N, K], per-row scales
+        for n in (4096, 14336):
+            k = 4096
+            a = torch.randint(0, 256, (m, k), generator=g, device=dev, dtype=torch.uint8)
+            sc = torch.rand(n, generator=g, device=dev) * 0.01
+            y = torch.empty((m, n), device=dev)
+            run(f"u8s8 M={m} N={n} K={k}",
+                lambda n=n, k=k: torch.randint(-128, 128, (n, k), generator=g, device=dev, dtype=torch.int8),
+                lambda w, a=a, sc=sc, y=y: sk.sgemm_u8s8(a, w, 0.02, 128, sc, y, trans_b=True),
+                n * k + m * k + 4 * n + 4 * m * n)
     g.manual_seed(4)
     for n, k in ((28672, 8192), (8192, 28672), (128256, 8192)):
         for m in (1, 8):
@@ -626,6 +639,8 @@ def main() -> None:
                     help="N > 1: all-gather of y fused into the GEMV over NVLink, or NCCL's all-gather")
     ap.add_argument("--case", default=None,
                     help="time only the config 1/3/4 cases whose label contains this text (after the config-0 line)")
+    ap.add_argument("--llama-tokens", type=int, default=LLAMA_TOKENS,
+                    help="decode steps per Llama-stack CUDA graph (fewer: shorter profiler launch lists)")
     ap.add_argument("--only-gemv", action="store_true",
                     help="time the config-0 GEMV only (no e2e, Llama stack or CPU baseline): for profilers")
     args = ap.parse_args()

@@ -127,6 +127,22 @@ smk_status smk_gemv_dense(smk_ctx* ctx, smk_dtype w_type, smk_dtype x_type, int 
 smk_status smk_gemv_dense_host(smk_ctx* ctx, smk_dtype w_type, smk_dtype x_type, int M, int N, int K, float alpha,
                                const void* X, const void* W, float beta, float* C);
 
+/* ---- INT8 decode GEMV (replaces GemmU8S8Fn with trans_b = true, M <= 8:
+ * src/dispatch/kernels.hpp:47,69; the M = 1 row path
+ * src/kernels/gemm/int8_rows.hpp) ----
+ * C[i][j] = a_scale·b_scales[j]·Σ_k (A[i][k] − a_zero_point)·W[j][k];
+ * A uint8 [M, lda], W int8 [N, ldw] (the nn.Linear layout), b_scales [N],
+ * C float32 [M, ldc] (overwritten). The sums are exact and C is the
+ * reference's scalar-table value float(double(a_scale)·b_scales[j]·sum)
+ * (src/kernels/scalar_kernels.cpp:148-170). a_zero_point in [0, 255],
+ * a_scale finite. Device pointers, asynchronous on `stream`. */
+smk_status smk_gemv_u8s8(smk_ctx* ctx, int M, int N, int K, const uint8_t* A, int64_t lda, int a_zero_point,
+                         const int8_t* W, int64_t ldw, float a_scale, const float* b_scales, float* C, int64_t ldc,
+                         void* stream);
+/* Host-or-device pointers, contiguous operands, synchronous. */
+smk_status smk_gemv_u8s8_host(smk_ctx* ctx, int M, int N, int K, const uint8_t* A, int a_zero_point, const int8_t* W,
+                              float a_scale, const float* b_scales, float* C);
+
 /* ---- weight quantization on the device (replaces quantize_q4_0_rows / quantize_q8_0_rows) ----
  * W [rows, K] fp32 -> rows·K/32 blocks, byte-identical to ggml's
  * quantize_row_q4_0_ref / quantize_row_q8_0_ref. Synchronous (the rejection

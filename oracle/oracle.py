@@ -64,6 +64,8 @@ def lib() -> ctypes.CDLL:
         L.smko_dense_ref64.argtypes = [_I, _I, _I, _P, _I, _P, _I, _P, _P]
         L.smko_dense_scalar.argtypes = [_I, _I, _I, _F, _P, _I, _P, _I, _F, _P]
         L.smko_gemv_slice.argtypes = [_I, _I, _I, ctypes.POINTER(_I), ctypes.POINTER(_I)]
+        L.smko_sgemm_u8s8.argtypes = [_I, _I, _I, _I, _P, _I, _I, _P, _I, _F, _P, _P, _I]
+        L.smko_u8s8_ref64.argtypes = [_I, _I, _I, _I, _P, _I, _P, _P, _P]
         _lib = L
     return _lib
 
@@ -172,6 +174,33 @@ def gemv_slice(N: int, t: int, parts: int) -> tuple[int, int]:
     return lo.value, hi.value
 
 
+def _u8s8_shapes(A, B, trans_b):
+    A = np.ascontiguousarray(A, np.uint8)
+    B = np.ascontiguousarray(B, np.int8)
+    M, K = A.shape
+    N = B.shape[0] if trans_b else B.shape[1]
+    return A, B, M, N, K
+
+
+def sgemm_u8s8(A, B, a_scale, a_zero_point, b_scales, trans_b=False) -> np.ndarray:
+    """The reference's scalar-table sgemm_u8s8 (exact int64 sums, one double epilogue)."""
+    A, B, M, N, K = _u8s8_shapes(A, B, trans_b)
+    bs = np.ascontiguousarray(b_scales, np.float32)
+    C = np.zeros((M, N), np.float32)
+    lib().smko_sgemm_u8s8(int(trans_b), M, N, K, _ptr(A), K, int(a_zero_point), _ptr(B), B.shape[1],
+                          float(a_scale), _ptr(bs), _ptr(C), N)
+    return C
+
+
+def u8s8_ref64(A, B, a_zero_point, trans_b=False) -> tuple[np.ndarray, np.ndarray]:
+    """Exact Σ (A − zp)·op(B) and the bound's Σ |A − zp|·|op(B)|, as float64 [M, N]."""
+    A, B, M, N, K = _u8s8_shapes(A, B, trans_b)
+    s64 = np.zeros((M, N), np.float64)
+    mag = np.zeros((M, N), np.float64)
+    lib().smko_u8s8_ref64(int(trans_b), M, N, K, _ptr(A), int(a_zero_point), _ptr(B), _ptr(s64), _ptr(mag))
+    return s64, mag
+
+
 def bf16_bits(x: np.ndarray) -> np.ndarray:
     """float32 -> bfloat16 bit patterns, round to nearest even (tests/test_precision.py:196-198)."""
     u = np.ascontiguousarray(x, np.float32).view(np.uint32).astype(np.uint64)
@@ -208,6 +237,8 @@ def ref() -> ctypes.CDLL:
         R.smkref_sgemm_tb.argtypes = [_I, _I, _I, _I, _F, _P, _P, _F, _P]
         R.smkref_sgemm_f16_tb.argtypes = [_I, _I, _I, _I, _F, _P, _P, _F, _P]
         R.smkref_sgemm_bf16_tb.argtypes = [_I, _I, _I, _I, _F, _P, _P, _F, _P]
+        R.smkref_sgemm_u8s8.argtypes = [_I, _I, _I, _I, _I, _P, _I, _P, _F, _P, _P]
+        R.smkref_u8s8_path.restype = ctypes.c_char_p
         _ref = R
     return _ref
 
@@ -226,3 +257,13 @@ def ref_quantize(fmt: str, W: np.ndarray) -> np.ndarray | None:
     out = np.zeros(W.shape[:-1] + (K // 32 * BLOCK_BYTES[fmt],), np.uint8)
     fn = ref().smkref_quantize_q4_0 if fmt == "q4_0" else ref().smkref_quantize_q8_0
     return out if (rows == 0 or fn(_ptr(W), rows, K, _ptr(out))) else None
+
+
+def ref_sgemm_u8s8(A, B, a_scale, a_zero_point, b_scales, trans_b=False, isa: int = -1) -> np.ndarray:
+    """The reference's own sgemm_u8s8 (table `isa`: -1 this CPU's, 0 scalar)."""
+    A, B, M, N, K = _u8s8_shapes(A, B, trans_b)
+    bs = np.ascontiguousarray(b_scales, np.float32)
+    C = np.zeros((M, N), np.float32)
+    ref().smkref_sgemm_u8s8(isa, int(trans_b), M, N, K, _ptr(A), int(a_zero_point), _ptr(B), float(a_scale),
+                            _ptr(bs), _ptr(C))
+    return C

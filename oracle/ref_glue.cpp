@@ -13,11 +13,13 @@
 //   quant::quantize_q8_0_rows            src/kernels/quant/q8_0.hpp:58
 //   quant::quantize_x_q8                 src/kernels/quant/q8_0.hpp:64
 //   kernels().sgemm / sgemm_f16 / _bf16  src/dispatch/kernels.hpp:66-68 (trans_b, x·Wᵀ)
+//   kernels().sgemm_u8s8, gemm::u8s8_path src/dispatch/kernels.hpp:47,69, src/kernels/gemm/int8_gemm.hpp:41
 //   gemm::set_num_threads                src/kernels/gemm/avx2_gemm_packed.hpp:94
 //   use_kernels / kernels_for            src/dispatch/kernels.hpp:91,98
 
 #include "dispatch/kernels.hpp"
 #include "kernels/gemm/avx2_gemm_packed.hpp"
+#include "kernels/gemm/int8_gemm.hpp"
 #include "kernels/quant/q4_0.hpp"
 #include "kernels/quant/q8_0.hpp"
 
@@ -71,5 +73,12 @@ void smkref_sgemm_bf16_tb(int isa, int M, int N, int K, float alpha, const std::
                           const std::uint16_t* B, float beta, float* C) {
     table(isa).sgemm_bf16(true, M, N, K, alpha, A, K, B, K, beta, C, N);
 }
+
+// C [M, N] = a_scale·b_scales[j]·Σ_k (A − zp)·op(B); A [M, K]; B [N, K] (trans_b) or [K, N].
+void smkref_sgemm_u8s8(int isa, int trans_b, int M, int N, int K, const std::uint8_t* A, int a_zero_point,
+                       const std::int8_t* B, float a_scale, const float* b_scales, float* C) {
+    table(isa).sgemm_u8s8(trans_b != 0, M, N, K, A, K, a_zero_point, B, trans_b ? K : N, a_scale, b_scales, C, N);
+}
+const char* smkref_u8s8_path(void) { return simd_ml::gemm::u8s8_path(); }
 
 }  // extern "C"

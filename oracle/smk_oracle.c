@@ -303,3 +303,39 @@ void smko_gemv_slice(int N, int t, int parts, int* lo, int* hi) {
     *lo = (int)(a < N ? a : N);
     *hi = (int)(b < N ? b : N);
 }
+
+/* B element (row k, column j) of op(B). */
+static int64_t u8s8_b(int trans_b, const int8_t* B, int ldb, int k, int j) {
+    return trans_b ? (int64_t)B[(int64_t)j * ldb + k] : (int64_t)B[(int64_t)k * ldb + j];
+}
+
+void smko_sgemm_u8s8(int trans_b, int M, int N, int K, const uint8_t* A, int lda, int a_zero_point,
+                     const int8_t* B, int ldb, float a_scale, const float* b_scales, float* C, int ldc) {
+    if (M <= 0 || N <= 0 || K < 0) return;
+#pragma omp parallel for schedule(static) collapse(2)
+    for (int i = 0; i < M; ++i)
+        for (int j = 0; j < N; ++j) {
+            int64_t acc = 0;
+            for (int k = 0; k < K; ++k)
+                acc += ((int64_t)A[(int64_t)i * lda + k] - a_zero_point) * u8s8_b(trans_b, B, ldb, k, j);
+            const double s = (double)a_scale * (double)b_scales[j];   /* exact: two 24-bit significands */
+            C[(int64_t)i * ldc + j] = (float)(s * (double)acc);
+        }
+}
+
+void smko_u8s8_ref64(int trans_b, int M, int N, int K, const uint8_t* A, int a_zero_point, const int8_t* B,
+                     double* sum64, double* mag) {
+    const int ldb = trans_b ? K : N;
+#pragma omp parallel for schedule(static) collapse(2)
+    for (int i = 0; i < M; ++i)
+        for (int j = 0; j < N; ++j) {
+            int64_t acc = 0, m = 0;
+            for (int k = 0; k < K; ++k) {
+                const int64_t a = (int64_t)A[(int64_t)i * K + k] - a_zero_point, b = u8s8_b(trans_b, B, ldb, k, j);
+                acc += a * b;
+                m += (a < 0 ? -a : a) * (b < 0 ? -b : b);
+            }
+            sum64[(int64_t)i * N + j] = (double)acc;
+            mag[(int64_t)i * N + j] = (double)m;
+        }
+}

@@ -68,6 +68,17 @@ void smko_dense_ref64(int M, int N, int K, const void* A, int a_kind, const void
 void smko_dense_scalar(int M, int N, int K, float alpha, const void* A, int a_kind, const void* B, int b_kind,
                        float beta, float* C);
 
+/* sgemm_u8s8 as the reference's scalar table (src/kernels/scalar_kernels.cpp:148-170,
+ * contract src/kernels/gemm/int8_gemm.hpp:5-26): acc[i][j] = Σ_k (A[i][k] − zp)·op(B)[k][j]
+ * exactly in int64, then C[i][j] = float(double(a_scale)·b_scales[j]·double(acc)).
+ * trans_b: B [N, ldb] (ldb ≥ K); else B [K, ldb] (ldb ≥ N). A [M, lda], C [M, ldc]. */
+void smko_sgemm_u8s8(int trans_b, int M, int N, int K, const uint8_t* A, int lda, int a_zero_point,
+                     const int8_t* B, int ldb, float a_scale, const float* b_scales, float* C, int ldc);
+/* The exact sums and the magnitude of the documented bound,
+ * Σ_k |A − zp|·|op(B)| (int8_gemm.hpp:23-24), both in float64 (exact below 2^53). */
+void smko_u8s8_ref64(int trans_b, int M, int N, int K, const uint8_t* A, int a_zero_point, const int8_t* B,
+                     double* sum64, double* mag);
+
 /* Row slice [lo, hi) of part t of `parts` in whole 8-row groups
  * (src/dispatch/dispatch.cpp:373-379, kGemvRowGroup = 8). */
 void smko_gemv_slice(int N, int t, int parts, int* lo, int* hi);

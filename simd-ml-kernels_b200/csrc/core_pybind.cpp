@@ -16,6 +16,7 @@
 
 #include <cstdint>
 #include <cstring>
+#include <cmath>
 #include <limits>
 #include <mutex>
 #include <stdexcept>
@@ -394,6 +395,74 @@ void decode_shape(const Arr& A, const Arr& B, bool trans_a, bool trans_b, int* M
     *K = (int)k;
 }
 
+// ---- INT8 decode GEMV: sgemm_u8s8 with trans_b (pybind_entry.cpp:837-893) ----
+
+const char* kDecodeOnlyU8S8 =
+    "this build implements the INT8 decode GEMV on the B200: sgemm_u8s8 with trans_b=True (B as [N, K]) "
+    "and at most 8 rows of A";
+
+py::object py_sgemm_u8s8(const py::handle& Ah, const py::handle& Bh, float a_scale, int a_zero_point,
+                         const py::handle& Sh, const py::object& C, bool trans_b, const py::object& stream) {
+    // The reference's checks, in its order and with its messages (pybind_entry.cpp:849-876).
+    const Arr A = as_arr(Ah), B = as_arr(Bh), S = as_arr(Sh);
+    if (A.kind != 'u' || A.itemsize != 1) throw DTypeError("A must be uint8 (quantized activations; dtype=np.uint8)");
+    if (B.kind != 'i' || B.itemsize != 1) throw DTypeError("B must be int8 (quantized weights; dtype=np.int8)");
+    check_float32(S, "b_scales");
+    if (A.ndim() != 2) throw ArgumentError("A must be 2-D");
+    if (B.ndim() != 2) throw ArgumentError("B must be 2-D");
+    if (S.ndim() != 1) throw ArgumentError("b_scales must be 1-D (one scale per output column)");
+    check_contiguous(A, "A");
+    check_contiguous(B, "B");
+    check_contiguous(S, "b_scales");
+    if (a_zero_point < 0 || a_zero_point > 255)
+        throw ArgumentError("a_zero_point must be in [0, 255] (got " + std::to_string(a_zero_point) + ")");
+    if (!std::isfinite(a_scale)) throw ArgumentError("a_scale must be finite");
+    const int64_t M = A.shape[0], K = A.shape[1];
+    const int64_t N = B.shape[trans_b ? 0 : 1], Kb = B.shape[trans_b ? 1 : 0];
+    if (Kb != K)
+        throw ArgumentError("Shape mismatch: A is [" + std::to_string(M) + "×" + std::to_string(K) + "] but " +
+                            (trans_b ? "B.T" : "B") + " is [" + std::to_string(Kb) + "×" + std::to_string(N) + "]");
+    if (S.shape[0] != N)
+        throw ArgumentError("b_scales must have N = " + std::to_string(N) + " elements (got " +
+                            std::to_string(S.shape[0]) + ")");
+    // With no elements the layout of B does not matter; otherwise the decode contract.
+    if (M * N * K != 0 && (!trans_b || M > 8)) throw ArgumentError(kDecodeOnlyU8S8);
+    if (N > std::numeric_limits<int>::max() || K > std::numeric_limits<int>::max())
+        throw ArgumentError("N or K is too large");
+    py::object result;
+    float* cp;
+    bool c_device = false;
+    if (C.is_none()) {
+        if (A.device) throw ArgumentError("C is required when A is a CUDA array");
+        py::array_t<float> out = result_array({(py::ssize_t)M, (py::ssize_t)N});
+        cp = out.mutable_data();
+        result = out;
+    } else {
+        Arr ci;
+        output_matrix(C, M, N, &ci);
+        cp = static_cast<float*>(ci.ptr);
+        c_device = ci.device;
+        result = C;
+    }
+    if (M * N == 0) return result;
+    smk_ctx* c = ctx_for(A.device ? A.device_id : (B.device ? B.device_id : current_device_hint));
+    const bool async = A.device && B.device && S.device && c_device && !stream.is_none();
+    void* strm = async ? reinterpret_cast<void*>(stream.cast<uintptr_t>()) : nullptr;   // read with the GIL held
+    smk_status st;
+    {
+        py::gil_scoped_release release;
+        if (async)
+            st = smk_gemv_u8s8(c, (int)M, (int)N, (int)K, static_cast<const uint8_t*>(A.ptr), K, a_zero_point,
+                               static_cast<const int8_t*>(B.ptr), K, a_scale, static_cast<const float*>(S.ptr), cp, N,
+                               strm);
+        else
+            st = smk_gemv_u8s8_host(c, (int)M, (int)N, (int)K, static_cast<const uint8_t*>(A.ptr), a_zero_point,
+                                    static_cast<const int8_t*>(B.ptr), a_scale, static_cast<const float*>(S.ptr), cp);
+    }
+    check(st);
+    return result;
+}
+
 py::object py_sgemm(const py::handle& Ah, const py::handle& Bh, const py::object& C, float alpha, float beta,
                     const std::string& isa, bool trans_a, bool trans_b, const py::object& stream) {
     if (!isa.empty()) {
@@ -585,6 +654,12 @@ PYBIND11_MODULE(_core, m) {
     m.def("sgemm_bf16", &py_sgemm_bf16, py::arg("A"), py::arg("B"), py::arg("alpha") = 1.0f,
           py::arg("beta") = 0.0f, py::arg("C") = py::none(), py::kw_only(), py::arg("trans_b") = false,
           py::arg("stream") = py::none());
+    m.def("sgemm_u8s8", &py_sgemm_u8s8, py::arg("A"), py::arg("B"), py::arg("a_scale"), py::arg("a_zero_point"),
+          py::arg("b_scales"), py::arg("C") = py::none(), py::kw_only(), py::arg("trans_b") = false,
+          py::arg("stream") = py::none(),
+          "sgemm_u8s8(A, B, a_scale, a_zero_point, b_scales, C=None, *, trans_b=False) -> float32 [M, N]: "
+          "C = a_scale * b_scales[j] * sum_k (A - a_zero_point) * B.T, A uint8 [M, K] (M <= 8), B int8 [N, K] "
+          "with trans_b=True; exact integer sums, the reference's scalar-table rounding.");
     m.def("gemv_dense", &py_gemv_dense, py::arg("x"), py::arg("W"), py::arg("wtype") = "float32",
           py::arg("out") = py::none(), py::arg("stream") = py::none());
     // The device path of the Python package for torch CUDA tensors: the

@@ -5,9 +5,11 @@
 
 #include "../../include/smk_cuda.h"
 #include "gemv_dense.cuh"
+#include "gemv_int8.cuh"
 #include "gemv_quant.cuh"
 
 #include <algorithm>
+#include <cmath>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -715,6 +717,69 @@ smk_status smk_gemv_dense_host(smk_ctx* c, smk_dtype wt, smk_dtype xt, int M, in
     smk_status st = smk_gemv_dense(c, wt, xt, M, N, K, alpha, dX, K, dW, K, beta, dC, N, s);
     if (st != SMK_OK) return st;
     if (K == 0 && beta == 0.0f) SMK_CUDA(cudaMemsetAsync(dC, 0, cb, s), "cudaMemsetAsync");
+    if (ch) SMK_CUDA(cudaMemcpyAsync(C, dC, cb, cudaMemcpyDeviceToHost, s), "cudaMemcpyAsync (C)");
+    SMK_CUDA(cudaStreamSynchronize(s), "cudaStreamSynchronize");
+    return SMK_OK;
+}
+
+// Argument checks of sgemm_u8s8 (src/bindings/pybind_entry.cpp:866-868) and
+// of this decode path.
+static smk_status check_u8s8_args(int M, int N, int K, int a_zero_point, float a_scale) {
+    if (M < 0 || N < 0 || K < 0) return fail(SMK_ERR_ARGUMENT, "M, N and K must be >= 0");
+    if (M > smk::kMaxRows)
+        return fail(SMK_ERR_ARGUMENT, "the decode path takes at most %d rows of A (got %d)", smk::kMaxRows, M);
+    if (a_zero_point < 0 || a_zero_point > 255)
+        return fail(SMK_ERR_ARGUMENT, "a_zero_point must be in [0, 255] (got %d)", a_zero_point);
+    if (!std::isfinite(a_scale)) return fail(SMK_ERR_ARGUMENT, "a_scale must be finite");
+    return SMK_OK;
+}
+
+smk_status smk_gemv_u8s8(smk_ctx* c, int M, int N, int K, const uint8_t* A, int64_t lda, int a_zero_point,
+                         const int8_t* W, int64_t ldw, float a_scale, const float* b_scales, float* C, int64_t ldc,
+                         void* stream) {
+    if (!c) return fail(SMK_ERR_ARGUMENT, "ctx must not be NULL");
+    smk_status st = check_u8s8_args(M, N, K, a_zero_point, a_scale);
+    if (st != SMK_OK) return st;
+    if (M == 0 || N == 0) return SMK_OK;
+    if (!C || !b_scales || (K > 0 && (!A || !W))) return fail(SMK_ERR_ARGUMENT, "A, W, b_scales and C must not be NULL");
+    if (ldc < N || (K > 0 && (lda < K || ldw < K))) return fail(SMK_ERR_ARGUMENT, "leading dimensions too small");
+    DeviceGuard g(c->device);
+    if (!g.ok) return fail(SMK_ERR_CUDA, "cudaSetDevice(%d) failed", c->device);
+    smk::U8S8Params p;
+    p.a = A; p.lda = lda; p.w = W; p.ldw = ldw; p.scales = b_scales; p.y = C; p.ldy = ldc;
+    p.M = M; p.N = N; p.K = K; p.zp = a_zero_point; p.a_scale = a_scale;
+    p.err = c->d_err;
+    SMK_CUDA(smk::launch_gemv_u8s8(static_cast<cudaStream_t>(stream), c->pdl, c->num_sms, p), "u8s8 gemv launch");
+    return SMK_OK;
+}
+
+smk_status smk_gemv_u8s8_host(smk_ctx* c, int M, int N, int K, const uint8_t* A, int a_zero_point, const int8_t* W,
+                              float a_scale, const float* b_scales, float* C) {
+    if (!c) return fail(SMK_ERR_ARGUMENT, "ctx must not be NULL");
+    smk_status st = check_u8s8_args(M, N, K, a_zero_point, a_scale);
+    if (st != SMK_OK) return st;
+    if (M == 0 || N == 0) return SMK_OK;
+    if (!C || !b_scales || (K > 0 && (!A || !W))) return fail(SMK_ERR_ARGUMENT, "A, W, b_scales and C must not be NULL");
+    DeviceGuard g(c->device);
+    if (!g.ok) return fail(SMK_ERR_CUDA, "cudaSetDevice(%d) failed", c->device);
+    const size_t ab = (size_t)M * K, wb = (size_t)N * K, sb = (size_t)N * 4, cb = (size_t)M * N * 4;
+    const bool ah = K > 0 && !is_device_ptr(A), wh = K > 0 && !is_device_ptr(W), sh = !is_device_ptr(b_scales),
+               ch = !is_device_ptr(C);
+    cudaStream_t s = nullptr;
+    std::lock_guard<std::mutex> lock(c->mu_stage);
+    const size_t oa = 0, ow = oa + (ah ? align256(ab) : 0), os = ow + (wh ? align256(wb) : 0),
+                 oc = os + (sh ? align256(sb) : 0), total = oc + (ch ? align256(cb) : 0);
+    if (total) SMK_CUDA(c->staging.reserve(total), "cudaMalloc (staging)");
+    char* base = static_cast<char*>(c->staging.ptr);
+    const uint8_t* dA = ah ? reinterpret_cast<const uint8_t*>(base + oa) : A;
+    const int8_t* dW = wh ? reinterpret_cast<const int8_t*>(base + ow) : W;
+    const float* dS = sh ? reinterpret_cast<const float*>(base + os) : b_scales;
+    float* dC = ch ? reinterpret_cast<float*>(base + oc) : C;
+    if (ah) SMK_CUDA(cudaMemcpyAsync(base + oa, A, ab, cudaMemcpyHostToDevice, s), "cudaMemcpyAsync (A)");
+    if (wh) SMK_CUDA(cudaMemcpyAsync(base + ow, W, wb, cudaMemcpyHostToDevice, s), "cudaMemcpyAsync (W)");
+    if (sh) SMK_CUDA(cudaMemcpyAsync(base + os, b_scales, sb, cudaMemcpyHostToDevice, s), "cudaMemcpyAsync (b_scales)");
+    st = smk_gemv_u8s8(c, M, N, K, dA, K, a_zero_point, dW, K, a_scale, dS, dC, N, s);
+    if (st != SMK_OK) return st;
     if (ch) SMK_CUDA(cudaMemcpyAsync(C, dC, cb, cudaMemcpyDeviceToHost, s), "cudaMemcpyAsync (C)");
     SMK_CUDA(cudaStreamSynchronize(s), "cudaStreamSynchronize");
     return SMK_OK;

@@ -6,6 +6,7 @@ arguments, return types, error classes and messages):
     gemv_q4_0(x, Wq, N, K)        quantize_q4_0(W)
     gemv_q8_0(x, Wq, N, K)        quantize_q8_0(W)
     sgemm(x, W, trans_b=True)     sgemm_f16(x, W, trans_b=True)     sgemm_bf16(x, W, trans_b=True)
+    sgemm_u8s8(A, W, a_scale, a_zero_point, b_scales, trans_b=True)
 
 Every call runs CUDA kernels on a Blackwell GPU (there is no CPU path).
 NumPy operands are copied to the device and the call returns NumPy results,
@@ -47,6 +48,7 @@ __all__ = [
     "sgemm",
     "sgemm_bf16",
     "sgemm_f16",
+    "sgemm_u8s8",
     "silu_mul",
 ]
 
@@ -320,6 +322,22 @@ def sgemm_bf16(A, B, alpha=1.0, beta=0.0, C=None, *, trans_b=False):
     """bfloat16 A and B (uint16 bit patterns or ml_dtypes.bfloat16; torch.bfloat16 on the device),
     float32 accumulation and output; trans_b=True, M <= 8."""
     return _dense(_core.sgemm_bf16, A, B, C, alpha, beta, trans_b)
+
+
+def sgemm_u8s8(A, B, a_scale, a_zero_point, b_scales, C=None, *, trans_b=False):
+    """C = a_scale * b_scales[j] * sum_k (A[i, k] - a_zero_point) * B[j, k] in float32 for the
+    decode shape: A uint8 [M, K] (M <= 8), B int8 [N, K] with trans_b=True, b_scales float32 [N].
+    The integer sums are exact and each output is the reference's scalar-table value."""
+    if any(_is_cuda_tensor(a) for a in (A, B, b_scales)):
+        t = _torch()
+        if C is None:
+            C = t.empty((A.shape[0], B.shape[0] if trans_b else B.shape[1]), dtype=t.float32, device=A.device)
+        with t.cuda.device(A.device):
+            _core._set_device(A.device.index)
+            _core.sgemm_u8s8(_wrap(A), _wrap(B), a_scale, a_zero_point, _wrap(b_scales), C=_wrap(C),
+                             trans_b=trans_b, stream=_stream_of(C))
+        return C
+    return _core.sgemm_u8s8(A, B, a_scale, a_zero_point, b_scales, C=C, trans_b=trans_b)
 
 
 def gemv_dense(x, W, *, wtype=None, out=None):

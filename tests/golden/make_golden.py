@@ -8,6 +8,7 @@ Run in a container that has the reference tree (it reads it; the GPU box
 does not have it and only reads the .npz files written here):
 
     make -C oracle all && python tests/golden/make_golden.py
+    python tests/golden/make_golden.py u8s8     # only ref_u8s8.npz
 
 Large weight matrices are not stored: each case keeps its seed and shape, the
 SHA-256 of the reference's quantized bytes and the reference's outputs; the
@@ -98,6 +99,44 @@ def dense_operands(kind: str, A: np.ndarray, B: np.ndarray):
     if kind == "f16":
         return A.astype(np.float16).view(np.uint16), B.astype(np.float16).view(np.uint16)
     return O.bf16_bits(A), O.bf16_bits(B)
+
+
+# sgemm_u8s8 cases (M, N, K, zero point): decode shapes M <= 8 with ragged N
+# and K, the shapes of the reference's own parameter list
+# (tests/test_precision.py:256-258) that have M <= 8, and one case of all-extreme
+# operands (A = 255, B = -128, zp = 0: tests/test_precision.py:282-288).
+U8S8_CASES = [(1, 1, 1, 0), (7, 9, 8, 128), (1, 4096, 128, 255), (5, 15, 3, 3), (8, 33, 385, 128),
+              (1, 300, 257, 77), (4, 33, 1027, 200), (2, 64, 4096, 0), (1, 257, 1024, 128), (3, 33, 4096, 0),
+              (1, 2048, 2048, 128), (8, 1000, 2080, 31)]
+U8S8_EXTREME = 9   # index of the all-extreme case
+
+
+def u8s8_case_inputs(i: int, m: int, n: int, k: int):
+    """A uint8 [m, k], W int8 [n, k] (the trans_b layout), b_scales [n], a_scale of u8s8 case i."""
+    rng = np.random.default_rng(700 + i)
+    if i == U8S8_EXTREME:
+        A = np.full((m, k), 255, np.uint8)
+        W = np.full((n, k), -128, np.int8)
+        return A, W, np.ones(n, np.float32), np.float32(1.0)
+    A = rng.integers(0, 256, (m, k), dtype=np.uint8)
+    W = rng.integers(-128, 128, (n, k), dtype=np.int8)
+    scales = rng.uniform(-0.1, 0.1, n).astype(np.float32)
+    return A, W, scales, np.float32(0.0173)
+
+
+def write_u8s8() -> None:
+    """sgemm_u8s8 outputs of the reference's scalar table and its table for
+    this CPU, with B as [N, K] (trans_b) and as [K, N]."""
+    uo = {"cases": np.array(U8S8_CASES, np.int64), "u8s8_path": np.array(O.ref().smkref_u8s8_path().decode())}
+    for i, (m, n, k, zp) in enumerate(U8S8_CASES):
+        A, W, scales, a_scale = u8s8_case_inputs(i, m, n, k)
+        uo[f"sha{i}"] = np.array(sha(np.concatenate([A.view(np.uint8).ravel(), W.view(np.uint8).ravel(),
+                                                    scales.view(np.uint8)])))
+        for tb in (1, 0):
+            B = W if tb else np.ascontiguousarray(W.T)
+            uo[f"tb{tb}_{i}_scalar"] = O.ref_sgemm_u8s8(A, B, a_scale, zp, scales, bool(tb), isa=ISA_SCALAR)
+            uo[f"tb{tb}_{i}_simd"] = O.ref_sgemm_u8s8(A, B, a_scale, zp, scales, bool(tb), isa=-1)
+    np.savez_compressed(os.path.join(HERE, "ref_u8s8.npz"), **uo)
 
 
 def special_quant_rows() -> np.ndarray:
@@ -202,6 +241,9 @@ def main() -> None:
             do[f"{kind}_{i}_simd"] = ref_dense(kind, -1, a, b, alpha, beta, C0)
     np.savez_compressed(os.path.join(HERE, "ref_dense.npz"), **do)
 
+    # 6. INT8 sgemm_u8s8.
+    write_u8s8()
+
     with open(os.path.join(HERE, "PROVENANCE.txt"), "w") as f:
         f.write("Golden vectors written by tests/golden/make_golden.py from\n")
         for key, val in meta.items():
@@ -212,4 +254,7 @@ def main() -> None:
 
 
 if __name__ == "__main__":
-    main()
+    if sys.argv[1:] == ["u8s8"]:   # only the sgemm_u8s8 vectors
+        write_u8s8()
+    else:
+        main()

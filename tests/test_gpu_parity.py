@@ -592,6 +592,90 @@ def test_dense_rejects_non_decode(sk):
         sk.sgemm(A[:2], B.T.copy())
 
 
+# ---- INT8 sgemm_u8s8 (trans_b, M <= 8) ------------------------------------------------
+
+def test_u8s8_golden_bitwise(sk, torch):
+    """Every golden case, through host arrays and through CUDA tensors:
+    bitwise the reference's scalar table (exact sums and its epilogue)."""
+    g = np.load(os.path.join(GOLD, "ref_u8s8.npz"))
+    for i, (m, n, k, zp) in enumerate(g["cases"]):
+        A, W, scales, a_scale = G.u8s8_case_inputs(i, int(m), int(n), int(k))
+        want = g[f"tb1_{i}_scalar"]
+        got = sk.sgemm_u8s8(A, W, a_scale, int(zp), scales, trans_b=True)
+        assert got.dtype == np.float32 and got.shape == (m, n)
+        np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32), err_msg=f"case {i}")
+        dev = sk.sgemm_u8s8(torch.from_numpy(A).cuda(), torch.from_numpy(W).cuda(), a_scale, int(zp),
+                            torch.from_numpy(scales).cuda(), trans_b=True)
+        np.testing.assert_array_equal(dev.cpu().numpy().view(np.uint32), want.view(np.uint32), err_msg=f"case {i}")
+
+
+def _u8s8_case(seed, M, N, K):
+    rng = np.random.default_rng(seed)
+    A = rng.integers(0, 256, (M, K), dtype=np.uint8)
+    W = rng.integers(-128, 128, (N, K), dtype=np.int8)
+    return A, W, rng.uniform(-0.1, 0.1, N).astype(np.float32)
+
+
+@pytest.mark.parametrize("M,N,K,zp", [
+    (1, 4096, 4096, 128),      # the row path's shape; A in shared memory
+    (8, 4096, 4096, 0),        # zero point 0: no column sums
+    (4, 1003, 2048, 255),      # ragged N
+    (1, 333, 1040, 3),         # K tail inside an item
+    (8, 2048, 28672, 77),      # A too large for shared memory: read through L1
+    (3, 17, 40, 9),            # K % 16 != 0: the per-byte kernel
+    (1, 8, 1049600, 128),      # more than 1024 items per row: the per-byte kernel's int64 sums
+])
+def test_u8s8_shapes_bitwise_oracle(sk, torch, M, N, K, zp):
+    A, W, scales = _u8s8_case(M * 131 + N + K, M, N, K)
+    want = O.sgemm_u8s8(A, W, 0.0173, zp, scales, True)
+    got = sk.sgemm_u8s8(torch.from_numpy(A).cuda(), torch.from_numpy(W).cuda(), 0.0173, zp,
+                        torch.from_numpy(scales).cuda(), trans_b=True).cpu().numpy()
+    np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+def test_u8s8_unaligned_and_extreme(sk, torch):
+    """Views of A and W at odd byte offsets (A staged byte by byte, W through
+    the per-byte kernel) give the same bits; A = 255, W = -128, zp = 0 is
+    exact (the largest sums: -255·128·K)."""
+    M, N, K, zp = 3, 257, 2048, 100
+    A, W, scales = _u8s8_case(5, M, N, K)
+    want = O.sgemm_u8s8(A, W, 0.25, zp, scales, True)
+    abuf = torch.zeros(M * K + 16, dtype=torch.uint8, device="cuda")
+    wbuf = torch.zeros(N * K + 16, dtype=torch.int8, device="cuda")
+    for ao, wo in ((3, 0), (0, 1), (5, 7)):
+        a = abuf[ao:ao + M * K].view(M, K)
+        w = wbuf[wo:wo + N * K].view(N, K)
+        a.copy_(torch.from_numpy(A))
+        w.copy_(torch.from_numpy(W))
+        got = sk.sgemm_u8s8(a, w, 0.25, zp, torch.from_numpy(scales).cuda(), trans_b=True).cpu().numpy()
+        np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32), err_msg=f"offsets {ao}, {wo}")
+    K = 4096
+    got = sk.sgemm_u8s8(np.full((8, K), 255, np.uint8), np.full((33, K), -128, np.int8), 1.0, 0,
+                        np.ones(33, np.float32), trans_b=True)
+    np.testing.assert_array_equal(got, np.full((8, 33), -255.0 * 128 * K, np.float32))
+
+
+def test_u8s8_in_cuda_graph(sk, torch):
+    """The CUDA-tensor path only launches on torch's current stream: it
+    captures into a CUDA graph, and replays give the oracle's bits."""
+    M, N, K, zp = 2, 1536, 3072, 17
+    A, W, scales = _u8s8_case(9, M, N, K)
+    a, w, s = torch.from_numpy(A).cuda(), torch.from_numpy(W).cuda(), torch.from_numpy(scales).cuda()
+    C = torch.empty((M, N), device="cuda")
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        sk.sgemm_u8s8(a, w, 0.5, zp, s, C, trans_b=True)   # warm-up outside capture
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            sk.sgemm_u8s8(a, w, 0.5, zp, s, C, trans_b=True)
+    C.zero_()
+    g.replay()
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(C.cpu().numpy().view(np.uint32),
+                                  O.sgemm_u8s8(A, W, 0.5, zp, scales, True).view(np.uint32))
+    del g
+
+
 def test_no_device_errors(sk):
     from simd_ml_kernels import _core
     assert _core._device_error(0) == 0

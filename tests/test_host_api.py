@@ -97,12 +97,52 @@ def test_valid_call_fails_loudly_without_a_gpu():
 def test_c_abi_exports_every_declared_symbol():
     header = open(os.path.join(REPO, "include", "smk_cuda.h")).read()
     declared = set(re.findall(r"^\s*(?:smk_status|const char\*)\s+(smk_\w+)\(", header, re.M))
-    assert {"smk_gemv_q4_0", "smk_gemv_q8_0", "smk_gemv_q", "smk_gemv_dense", "smk_quantize"} <= declared
+    assert {"smk_gemv_q4_0", "smk_gemv_q8_0", "smk_gemv_q", "smk_gemv_dense", "smk_quantize",
+            "smk_gemv_u8s8", "smk_gemv_u8s8_host", "smk_gemv_q_silu_mul"} <= declared
     lib = ctypes.CDLL(sk.library_path())
     missing = [name for name in sorted(declared) if not hasattr(lib, name)]
     assert not missing, f"declared but not exported: {missing}"
     lib.smk_version.restype = ctypes.c_char_p
     assert b"sm_100a" in lib.smk_version()
+
+
+def test_sgemm_u8s8_argument_checks():
+    """sgemm_u8s8 rejects what the reference rejects, in its order and with its
+    messages (the reference's tests/test_bindings_edge_cases.py:190-258 restated),
+    before any device work; shapes outside the decode contract raise
+    ArgumentError naming it; empty outputs come back without a GPU."""
+    A, B, s, zp, bs = np.ones((4, 6), np.uint8), np.ones((5, 6), np.int8), 0.5, 1, np.ones(5, np.float32)
+    f = sk.sgemm_u8s8
+    for dt in (np.int8, np.uint16, np.float32):
+        with pytest.raises(sk.DTypeError, match="A must be uint8"):
+            f(A.astype(dt), B, s, zp, bs, trans_b=True)
+    for dt in (np.uint8, np.int16, np.float32):
+        with pytest.raises(sk.DTypeError, match="B must be int8"):
+            f(A, B.astype(dt), s, zp, bs, trans_b=True)
+    with pytest.raises(sk.DTypeError, match="b_scales"):
+        f(A, B, s, zp, bs.astype(np.float64), trans_b=True)
+    with pytest.raises(sk.ArgumentError, match="b_scales must have N = 5"):
+        f(A, B, s, zp, np.ones(4, np.float32), trans_b=True)
+    with pytest.raises(sk.ArgumentError, match="1-D"):
+        f(A, B, s, zp, np.ones((5, 1), np.float32), trans_b=True)
+    for bad in (-1, 256):
+        with pytest.raises(sk.ArgumentError, match=r"\[0, 255\]"):
+            f(A, B, s, bad, bs, trans_b=True)
+    with pytest.raises(sk.ArgumentError, match="finite"):
+        f(A, B, float("nan"), zp, bs, trans_b=True)
+    with pytest.raises(sk.ArgumentError, match="Shape mismatch"):
+        f(A, np.ones((6, 5), np.int8), s, zp, bs, trans_b=True)
+    with pytest.raises(sk.ArgumentError, match="C-contiguous"):
+        f(np.asfortranarray(A), B, s, zp, bs, trans_b=True)
+    with pytest.raises(sk.ArgumentError, match="trans_b=True"):
+        f(A, np.ones((6, 5), np.int8), s, zp, bs)             # B as [K, N]: outside the decode path
+    with pytest.raises(sk.ArgumentError, match="at most 8 rows"):
+        f(np.ones((9, 6), np.uint8), B, s, zp, bs, trans_b=True)
+    with pytest.raises(sk.DTypeError, match="C must be float32"):
+        f(A, B, s, zp, bs, np.zeros((4, 5)), trans_b=True)
+    for M, K, N in ((0, 3, 5), (4, 3, 0)):   # no outputs: any layout of B
+        C = f(np.ones((M, K), np.uint8), np.ones((K, N), np.int8), 1.0, 0, np.ones(N, np.float32))
+        assert C.shape == (M, N)
 
 
 def test_row_slices_match_reference_rule():

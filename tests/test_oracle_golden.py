@@ -113,6 +113,29 @@ def test_dense_matches_reference(kind):
         assert (np.abs(g[f"{kind}_{i}_simd"] - want) <= bound).all()
 
 
+def test_u8s8_matches_reference():
+    """sgemm_u8s8: the restatement is bitwise the reference's scalar table for
+    both B layouts, and the reference's table for this CPU is within the
+    documented bound 2(K+2)u·|a_scale·b_j|·Σ|A − zp||B| of the exact sums
+    (int8_gemm.hpp:23-24, tests/test_precision.py:262-280 there)."""
+    g = load("ref_u8s8.npz")
+    for i, (m, n, k, zp) in enumerate(g["cases"]):
+        A, W, scales, a_scale = G.u8s8_case_inputs(i, int(m), int(n), int(k))
+        assert sha(np.concatenate([A.view(np.uint8).ravel(), W.view(np.uint8).ravel(),
+                                   scales.view(np.uint8)])) == str(g[f"sha{i}"])
+        sc = np.float64(a_scale) * scales.astype(np.float64)
+        for tb in (1, 0):
+            B = W if tb else np.ascontiguousarray(W.T)
+            got = O.sgemm_u8s8(A, B, a_scale, int(zp), scales, bool(tb))
+            np.testing.assert_array_equal(got.view(np.uint32), g[f"tb{tb}_{i}_scalar"].view(np.uint32))
+            s64, mag = O.u8s8_ref64(A, B, int(zp), bool(tb))
+            bound = 2 * (int(k) + 2) * U * mag * np.abs(sc) + 1e-30
+            assert (np.abs(g[f"tb{tb}_{i}_simd"] - s64 * sc) <= bound).all()
+    # The all-extreme case is exact: -255·128·K.
+    m, n, k, _ = g["cases"][G.U8S8_EXTREME]
+    np.testing.assert_array_equal(g[f"tb1_{G.U8S8_EXTREME}_scalar"], np.full((m, n), -255.0 * 128 * k, np.float32))
+
+
 def test_fp16_conversion_sample():
     """binary32 -> binary16 RNE on every half-way point between consecutive
     halves, their neighbours, and a random sample (the reference's exhaustive
