@@ -19,8 +19,10 @@
  *
  * Two kinds of entry points:
  *   smk_*           device pointers, asynchronous on `stream`, capturable in
- *                   a CUDA graph (no allocation, no synchronisation, unless a
- *                   call needs library scratch for the first time at a size).
+ *                   a CUDA graph (no synchronisation; a call that needs
+ *                   library scratch for the first time at a size allocates
+ *                   it, during a capture too, and keeps replaced buffers
+ *                   until smk_ctx_destroy).
  *   smk_*_host      any mix of host and device pointers (told apart with
  *                   cudaPointerGetAttributes); host operands are staged
  *                   through library-owned device buffers; returns when y is
@@ -105,9 +107,11 @@ smk_status smk_gemv_q4_0(smk_ctx* ctx, int N, int K, const float* x, const uint8
 smk_status smk_gemv_q8_0(smk_ctx* ctx, int N, int K, const float* x, const uint8_t* Wq, float* y, void* stream);
 /* The decode step's down projection with its SwiGLU input formed on the fly:
  * y = (silu(gate) * up) @ W.T, silu(g) = g / (1 + exp(-g)) as the reference
- * (src/kernels/scalar_kernels.cpp:196-198), the product quantized to Q8 inside
- * the GEMV; replaces w_down(silu(w_gate(h)) * w_up(h)) of the reference's
- * examples/llama/llama.py:434 without the separate SiLU and product passes.
+ * (src/kernels/scalar_kernels.cpp:196-198), the product formed once per call
+ * while x is quantized to Q8 (into the context's scratch for this stream), then
+ * the GEMV on those blocks; replaces w_down(silu(w_gate(h)) * w_up(h)) of the
+ * reference's examples/llama/llama.py:434 without a separate SiLU and product
+ * pass over fp32 values.
  * Device pointers, asynchronous; gate [M, ldg], up [M, ldu]. An addition. */
 smk_status smk_gemv_q_silu_mul(smk_ctx* ctx, smk_qformat fmt, int M, int N, int K, const float* gate, int64_t ldg,
                                const float* up, int64_t ldu, const uint8_t* Wq, float* y, int64_t ldy, void* stream);

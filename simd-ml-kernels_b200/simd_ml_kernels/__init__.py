@@ -234,7 +234,7 @@ def gemv_q8_0_batch(x, Wq, N, K, *, out=None):
 
 def _silu_mul_gemv(fmt, gate, up, Wq, N, K, out):
     """The decode step's down projection, y = (silu(gate) * up) @ W.T, with the
-    SwiGLU product formed while x is quantized (CUDA tensors; gate and up [K]
+    SwiGLU product formed once while x is quantized (CUDA tensors; gate and up [K]
     or [M, K], M <= 8; asynchronous on the current stream)."""
     t = _torch()
     if not (_is_cuda_tensor(gate) and _is_cuda_tensor(up)):
@@ -253,8 +253,9 @@ def _silu_mul_gemv(fmt, gate, up, Wq, N, K, out):
 
 def gemv_q4_0_silu_mul(gate, up, Wq, N, K, *, out=None):
     """y = (silu(gate) * up) @ W.T, W as quantize_q4_0 blocks: the reference
-    decoder's w_down(silu(w_gate(h)) * w_up(h)) after the gate/up GEMV, in one
-    kernel (silu(g) = g / (1 + exp(-g)))."""
+    decoder's w_down(silu(w_gate(h)) * w_up(h)) after the gate/up GEMV, with no
+    separate SiLU pass: the product (silu(g) = g / (1 + exp(-g))) is formed
+    once per call while x is quantized to Q8, and the GEMV reads those blocks."""
     return _silu_mul_gemv("q4_0", gate, up, Wq, N, K, out)
 
 

@@ -303,6 +303,37 @@ def test_gemv_silu_mul_equals_unfused(sk, torch, fmt, M, N, K):
     assert torch.equal(fused1.view(torch.int32), plain1.view(torch.int32))
 
 
+def test_gemv_silu_mul_first_call_inside_capture(sk, torch):
+    """The fused down projection keeps its quantized activations in a scratch
+    buffer per stream. Its first call on a fresh stream may come inside a
+    CUDA-graph capture (the allocation is made there), and a later, larger
+    call in the same capture grows the buffer without invalidating the first:
+    replays equal the unfused results bit for bit."""
+    rng = np.random.default_rng(11)
+    shapes = [(2048, 8192), (1024, 16384)]   # the second needs a larger scratch
+    cases = []
+    for N, K in shapes:
+        W = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+        Wq = torch.from_numpy(O.quantize("q4_0", W).ravel()).cuda()
+        g = torch.from_numpy((rng.standard_normal(K) * 3).astype(np.float32)).cuda()
+        u = torch.from_numpy(rng.standard_normal(K).astype(np.float32)).cuda()
+        cases.append((N, K, Wq, g, u, torch.empty(N, device="cuda")))
+    stream = torch.cuda.Stream()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        with torch.cuda.graph(graph, stream=stream):
+            for N, K, Wq, g, u, y in cases:
+                sk.gemv_q4_0_silu_mul(g, u, Wq, N, K, out=y)
+    for _, _, _, _, _, y in cases:
+        y.fill_(float("nan"))
+    graph.replay()
+    torch.cuda.synchronize()
+    for N, K, Wq, g, u, y in cases:
+        want = sk.gemv_q4_0(sk.silu_mul(g, u), Wq, N, K)
+        assert torch.equal(y.view(torch.int32), want.view(torch.int32))
+    del graph
+
+
 @pytest.mark.parametrize("fmt", ["q4_0", "q8_0"])
 def test_gemv_k0_and_n0(sk, fmt):
     fn = sk.gemv_q4_0 if fmt == "q4_0" else sk.gemv_q8_0
