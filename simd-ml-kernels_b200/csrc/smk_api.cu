@@ -314,6 +314,12 @@ smk_status run_q(smk_ctx* c, smk_qformat fmt, int M, int N, int K, const float* 
     // GEMV (measured on the Llama-1B decode stack: 3,100-3,127 against
     // 2,836-2,855 tok/s).
     if (up && q.fast && q.x_in_smem && !dump) q.x_in_smem = false;
+    // Long rows of x and few weight rows per SM: one quantize kernel writes x
+    // to scratch once, instead of every CTA quantizing all of K (B200,
+    // graph-chained: 8192x28672 28.9 against 33.9 us; the Llama-1B stack
+    // 3,177 against 3,132 tok/s). 28672x8192 measured 3 % slower that way and
+    // K = 2048 (config 0) far slower, so those keep x in shared memory.
+    if (!up && !gather && !dump && q.fast && q.x_in_smem && K >= 8192 && N <= 16384) q.x_in_smem = false;
     if (!q.x_in_smem) {
         uint8_t* xq;
         {

@@ -303,6 +303,29 @@ def test_gemv_silu_mul_equals_unfused(sk, torch, fmt, M, N, K):
     assert torch.equal(fused1.view(torch.int32), plain1.view(torch.int32))
 
 
+@pytest.mark.parametrize("fmt", ["q4_0", "q8_0"])
+@pytest.mark.parametrize("K", [8192, 28672])
+def test_x_in_global_equals_x_in_shared(sk, torch, fmt, K):
+    """With K >= 8192 and at most 16384 rows, x is quantized once into global
+    scratch; with more rows each CTA quantizes it into shared memory. A row's
+    arithmetic is the same either way: the first 2048 rows of a 16392-row
+    GEMV equal a 2048-row GEMV over the same rows, bit for bit, and stay
+    within the bound of the float64 sums."""
+    N_big, N_small = 16392, 2048
+    g = torch.Generator(device="cuda")
+    g.manual_seed(K + (fmt == "q8_0"))
+    quant = sk.quantize_q4_0 if fmt == "q4_0" else sk.quantize_q8_0
+    wd = quant(torch.randn((N_big, K), generator=g, device="cuda") * 0.02).reshape(-1)
+    xd = torch.randn(K, generator=g, device="cuda")
+    fn = sk.gemv_q4_0 if fmt == "q4_0" else sk.gemv_q8_0
+    big = fn(xd, wd, N_big, K)
+    small_bytes = N_small * (K // 32) * O.BLOCK_BYTES[fmt]
+    small = fn(xd, wd[:small_bytes], N_small, K)
+    assert torch.equal(big[:N_small].view(torch.int32), small.view(torch.int32))
+    y64, mag = O.ref64(fmt, xd.cpu().numpy(), wd[:small_bytes].cpu().numpy().reshape(N_small, -1), N_small, K)
+    assert_gemv_close(small.cpu().numpy(), y64, mag, K, f"{fmt} K={K}")
+
+
 def test_gemv_silu_mul_first_call_inside_capture(sk, torch):
     """The fused down projection keeps its quantized activations in a scratch
     buffer per stream. Its first call on a fresh stream may come inside a
