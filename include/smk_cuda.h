@@ -131,6 +131,16 @@ smk_status smk_gemv_dense(smk_ctx* ctx, smk_dtype w_type, smk_dtype x_type, int 
 smk_status smk_gemv_dense_host(smk_ctx* ctx, smk_dtype w_type, smk_dtype x_type, int M, int N, int K, float alpha,
                                const void* X, const void* W, float beta, float* C);
 
+/* ---- rows of a quantized matrix as float32 (replaces dequantize_rows of
+ * examples/llama/gguf_reader.py:113-129 for Q4_0 / Q8_0: the embedding lookup
+ * of a decode step) ----
+ * out[r][k] (row stride ldo) = value k of row rows[r] of Wq (N rows of K/32
+ * blocks): fp16(d)·(q − 8) for Q4_0, fp16(d)·q for Q8_0, exact. rows is an
+ * int32 array in device memory; an index outside [0, N) gives a row of NaN and
+ * a nonzero smk_device_error. Device pointers, asynchronous. */
+smk_status smk_dequantize_rows(smk_ctx* ctx, smk_qformat fmt, int N, int K, const uint8_t* Wq, const int32_t* rows,
+                               int nrows, float* out, int64_t ldo, void* stream);
+
 /* ---- INT8 decode GEMV (replaces GemmU8S8Fn with trans_b = true, M <= 8:
  * src/dispatch/kernels.hpp:47,69; the M = 1 row path
  * src/kernels/gemm/int8_rows.hpp) ----

@@ -267,3 +267,19 @@ def ref_sgemm_u8s8(A, B, a_scale, a_zero_point, b_scales, trans_b=False, isa: in
     ref().smkref_sgemm_u8s8(isa, int(trans_b), M, N, K, _ptr(A), int(a_zero_point), _ptr(B), float(a_scale),
                             _ptr(bs), _ptr(C))
     return C
+
+
+def dequantize_rows(fmt: str, Wq: np.ndarray, K: int, rows) -> np.ndarray:
+    """float32 rows of a Q4_0 / Q8_0 matrix [N, K/32 blocks]: fp16(d)·(q − 8)
+    (Q4_0: value j in the low nibble of byte j, value 16 + j in the high one)
+    or fp16(d)·q (Q8_0), as examples/llama/gguf_reader.py:113-129 computes it."""
+    r = np.atleast_1d(np.asarray(rows))
+    nb = K // 32
+    blocks = np.ascontiguousarray(Wq, np.uint8).reshape(-1, nb, BLOCK_BYTES[fmt])[r]
+    d = blocks[:, :, :2].copy().view("<f2").astype(np.float32)
+    if fmt == "q8_0":
+        q = blocks[:, :, 2:].view(np.int8).astype(np.float32)
+    else:
+        b = blocks[:, :, 2:]
+        q = np.concatenate([b & 0x0F, b >> 4], axis=-1).astype(np.float32) - np.float32(8.0)
+    return (d * q).reshape(len(r), K)

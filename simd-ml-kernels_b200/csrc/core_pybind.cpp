@@ -740,6 +740,12 @@ PYBIND11_MODULE(_core, m) {
         check(smk_silu_mul(ctx_for(device), n, reinterpret_cast<const float*>(g), reinterpret_cast<const float*>(u),
                            reinterpret_cast<float*>(out), reinterpret_cast<void*>(stream)));
     });
+    m.def("_dequantize_rows", [](int fmt, int N, int K, uintptr_t w, uintptr_t rows, int nrows, uintptr_t out,
+                                 long long ldo, uintptr_t stream, int device) {
+        check(smk_dequantize_rows(ctx_for(device), (smk_qformat)fmt, N, K, reinterpret_cast<const uint8_t*>(w),
+                                  reinterpret_cast<const int32_t*>(rows), nrows, reinterpret_cast<float*>(out), ldo,
+                                  reinterpret_cast<void*>(stream)));
+    });
     m.def("version", []() { return std::string(smk_version()); });
     m.def("_set_device", [](int d) { current_device_hint = d; });
     m.def("_ctx_set", [](int option, long long value) { check(smk_ctx_set(ctx_for(current_device_hint), option, value)); });

@@ -4,6 +4,7 @@
 // synchronous *_host entry points, and error reporting.
 
 #include "../../include/smk_cuda.h"
+#include "dequant.cuh"
 #include "gemv_dense.cuh"
 #include "gemv_int8.cuh"
 #include "gemv_quant.cuh"
@@ -800,6 +801,23 @@ smk_status smk_gemv_u8s8_host(smk_ctx* c, int M, int N, int K, const uint8_t* A,
     if (st != SMK_OK) return st;
     if (ch) SMK_CUDA(cudaMemcpyAsync(C, dC, cb, cudaMemcpyDeviceToHost, s), "cudaMemcpyAsync (C)");
     SMK_CUDA(cudaStreamSynchronize(s), "cudaStreamSynchronize");
+    return SMK_OK;
+}
+
+smk_status smk_dequantize_rows(smk_ctx* c, smk_qformat fmt, int N, int K, const uint8_t* Wq, const int32_t* rows,
+                               int nrows, float* out, int64_t ldo, void* stream) {
+    if (!c) return fail(SMK_ERR_ARGUMENT, "ctx must not be NULL");
+    if (fmt != SMK_Q4_0 && fmt != SMK_Q8_0) return fail(SMK_ERR_DTYPE, "unknown block format %d", (int)fmt);
+    if (N < 0 || K < 0 || nrows < 0) return fail(SMK_ERR_ARGUMENT, "N, K and nrows must be >= 0");
+    if (K % 32 != 0) return fail(SMK_ERR_ARGUMENT, "K must be a multiple of 32 (got %d)", K);
+    if (nrows == 0 || K == 0) return SMK_OK;
+    if (!Wq || !rows || !out) return fail(SMK_ERR_ARGUMENT, "Wq, rows and out must not be NULL");
+    if (ldo < K) return fail(SMK_ERR_ARGUMENT, "ldo must be >= K");
+    DeviceGuard g(c->device);
+    if (!g.ok) return fail(SMK_ERR_CUDA, "cudaSetDevice(%d) failed", c->device);
+    SMK_CUDA(smk::launch_dequantize_rows(static_cast<cudaStream_t>(stream), (int)fmt, Wq, N, K, rows, nrows, out, ldo,
+                                         c->d_err, c->num_sms),
+             "dequantize launch");
     return SMK_OK;
 }
 

@@ -15,7 +15,10 @@ is queued on torch's current stream and returns a CUDA tensor.
 
 Additions for this build: gemv_q4_0_batch / gemv_q8_0_batch (up to 8 rows of
 x against one read of W), gemv_dense (float32 x against float32 / float16 /
-bfloat16 W), set_pdl (programmatic dependent launch between GEMVs).
+bfloat16 W), gemv_q4_0_silu_mul / gemv_q8_0_silu_mul (the decoder's down
+projection on silu(gate) * up), set_pdl (programmatic dependent launch
+between GEMVs), and the gguf submodule (llama.cpp model files onto the
+device, embedding rows).
 """
 
 from __future__ import annotations
