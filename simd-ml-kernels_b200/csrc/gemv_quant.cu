@@ -307,11 +307,9 @@ __device__ __forceinline__ void superblock(const uint8_t* sp, const XPtr& xp, fl
 // of the CTA calls this once, after its last store of y.
 __device__ __forceinline__ void copy_y_to_host(const QGemvParams& p) {
     __shared__ unsigned last;
+    __threadfence();   // this thread's rows of y before the CTA's ticket
     __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence();   // this CTA's rows of y before its ticket
-        last = atomicAdd(p.ticket, 1u) == gridDim.x - 1;
-    }
+    if (threadIdx.x == 0) last = atomicAdd(p.ticket, 1u) == gridDim.x - 1;
     __syncthreads();
     if (!last) return;
     __threadfence();   // every other CTA's rows, seen through their tickets
@@ -583,9 +581,12 @@ template <int F> __host__ __device__ constexpr int mma_rs() { return 8 * block_b
 
 __global__ void __launch_bounds__(kThreadsQuantX) quantize_x_mma_kernel(const float* __restrict__ x, long long ldx,
                                                                          const float* __restrict__ up, long long ldu,
-                                                                         int M, int nb, uint8_t* xq) {
+                                                                         int M, int nb, uint8_t* xq, unsigned* tickets) {
     pdl_launch_dependents();
     pdl_wait_primary();   // x comes from the previous kernel; xq may still be read by it
+    // The K-parted GEMV that follows counts finished CTAs per tile range here.
+    if (tickets && blockIdx.x == 0)
+        for (int i = threadIdx.x; i < kMmaMaxTickets; i += blockDim.x) tickets[i] = 0u;
     const int gq = threadIdx.x & 7;
     const long long groups = (long long)nb * 8;   // (block, row) pairs, rows padded to 8
     const long long stride = (long long)gridDim.x * (blockDim.x >> 3);
@@ -718,14 +719,22 @@ __global__ void __launch_bounds__(kMmaWarps * 32) gemv_q_mma(const QGemvParams p
     const int g = lane >> 2, t = lane & 3;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem) + warp * p.stages;
     uint64_t* xbar = reinterpret_cast<uint64_t*>(smem) + nwarps * p.stages;
+    const int xnb = p.xnb > 0 ? p.xnb : p.nb;   // blocks of x a CTA holds in shared memory
     uint8_t* xsm = smem + mma_x_offset(nwarps, p.stages);
-    float4* parts = reinterpret_cast<float4*>(smem + mma_part_offset(nwarps, p.stages, p.nb, kXS));
-    uint8_t* ring = smem + mma_ring_offset(nwarps, p.stages, p.nb, kXS) + (size_t)warp * p.stages * ITEM;
+    float4* parts = reinterpret_cast<float4*>(smem + mma_part_offset(nwarps, p.stages, xnb, kXS));
+    uint8_t* ring = smem + mma_ring_offset(nwarps, p.stages, xnb, kXS) + (size_t)warp * p.stages * ITEM;
 
     pdl_launch_dependents();
     const int ntiles = (p.N + 15) / 16, ksteps = p.nb / KB;   // K % 256 == 0: whole items
+    // K parts across CTAs (kparts > 1): CTA c works on part c / C of K, over
+    // the tile groups of its index c % C within the part.
+    const int P = p.kparts > 1 ? p.kparts : 1;
+    const int cn = (int)gridDim.x / P, kp = (int)blockIdx.x / cn, cj = (int)blockIdx.x % cn;
+    const int kq0 = kp * ksteps / P, kspan = (kp + 1) * ksteps / P - kq0;   // this CTA's items
+    const int xb0 = kq0 * KB;                                               // its first block of x
     const int S = p.split, T = nwarps / S, part = warp % S, tl = warp / S;
-    const int ks_lo = part * ksteps / S, nks = (part + 1) * ksteps / S - ks_lo;
+    const int ks_lo = kq0 + part * kspan / S, nks = kq0 + (part + 1) * kspan / S - ks_lo;
+    const bool grouped = S > 1 || P > 1;
     // Rounds of this warp. S == 1: the CTA owns a contiguous range of tiles
     // (an even share, so every SM streams one region of W) and its warps
     // take them in turn (no CTA barrier). S > 1: the CTA's groups of T tiles,
@@ -734,17 +743,15 @@ __global__ void __launch_bounds__(kMmaWarps * 32) gemv_q_mma(const QGemvParams p
     const int c_lo = (int)((long long)blockIdx.x * ntiles / gridDim.x);
     const int c_hi = (int)((long long)(blockIdx.x + 1) * ntiles / gridDim.x);
     int my_groups, valid_groups;
-    if (S == 1) {
+    if (!grouped) {
         my_groups = valid_groups = c_lo + warp < c_hi ? (c_hi - 1 - c_lo - warp) / nwarps + 1 : 0;
     } else {
         const int ngroups = (ntiles + T - 1) / T;
-        my_groups = (int)blockIdx.x < ngroups ? (ngroups - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
-        const int last_tile = my_groups > 0 ? ((int)blockIdx.x + (my_groups - 1) * (int)gridDim.x) * T + tl : 0;
+        my_groups = cj < ngroups ? (ngroups - 1 - cj) / cn + 1 : 0;
+        const int last_tile = my_groups > 0 ? (cj + (my_groups - 1) * cn) * T + tl : 0;
         valid_groups = my_groups > 0 && last_tile >= ntiles ? my_groups - 1 : my_groups;
     }
-    auto tile_of = [&](int r) {
-        return S == 1 ? c_lo + warp + r * nwarps : ((int)blockIdx.x + r * (int)gridDim.x) * T + tl;
-    };
+    auto tile_of = [&](int r) { return !grouped ? c_lo + warp + r * nwarps : (cj + r * cn) * T + tl; };
     const int nitems = valid_groups * nks;
     if (lane == 0) {
         for (int i = 0; i < p.stages; ++i) mbar_init(&bars[i], 1);
@@ -766,18 +773,24 @@ __global__ void __launch_bounds__(kMmaWarps * 32) gemv_q_mma(const QGemvParams p
     pdl_wait_primary();   // x was quantized by the previous kernel
     const uint8_t* xbase = p.xq;
     int failed = 0;
+    int xnb_here = p.nb, xoff = 0;   // blocks of x at xbase, and the block index of the first
     if constexpr (kXS) {
+        // This CTA's slice of x, blocks [xb0, xb0 + kspan·KB): its quants and
+        // its (dx, bias) pairs, two bulk copies (all of x when P == 1).
+        xnb_here = kspan * KB;
+        xoff = xb0;
         if (threadIdx.x == 0) {
-            const uint32_t bytes = (uint32_t)p.nb * 320u;
-            mbar_arrive_expect_tx(xbar, bytes);
-            tma_load_1d(xsm, p.xq, bytes, xbar);
+            const uint32_t qbytes = (uint32_t)xnb_here * 256u, dbytes = (uint32_t)xnb_here * 64u;
+            mbar_arrive_expect_tx(xbar, qbytes + dbytes);
+            tma_load_1d(xsm, p.xq + (size_t)xb0 * 256, qbytes, xbar);
+            tma_load_1d(xsm + qbytes, p.xq + (size_t)p.nb * 256 + (size_t)xb0 * 64, dbytes, xbar);
         }
         failed = !mbar_wait_bounded(xbar, 0u, p.err);
         xbase = xsm;
     }
     failed = __syncthreads_or(failed);
     const uint2* xf = reinterpret_cast<const uint2*>(xbase);
-    const float4* xd = reinterpret_cast<const float4*>(xbase + (size_t)p.nb * 256);
+    const float4* xd = reinterpret_cast<const float4*>(xbase + (size_t)xnb_here * 256);
 
     int c_slot = 0, consumed = 0;
     uint32_t c_phase = 0;
@@ -798,7 +811,7 @@ __global__ void __launch_bounds__(kMmaWarps * 32) gemv_q_mma(const QGemvParams p
                 uint32_t sc[KB][2];
 #pragma unroll
                 for (int pr = 0; pr < KB / 2; ++pr) {
-                    const int b = b0 + 2 * pr;
+                    const int b = b0 + 2 * pr - xoff;   // index within the x held at xbase
                     const uint2 xe = ld_xfrag<kXS>(xf + ((size_t)b * 8 + g) * 4 + t);
                     const uint2 xo = ld_xfrag<kXS>(xf + ((size_t)(b + 1) * 8 + g) * 4 + t);
                     uint32_t ae[4], ao[4], s2[2][2];
@@ -812,7 +825,7 @@ __global__ void __launch_bounds__(kMmaWarps * 32) gemv_q_mma(const QGemvParams p
                 }
 #pragma unroll
                 for (int j = 0; j < KB; ++j)
-                    mma_accumulate<F>(c[j], sc[j], ld_xfrag<kXS>(xd + (size_t)(b0 + j) * 4 + t), acc);
+                    mma_accumulate<F>(c[j], sc[j], ld_xfrag<kXS>(xd + (size_t)(b0 - xoff + j) * 4 + t), acc);
                 __syncwarp();
                 if (issued < nitems) {
                     fence_proxy_async_smem();
@@ -822,7 +835,7 @@ __global__ void __launch_bounds__(kMmaWarps * 32) gemv_q_mma(const QGemvParams p
                 if (++c_slot == p.stages) { c_slot = 0; c_phase ^= 1u; }
             }
         }
-        if (S == 1) {
+        if (!grouped) {
             if (r < valid_groups && !failed) {
 #pragma unroll
                 for (int rr = 0; rr < 2; ++rr) {
@@ -844,15 +857,42 @@ __global__ void __launch_bounds__(kMmaWarps * 32) gemv_q_mma(const QGemvParams p
                     sum.w = __fadd_rn(sum.w, v.w);
                 }
                 const float vals[4] = {sum.x, sum.y, sum.z, sum.w};
+                // One K part of several: the sums go to this part's partial rows.
+                float* out = P > 1 ? p.partial + (size_t)kp * p.M * p.N : p.y;
+                const long long ldo = P > 1 ? p.N : p.ldy;
 #pragma unroll
                 for (int rr = 0; rr < 2; ++rr) {
                     const int row = tile * 16 + g + 8 * rr;
 #pragma unroll
                     for (int j = 0; j < 2; ++j)
-                        if (row < p.N && 2 * t + j < p.M) p.y[(size_t)(2 * t + j) * p.ldy + row] = vals[2 * rr + j];
+                        if (row < p.N && 2 * t + j < p.M) out[(size_t)(2 * t + j) * ldo + row] = vals[2 * rr + j];
                 }
             }
             __syncthreads();
+        }
+    }
+    if (P > 1) {
+        // The last of the P CTAs with this index (same tile groups, other K
+        // parts) adds the parts in K order: deterministic whatever the order
+        // in which the CTAs finish.
+        __shared__ unsigned last_cta;
+        __threadfence();   // this thread's partial rows before the ticket
+        __syncthreads();
+        if (threadIdx.x == 0) last_cta = atomicAdd(&p.tickets[cj], 1u) == (unsigned)(P - 1);
+        __syncthreads();
+        if (last_cta && !failed) {
+            __threadfence();   // the other CTAs' rows, seen through their tickets
+            for (int r = 0; r < my_groups; ++r) {
+                const int row0 = (cj + r * cn) * T * 16;
+                const int nrows = min(T * 16, p.N - row0);
+                for (int i = threadIdx.x; i < p.M * nrows; i += blockDim.x) {
+                    const int m = i / nrows, row = row0 + i % nrows;
+                    float sum = __ldcg(p.partial + (size_t)m * p.N + row);
+                    for (int q = 1; q < P; ++q)
+                        sum = __fadd_rn(sum, __ldcg(p.partial + ((size_t)q * p.M + m) * p.N + row));
+                    p.y[(size_t)m * p.ldy + row] = sum;
+                }
+            }
         }
     }
     if (failed) {
@@ -1149,12 +1189,12 @@ cudaError_t launch_quantize_x_mma(const LaunchCfg& c, const QGemvParams& p, uint
     const long long grid = std::min<long long>((groups + kThreadsQuantX / 8 - 1) / (kThreadsQuantX / 8),
                                                (long long)c.num_sms * 4);
     return launch(quantize_x_mma_kernel, dim3((unsigned)std::max<long long>(grid, 1)), dim3(kThreadsQuantX), 0, c,
-                  p.x, p.ldx, p.up, p.ldu, p.M, p.nb, xq);
+                  p.x, p.ldx, p.up, p.ldu, p.M, p.nb, xq, p.kparts > 1 ? p.tickets : nullptr);
 }
 
-size_t gemv_q_mma_smem(int fmt, int stages, int nb, bool x_in_smem) {
+size_t gemv_q_mma_smem(int fmt, int stages, int xnb, bool x_in_smem) {
     const int rs = fmt == kQ4_0 ? mma_rs<kQ4_0>() : mma_rs<kQ8_0>();
-    return mma_ring_offset(kMmaWarps, stages, nb, x_in_smem) + (size_t)kMmaWarps * stages * 16 * rs;
+    return mma_ring_offset(kMmaWarps, stages, xnb, x_in_smem) + (size_t)kMmaWarps * stages * 16 * rs;
 }
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no link
@@ -1196,7 +1236,9 @@ cudaError_t launch_gemv_q_mma(const LaunchCfg& c, int fmt, const QGemvParams& p,
     void (*k)(QGemvParams, CUtensorMap);
     if (fmt == kQ4_0) k = x_in_smem ? gemv_q_mma<kQ4_0, true> : gemv_q_mma<kQ4_0, false>;
     else k = x_in_smem ? gemv_q_mma<kQ8_0, true> : gemv_q_mma<kQ8_0, false>;
-    const size_t smem = gemv_q_mma_smem(fmt, p.stages, p.nb, x_in_smem);
+    const int P = p.kparts > 1 ? p.kparts : 1;
+    if (P > 1 && (!x_in_smem || !p.partial || !p.tickets)) return cudaErrorInvalidValue;
+    const size_t smem = gemv_q_mma_smem(fmt, p.stages, p.xnb > 0 ? p.xnb : p.nb, x_in_smem);
     int per_sm = 0;
     cudaError_t e = occupancy_cached((const void*)k, kMmaWarps * 32, smem, &per_sm);
     if (e != cudaSuccess) return e;
@@ -1207,8 +1249,23 @@ cudaError_t launch_gemv_q_mma(const LaunchCfg& c, int fmt, const QGemvParams& p,
     const long long cap = (long long)std::min(per_sm, std::max(c.ctas_per_sm, 1)) * c.num_sms;
     QGemvParams q = p;
     q.split = 1;
-    while (q.split < kMmaWarps && 2LL * q.split <= ksteps && ntiles * q.split * 4 < cap * kMmaWarps * 3) q.split *= 2;
     long long grid;
+    if (P > 1) {
+        // K parts across CTAs: C CTAs per part, the same tile groups in every
+        // part; within a CTA the part may be split again (S) while the groups
+        // do not fill the CTA slots of a part.
+        const long long kspan = ksteps / P, cap_part = std::max(1LL, cap / P);
+        while (q.split < kMmaWarps && 2LL * q.split <= kspan && ntiles * P * q.split * 4 < cap * kMmaWarps * 3)
+            q.split *= 2;
+        while (q.split < kMmaWarps && 2LL * q.split <= kspan &&
+               (ntiles * q.split + kMmaWarps - 1) / kMmaWarps < cap_part)
+            q.split *= 2;
+        const long long T = kMmaWarps / q.split;
+        const long long C = std::min((ntiles + T - 1) / T, cap_part);
+        if (C > kMmaMaxTickets) return cudaErrorInvalidConfiguration;
+        return launch(k, dim3((unsigned)(C * P)), dim3(kMmaWarps * 32), smem, c, q, wmap);
+    }
+    while (q.split < kMmaWarps && 2LL * q.split <= ksteps && ntiles * q.split * 4 < cap * kMmaWarps * 3) q.split *= 2;
     if (q.split == 1) {   // tiles interleaved over every warp of the grid
         grid = std::min(std::max((ntiles + kMmaWarps - 1) / kMmaWarps, std::min<long long>(ntiles, c.num_sms)), cap);
     } else {              // groups of kMmaWarps / S tiles per CTA: enough groups for every CTA slot

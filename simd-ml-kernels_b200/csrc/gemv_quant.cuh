@@ -55,6 +55,16 @@ struct QGemvParams {
     int stages;            // shared-memory stages per warp (fast kernel)
     int contiguous;        // fast kernel: 1 = each CTA takes a contiguous range of tiles, 0 = tiles interleaved over CTAs
     int split;             // tensor-core kernel: K parts per 16-row tile (set by its launcher)
+    // Tensor-core kernel with x larger than shared memory: K is cut into
+    // kparts parts across CTAs, each CTA holding only its part's slice of x
+    // (xnb blocks at most; xnb = nb when kparts == 1). The CTAs' sums go to
+    // partial [kparts][M][N], and the last CTA of each tile range (counted on
+    // tickets, zeroed by the quantize kernel of the same call) adds the parts
+    // in K order into y.
+    int kparts;
+    int xnb;
+    float* partial;
+    unsigned* tickets;
     const struct GatherArgs* gather;   // fused all-gather of y over peer GPUs, or nullptr (device copy)
     // Fast kernel, y wanted in page-locked host memory: y goes to device
     // memory as usual, and the CTA that finishes last (counted on *ticket,
@@ -122,8 +132,10 @@ cudaError_t launch_gather_wait(const LaunchCfg& c, const GatherArgs* g_dev, unsi
 // x quantized by launch_quantize_x_mma into xmma_bytes(nb) bytes at p.xq,
 // then launch_gemv_q_mma with p.stages stages per warp.
 constexpr int kMmaMinRows = 3;
+constexpr int kMmaMaxTickets = 1024;   // tile ranges of a K-parted launch (zeroed by the quantize kernel)
 size_t xmma_bytes(int nb);
-size_t gemv_q_mma_smem(int fmt, int stages, int nb, bool x_in_smem);
+// Shared memory of the kernel holding xnb blocks of x (x_in_smem) or none.
+size_t gemv_q_mma_smem(int fmt, int stages, int xnb, bool x_in_smem);
 cudaError_t launch_quantize_x_mma(const LaunchCfg& c, const QGemvParams& p, uint8_t* xq);
 // x_in_smem: each CTA copies the quantized x into shared memory first.
 cudaError_t launch_gemv_q_mma(const LaunchCfg& c, int fmt, const QGemvParams& p, bool x_in_smem);

@@ -278,18 +278,39 @@ smk_status run_q(smk_ctx* c, smk_qformat fmt, int M, int N, int K, const float* 
                 xs = true;
                 p.stages = st;
             }
+        // Otherwise K in P parts across CTAs, each CTA holding its part's slice
+        // of x, when a slice fits (B200, 8 rows, 8192x28672: see the design notes).
+        for (int P = 2; !xs && P <= 16 && P <= p.nb / 8; P *= 2) {
+            const int xnb = (p.nb / 8 + P - 1) / P * 8;
+            for (int st = c->stages > 0 ? c->stages : 4; st >= 2 && !xs; --st)
+                if (smk::gemv_q_mma_smem((int)fmt, st, xnb, true) <= c->smem_optin) {
+                    xs = true;
+                    p.stages = st;
+                    p.kparts = P;
+                    p.xnb = xnb;
+                }
+        }
         if (!xs) {
             p.stages = c->stages > 0 ? c->stages : 4;
             while (p.stages > 1 && smk::gemv_q_mma_smem((int)fmt, p.stages, p.nb, false) > c->smem_optin) --p.stages;
         }
         l.warps = 16;
         l.ctas_per_sm = c->ctas_per_sm > 0 ? c->ctas_per_sm : 1;
+        // Scratch: the quantized x, then (K parts) the parts' sums [P][M][N]
+        // and the tile ranges' tickets.
+        const size_t xqb = align256(smk::xmma_bytes(p.nb));
+        const size_t partb = p.kparts > 1 ? align256((size_t)p.kparts * M * N * 4) : 0;
+        const size_t tickb = p.kparts > 1 ? (size_t)smk::kMmaMaxTickets * 4 : 0;
         uint8_t* xq;
         {
             std::lock_guard<std::mutex> g(c->mu_scratch);
             DevBuf& b = c->scratch[s];
-            SMK_CUDA(b.reserve(smk::xmma_bytes(p.nb)), "cudaMalloc (scratch)");
+            SMK_CUDA(b.reserve(xqb + partb + tickb), "cudaMalloc (scratch)");
             xq = static_cast<uint8_t*>(b.ptr);
+        }
+        if (p.kparts > 1) {
+            p.partial = reinterpret_cast<float*>(xq + xqb);
+            p.tickets = reinterpret_cast<unsigned*>(xq + xqb + partb);
         }
         SMK_CUDA(smk::launch_quantize_x_mma(l, p, xq), "quantize_x launch");
         p.xq = xq;

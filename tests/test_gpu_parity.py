@@ -248,11 +248,13 @@ def test_mma_rows_bitwise_equal_reference_scalar(sk, torch, fmt, M, N, K):
 
 @pytest.mark.parametrize("fmt", ["q4_0", "q8_0"])
 @pytest.mark.parametrize("M,N,K", [(3, 1000, 2048), (8, 4099, 256), (5, 17, 8192), (8, 16, 512), (4, 2048, 28672),
-                                   (6, 31, 768), (8, 8192, 28672)])
+                                   (6, 31, 768), (8, 8192, 28672), (5, 1000, 57344)])
 def test_mma_rows_split_k(sk, torch, fmt, M, N, K):
-    """Fewer tiles than the GPU holds: K is split into parts whose sums are
-    added in order: within the reference's bound of the float64 sums,
-    identical from call to call, NaN rows as the reference."""
+    """Fewer tiles than the GPU holds, or x larger than shared memory: K is
+    split into parts (within a CTA, and for K = 28672 / 57344 across CTAs,
+    each holding its slice of x) whose sums are added in order: within the
+    reference's bound of the float64 sums, identical from call to call, NaN
+    rows as the reference."""
     X, Wq = _mma_case(fmt, M, N, K)
     batch = sk.gemv_q4_0_batch if fmt == "q4_0" else sk.gemv_q8_0_batch
     xd, wd = torch.from_numpy(X).cuda(), torch.from_numpy(Wq.ravel()).cuda()
