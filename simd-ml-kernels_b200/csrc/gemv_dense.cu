@@ -199,7 +199,15 @@ struct DenseGeom {
 // trips rather than one per element.
 constexpr int kXInFlight = 8;
 
-template <int XK, int M>
+// With 16-bit weights lane l reads 16-byte chunks 2l and 2l + 1 of a half
+// row of x, once per row of x and weight vector. Stored in order, lanes l and
+// l + 4 of each 8-lane shared-memory wavefront would hit the same banks. So
+// the rows are kept with chunk c at position c ^ ((c >> 3) & 1), which puts
+// the 8 lanes on 8 distinct bank groups for both of their chunks (row stride
+// a multiple of 8 floats, so the swap stays inside the row).
+__device__ __forceinline__ int xswz(int c) { return c ^ ((c >> 3) & 1); }
+
+template <int XK, int M, bool kSwz>
 __device__ __forceinline__ void stage_x(const DenseParams& p, const DenseGeom& g, float* xs) {
     const int nt = blockDim.x, t = threadIdx.x;
     if (g.xvec) {
@@ -220,12 +228,13 @@ __device__ __forceinline__ void stage_x(const DenseParams& p, const DenseGeom& g
                     const int v = v0 + i * nt;
                     if (v >= per_row) break;
                     if constexpr (XK == kF32) {
-                        *reinterpret_cast<uint4*>(dst + 4 * v) = u[i];
+                        *reinterpret_cast<uint4*>(dst + 4 * (kSwz ? xswz(v) : v)) = u[i];
                     } else {
                         float2 f[4];
                         widen<XK>(u[i], f);
-                        *reinterpret_cast<float4*>(dst + 8 * v) = make_float4(f[0].x, f[0].y, f[1].x, f[1].y);
-                        *reinterpret_cast<float4*>(dst + 8 * v + 4) = make_float4(f[2].x, f[2].y, f[3].x, f[3].y);
+                        const int c0 = kSwz ? xswz(2 * v) : 2 * v, c1 = kSwz ? xswz(2 * v + 1) : 2 * v + 1;
+                        *reinterpret_cast<float4*>(dst + 4 * c0) = make_float4(f[0].x, f[0].y, f[1].x, f[1].y);
+                        *reinterpret_cast<float4*>(dst + 4 * c1) = make_float4(f[2].x, f[2].y, f[3].x, f[3].y);
                     }
                 }
             }
@@ -233,7 +242,8 @@ __device__ __forceinline__ void stage_x(const DenseParams& p, const DenseGeom& g
     } else {
 #pragma unroll 1
         for (int m = 0; m < M; ++m)
-            for (int k = t; k < p.K; k += nt) xs[(size_t)m * g.kp + k] = to_f32<XK>(p.x, m * p.ldx + k);
+            for (int k = t; k < p.K; k += nt)
+                xs[(size_t)m * g.kp + (kSwz ? 4 * xswz(k >> 2) + (k & 3) : k)] = to_f32<XK>(p.x, m * p.ldx + k);
     }
 }
 
@@ -274,7 +284,8 @@ __global__ void __launch_bounds__(WARPS * 32, 1) gemv_dense_tma(const DenseParam
     const int gw = warp * gridDim.x + blockIdx.x;
     const int my_tiles = gw < g.ntiles ? (g.ntiles - 1 - gw) / GW + 1 : 0;
     const int nitems = my_tiles * g.ksteps;
-    constexpr bool kXBulk = XK == kF32;   // FP32 x rows go to shared memory by bulk copies
+    constexpr bool kSwz = WK != kF32;               // x chunk order (xswz) for 16-bit weights
+    constexpr bool kXBulk = XK == kF32 && !kSwz;    // FP32 x rows in order go by bulk copies
     if (lane == 0) {
         for (int i = 0; i < g.stages; ++i) mbar_init(&bars[i], 1);
         if (kXBulk && threadIdx.x == 0) mbar_init(xbar, 1);
@@ -306,7 +317,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1) gemv_dense_tma(const DenseParam
             return;
         }
     } else {
-        stage_x<XK, M>(p, g, xs);
+        stage_x<XK, M, kSwz>(p, g, xs);
         __syncthreads();
     }
 
@@ -338,11 +349,12 @@ __global__ void __launch_bounds__(WARPS * 32, 1) gemv_dense_tma(const DenseParam
                               wv[r]);
 #pragma unroll
                 for (int m = 0; m < M; ++m) {
-                    const float* xr = xs + m * g.kp + kb + e0;
+                    const float* xr = xs + m * g.kp;
+                    const int c0 = (kb + e0) >> 2;   // chunk of the row: kb + e0 is a multiple of 4
                     float2 xv[EPV / 2];
 #pragma unroll
                     for (int q = 0; q < EPV / 4; ++q) {
-                        const float4 t = *reinterpret_cast<const float4*>(xr + 4 * q);
+                        const float4 t = *reinterpret_cast<const float4*>(xr + 4 * (kSwz ? xswz(c0 + q) : c0 + q));
                         xv[2 * q] = make_float2(t.x, t.y);
                         xv[2 * q + 1] = make_float2(t.z, t.w);
                     }
@@ -408,7 +420,7 @@ cudaError_t launch_tma(cudaStream_t s, bool pdl, int num_sms, const DenseParams&
     DenseGeom g;
     g.ksteps = (int)(((long long)p.K * ES + kDRowBytes - 1) / kDRowBytes);
     g.ntiles = (p.N + kDTR - 1) / kDTR;
-    g.kp = (p.K + 3) & ~3;
+    g.kp = (p.K + 7) & ~7;   // an even number of 16-byte chunks per row (xswz stays in the row)
     {
         const int xes = XK == kF32 ? 4 : 2;
         g.xvec = (reinterpret_cast<uintptr_t>(p.x) & 15) == 0 && ((long long)p.ldx * xes) % 16 == 0 &&
