@@ -151,3 +151,30 @@ def test_row_slices_match_reference_rule():
             assert [shard.row_slice(N, t, parts) for t in range(parts)] == \
                    [O.gemv_slice(N, t, parts) for t in range(parts)]
     assert shard.shard_sizes(128256, 8) == [16032] * 8
+
+
+def test_stub_matches_extension():
+    """simd_ml_kernels/_core.pyi names every public function of the extension
+    with its parameter names, order, keyword-only markers and defaults, as
+    pybind11 states them on the first docstring line (a stub that drifts
+    from the module would mislead a type checker)."""
+    import ast
+    from simd_ml_kernels import _core
+    stub = ast.parse(open(os.path.join(os.path.dirname(sk.__file__), "_core.pyi"), encoding="utf-8").read())
+    stubs = {n.name: n for n in stub.body if isinstance(n, ast.FunctionDef)}
+    public = sorted(n for n in dir(_core) if not n.startswith("_") and callable(getattr(_core, n))
+                    and not isinstance(getattr(_core, n), type))
+    assert sorted(stubs) == public
+
+    def params(fn):
+        a = fn.args
+        pos = [p.arg for p in a.args]
+        pos_def = [None] * (len(pos) - len(a.defaults)) + [ast.literal_eval(d) for d in a.defaults]
+        kw = [p.arg for p in a.kwonlyargs]
+        kw_def = [None if d is None else ast.literal_eval(d) for d in a.kw_defaults]
+        return list(zip(pos, pos_def)), list(zip(kw, kw_def))
+
+    for name in public:
+        head = getattr(_core, name).__doc__.strip().splitlines()[0].split(") ->")[0] + ")"
+        runtime = ast.parse(f"def {head}: ...").body[0]
+        assert params(runtime) == params(stubs[name]), name
