@@ -358,10 +358,12 @@ __global__ void __launch_bounds__(WARPS * 32, 1) gemv_dense_tma(const DenseParam
                         xv[2 * q] = make_float2(t.x, t.y);
                         xv[2 * q + 1] = make_float2(t.z, t.w);
                     }
+                    // j outer, rows inner: consecutive FFMA2s feed different
+                    // accumulators (each still adds its terms in j order).
 #pragma unroll
-                    for (int r = 0; r < kDTR; ++r)
+                    for (int j = 0; j < EPV / 2; ++j)
 #pragma unroll
-                        for (int j = 0; j < EPV / 2; ++j) acc[r][m] = __ffma2_rn(wv[r][j], xv[j], acc[r][m]);
+                        for (int r = 0; r < kDTR; ++r) acc[r][m] = __ffma2_rn(wv[r][j], xv[j], acc[r][m]);
                 }
             }
         }

@@ -158,13 +158,15 @@ __global__ void __launch_bounds__(WARPS * 32, 1) gemv_u8s8_tma(const U8S8Params 
 #pragma unroll
                 for (int r = 0; r < kITR; ++r) wv[r] = *reinterpret_cast<const uint4*>(st + r * kIRowBytes + e0);
                 if (zp) {
+                    // Word outer, rows inner: consecutive dp4a feed different sums.
 #pragma unroll
-                    for (int r = 0; r < kITR; ++r) {
-                        sb[r] = dp4a_ss(wv[r].x, 0x01010101u, sb[r]);
-                        sb[r] = dp4a_ss(wv[r].y, 0x01010101u, sb[r]);
-                        sb[r] = dp4a_ss(wv[r].z, 0x01010101u, sb[r]);
-                        sb[r] = dp4a_ss(wv[r].w, 0x01010101u, sb[r]);
-                    }
+                    for (int r = 0; r < kITR; ++r) sb[r] = dp4a_ss(wv[r].x, 0x01010101u, sb[r]);
+#pragma unroll
+                    for (int r = 0; r < kITR; ++r) sb[r] = dp4a_ss(wv[r].y, 0x01010101u, sb[r]);
+#pragma unroll
+                    for (int r = 0; r < kITR; ++r) sb[r] = dp4a_ss(wv[r].z, 0x01010101u, sb[r]);
+#pragma unroll
+                    for (int r = 0; r < kITR; ++r) sb[r] = dp4a_ss(wv[r].w, 0x01010101u, sb[r]);
                 }
 #pragma unroll
                 for (int m = 0; m < M; ++m) {
@@ -172,12 +174,13 @@ __global__ void __launch_bounds__(WARPS * 32, 1) gemv_u8s8_tma(const U8S8Params 
                     if constexpr (kASmem) av = *reinterpret_cast<const uint4*>(as + (size_t)m * g.kp + kb + e0);
                     else av = ld_nc_v4(p.a + (size_t)m * p.lda + kb + e0);
 #pragma unroll
-                    for (int r = 0; r < kITR; ++r) {
-                        sab[r][m] = dp4a_us(av.x, wv[r].x, sab[r][m]);
-                        sab[r][m] = dp4a_us(av.y, wv[r].y, sab[r][m]);
-                        sab[r][m] = dp4a_us(av.z, wv[r].z, sab[r][m]);
-                        sab[r][m] = dp4a_us(av.w, wv[r].w, sab[r][m]);
-                    }
+                    for (int r = 0; r < kITR; ++r) sab[r][m] = dp4a_us(av.x, wv[r].x, sab[r][m]);
+#pragma unroll
+                    for (int r = 0; r < kITR; ++r) sab[r][m] = dp4a_us(av.y, wv[r].y, sab[r][m]);
+#pragma unroll
+                    for (int r = 0; r < kITR; ++r) sab[r][m] = dp4a_us(av.z, wv[r].z, sab[r][m]);
+#pragma unroll
+                    for (int r = 0; r < kITR; ++r) sab[r][m] = dp4a_us(av.w, wv[r].w, sab[r][m]);
                 }
             }
         }

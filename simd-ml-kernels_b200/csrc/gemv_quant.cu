@@ -215,16 +215,16 @@ __device__ __forceinline__ void block_dot(const uint32_t (&q)[8], float dw, cons
         int isum;
         if constexpr (F == kQ4_0) {
             // q[0..3]: the 16 nibble bytes; low nibbles are values 0-15, high 16-31.
-            int a = __float_as_int(db.y);
-            a = dp4a_us(q[0] & 0x0F0F0F0Fu, xl.x, a);
-            a = dp4a_us(q[1] & 0x0F0F0F0Fu, xl.y, a);
-            a = dp4a_us(q[2] & 0x0F0F0F0Fu, xl.z, a);
-            a = dp4a_us(q[3] & 0x0F0F0F0Fu, xl.w, a);
+            // Four chains of two dp4a each (integer sums: any grouping is exact).
+            int a = dp4a_us(q[0] & 0x0F0F0F0Fu, xl.x, __float_as_int(db.y));
+            int a2 = dp4a_us(q[1] & 0x0F0F0F0Fu, xl.y, 0);
             int h = dp4a_us(q[0] & 0xF0F0F0F0u, xh.x, 0);
-            h = dp4a_us(q[1] & 0xF0F0F0F0u, xh.y, h);
+            int h2 = dp4a_us(q[1] & 0xF0F0F0F0u, xh.y, 0);
+            a = dp4a_us(q[2] & 0x0F0F0F0Fu, xl.z, a);
+            a2 = dp4a_us(q[3] & 0x0F0F0F0Fu, xl.w, a2);
             h = dp4a_us(q[2] & 0xF0F0F0F0u, xh.z, h);
-            h = dp4a_us(q[3] & 0xF0F0F0F0u, xh.w, h);
-            isum = a + (h >> 4);   // h is 16·Σ hi·x: exact
+            h2 = dp4a_us(q[3] & 0xF0F0F0F0u, xh.w, h2);
+            isum = (a + a2) + ((h + h2) >> 4);   // h + h2 is 16·Σ hi·x: exact
         } else {
             int a = dp4a_ss(q[0], xl.x, 0);
             a = dp4a_ss(q[1], xl.y, a);
