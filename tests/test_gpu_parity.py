@@ -680,6 +680,8 @@ def _u8s8_case(seed, M, N, K):
     (8, 2048, 28672, 77),      # A too large for shared memory: read through L1
     (3, 17, 40, 9),            # K % 16 != 0: the per-byte kernel
     (1, 8, 1049600, 128),      # more than 1024 items per row: the per-byte kernel's int64 sums
+    (8, 3000, 4096, 77),       # tensor-core kernel: 8 rows, Σ W by an extra MMA, ragged N, K split
+    (5, 777, 1040, 200),       # tensor-core kernel: Σ W from a row of ones, K tail inside an item
 ])
 def test_u8s8_shapes_bitwise_oracle(sk, torch, M, N, K, zp):
     A, W, scales = _u8s8_case(M * 131 + N + K, M, N, K)
