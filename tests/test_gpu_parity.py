@@ -639,6 +639,34 @@ def test_dense_streaming_edges(sk, kind, M, N, K):
         assert (np.abs(C - want) <= bound).all(), f"{kind} alpha={alpha}: max err/bound {np.max(np.abs(C - want) / bound):.3g}"
 
 
+def test_dense_bf16_special_values(sk, torch):
+    """bfloat16 weights with several rows of fp32 x: an infinity in x gives
+    infinities of the right signs, a NaN gives NaN (IEEE arithmetic, as the
+    reference's fp32 loops), and a value near the fp32 maximum or tiny values
+    stay within the bound of the float64 sums."""
+    M, N, K = 6, 64, 256
+    rng = np.random.default_rng(21)
+    W32 = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    Wb = O.bf16_bits(W32)
+    X = rng.standard_normal((M, K)).astype(np.float32)
+    X[1, 17] = np.inf
+    X[2, 100] = np.nan
+    X[3, 5] = 3.0e38
+    X[4] *= np.float32(1e-30)
+    X[5, 200] = -np.inf
+    Y = sk.gemv_dense(torch.from_numpy(X).cuda(), torch.from_numpy(W32).to(torch.bfloat16).cuda()).cpu().numpy()
+    Wf = O.bf16_to_f32(Wb).astype(np.float64)
+    with np.errstate(invalid="ignore", over="ignore"):
+        want = X.astype(np.float64) @ Wf.T
+    for m in (1, 5):
+        assert np.isinf(Y[m]).all() and (np.sign(Y[m]) == np.sign(want[m])).all(), f"row {m}"
+    assert np.isnan(Y[2]).all()
+    for m in (0, 3, 4):
+        y64, mag = O.dense_ref64(X[m:m + 1], "f32", Wb, "bf16")
+        bound = 2 * (K + 2) * U * mag + 1e-300
+        assert (np.abs(Y[m:m + 1] - y64) <= bound).all(), f"row {m}"
+
+
 def test_dense_rejects_non_decode(sk):
     A = np.ones((9, 16), np.float32)
     B = np.ones((4, 16), np.float32)
