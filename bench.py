@@ -1,27 +1,38 @@
 """bench.py — decode-GEMV throughput on B200.
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--all]
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Workload: Q4_0 decode GEMV y = x @ W.T, M = 1, K = 2048,
-N = 8192 per GPU; W ~ N(0, 0.02) from seed 0 quantized ggml-style (the
-device quantizer, byte-identical to the reference's), x ~ N(0, 1). A step is
-one GEMV over the whole matrix. The timed region holds exactly K steps,
-launched as CUDA graphs with programmatic dependent launch; consecutive steps
-read different weight copies, together more than 2x the L2 cache, so every
-step streams its weights from HBM. value = algorithmic bytes (W + x + y per
-step, the reference's convention, _cli.py:1198) of all steps of all ranks /
-max-over-ranks device time.
+Headline workload: Q4_0 decode GEMV y = x @ W.T, M = 1,
+K = 2048, N = 8192 per GPU; W ~ N(0, 0.02) drawn by numpy's default_rng(0)
+in 8192-row chunks (then x ~ N(0, 1) from the same generator), quantized
+ggml-style on the device (byte-identical to the reference's quantize_q4_0).
+A step is one GEMV over the whole matrix. value = algorithmic bytes (W + x +
+y per step, the reference's convention, _cli.py:1198) of all steps of all
+ranks / max-over-ranks device time of exactly K steps.
 
-N > 1 (torchrun): weak scaling. Each rank holds its 8192-row slice of a
-[8192*N, 2048] matrix (the reference's row slicing, gemv_slice), and every
-step all-gathers the y slices over NVLink, so every rank ends the step with
-all 8192*N outputs: by default inside the GEMV kernel (it stores its slice
-into every rank's buffer through CUDA IPC mappings; a one-warp kernel then
-waits for the peers' signals), or with NCCL (--gather nccl).
+Timing. The steps are CUDA-graph launches chained with programmatic dependent
+launch; consecutive steps read different weight copies, together more than
+2x the L2 cache, so every step streams its weights from HBM. The start and
+end events are recorded inside the graphs (the start one on a forked stream,
+after a full rotation of untimed steps), so the K timed steps are the steady
+state of a decode chain and no graph-launch latency falls inside them.
+
+The same line carries every BASELINE config on one GPU (config 1 Q8_0,
+config 2 Llama-3.2-1B GEMV stack, config 3 dense, config 4 large Q4_0 at
+M = 1 and 8), each with its roofline fraction and the reference's CPU
+kernel timed on this host with all threads and with one pinned thread.
+
+N > 1 (torchrun): weak scaling for the headline (each rank holds its 8192-row
+slice of a [8192*N, 2048] matrix, the reference's row slicing, and every step
+all-gathers y over NVLink inside the GEMV), plus config 4 split by rows over
+the ranks (strong scaling).
 
 --impl reference: the reference's own CPU kernel (Mattral/simd-ml-kernels
-compiled from its sources, oracle/_ref) on the same workload with every host
-thread, rank 0 only.
+compiled from its sources, oracle/_ref) on the same workload and config with
+every host thread, rank 0 only; a step is one rotation over its weight copies.
+
+The workload generators (Workload, LLAMA_MATRICES, ...) are shared with the
+parity tests, which pin the quantized bytes by SHA-256.
 
 One JSON line on rank 0.
 """
@@ -29,8 +40,10 @@ One JSON line on rank 0.
 from __future__ import annotations
 
 import argparse
+import concurrent.futures as cf
 import json
 import os
+import queue
 import statistics
 import sys
 import threading
@@ -46,9 +59,81 @@ N_ROWS, K_COLS = 8192, 2048
 Q4_ROW_BYTES = K_COLS // 32 * 18
 W_BYTES = N_ROWS * Q4_ROW_BYTES
 STEP_BYTES = W_BYTES + 4 * K_COLS + 4 * N_ROWS          # 9,478,144 (W + x + y)
-LLAMA_SHAPES = [(2048, 2048), (512, 2048), (512, 2048), (2048, 2048), (8192, 2048), (8192, 2048), (2048, 8192)]
-LLAMA_LAYERS, LLAMA_VOCAB, LLAMA_TOKENS = 16, 128256, 128
+ROW_CHUNK = 8192
+BLOCK_BYTES = {"q4_0": 18, "q8_0": 34}
 
+# ---- the BASELINE workloads ------------------------------------------------------------
+
+CFG1_SHAPES = [(512, 2048), (2048, 2048), (8192, 2048), (2048, 8192)]     # (N, K), Q8_0, seed 1
+CFG3_SHAPES = [(4096, 4096), (14336, 4096)]                               # (N, K), dense, seed 3
+CFG3_ROWS = (1, 4, 8)
+CFG4_SHAPES = [(28672, 8192), (8192, 28672), (128256, 8192)]              # (N, K), Q4_0, seed 4
+CFG4_ROWS = (1, 8)
+# Llama-3.2-1B: per layer q, k, v, o, gate, up, down (N, K), then the tied LM head.
+LLAMA_LAYER = [(2048, 2048), (512, 2048), (512, 2048), (2048, 2048), (8192, 2048), (8192, 2048), (2048, 8192)]
+LLAMA_LAYERS, LLAMA_VOCAB, LLAMA_TOKENS = 16, 128256, 128
+LLAMA_MATRICES = LLAMA_LAYER * LLAMA_LAYERS + [(LLAMA_VOCAB, 2048)]       # 113 GEMVs per token
+
+
+class Workload:
+    """W ~ N(0, sigma) [N, K] and then x ~ N(0, 1) [M, K], both from one numpy
+    generator: W in 8192-row chunks (float64 normals times sigma, rounded to
+    float32), the order of the reference's bench (_cli.py:948-966), so a
+    128256-row matrix is never held whole in float32. `entropy` is the seed (an
+    int) or a sequence of ints for numpy's SeedSequence. x exists only after
+    every chunk has been drawn."""
+
+    def __init__(self, entropy, N: int, K: int, sigma: float, M: int = 1):
+        self.entropy, self.N, self.K, self.sigma, self.M = entropy, N, K, sigma, M
+        self.x = None
+
+    def chunks(self):
+        rng = np.random.default_rng(self.entropy)
+        for r0 in range(0, self.N, ROW_CHUNK):
+            rows = min(ROW_CHUNK, self.N - r0)
+            yield r0, (rng.standard_normal((rows, self.K)) * self.sigma).astype(np.float32)
+        self.x = rng.standard_normal((self.M, self.K)).astype(np.float32)
+
+    def full(self):
+        """(W [N, K] float32, x [M, K] float32)."""
+        W = np.concatenate([c for _, c in self.chunks()]) if self.N else np.empty((0, self.K), np.float32)
+        return W, self.x
+
+
+def config0(world: int = 1) -> Workload:
+    """Config 0; for N GPUs the [8192*N, 2048] matrix whose first 8192 rows are config 0's."""
+    return Workload(0, N_ROWS * world, K_COLS, 0.02)
+
+
+def config1(N: int, K: int) -> Workload:
+    return Workload(1, N, K, 0.02)
+
+
+def config3(N: int, K: int) -> Workload:
+    return Workload(3, N, K, 0.02, M=max(CFG3_ROWS))
+
+
+def config4(N: int, K: int) -> Workload:
+    return Workload(4, N, K, 0.015, M=max(CFG4_ROWS))
+
+
+def config2(i: int) -> Workload:
+    """Matrix i of the Llama stack (LLAMA_MATRICES order), its own generator
+    seeded (2, i) so the 113 matrices can be drawn in parallel."""
+    N, K = LLAMA_MATRICES[i]
+    return Workload([2, i], N, K, 0.02, M=0)
+
+
+def q_bytes(fmt: str, N: int, K: int) -> int:
+    return N * (K // 32) * BLOCK_BYTES[fmt]
+
+
+def gemv_bytes(wbytes: int, M: int, N: int, K: int, xsize: int = 4) -> int:
+    """Algorithmic bytes of one call: W + x + y, each once (_cli.py:1198)."""
+    return wbytes + xsize * M * K + 4 * M * N
+
+
+# ---- host-side helpers -------------------------------------------------------------------
 
 def measured_peaks() -> dict:
     p = os.path.join(REPO, "MEASURED_PEAKS.json")
@@ -68,13 +153,18 @@ def committed_traffic(name: str):
     return None
 
 
-# ---- clocks during the timed region (NVML) --------------------------------------
+def quantiles(ts: list[float]) -> dict:
+    q = statistics.quantiles(ts, n=4) if len(ts) >= 4 else [min(ts), statistics.median(ts), max(ts)]
+    return {"p25": q[0], "median": statistics.median(ts), "p75": q[2], "mean": sum(ts) / len(ts)}
+
 
 class ClockSampler:
+    """SM clock and throttle reasons through NVML, sampled while the GPU is under load."""
+
     REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
                "sw_power_cap": 0x4, "hw_power_brake_slowdown": 0x80}
 
-    def __init__(self, device: int, period_s: float = 0.01):
+    def __init__(self, device: int, period_s: float = 0.005):
         self.samples, self.reasons, self.period = [], set(), period_s
         self.max_mhz = None
         self._stop = threading.Event()
@@ -116,8 +206,6 @@ class ClockSampler:
                 "reasons": sorted(self.reasons), "samples": len(self.samples)}
 
 
-# ---- the reference's CPU kernel -------------------------------------------------------
-
 def llc_bytes() -> int:
     """Total last-level cache of the host: every distinct cache instance of the
     highest level, summed (a multi-die CPU has several L3s)."""
@@ -143,87 +231,383 @@ def llc_bytes() -> int:
     return total or 64 << 20
 
 
-def reference_setup(threads: int):
-    sys.path.insert(0, os.path.join(REPO, "oracle"))
-    import oracle as O
-
-    if not O.ref_available():
-        return None
-    R = O.ref()
-    R.smkref_set_num_threads(threads)
-    rng = np.random.default_rng(0)
-    W = (rng.standard_normal((N_ROWS, K_COLS)) * 0.02).astype(np.float32)
-    x = rng.standard_normal(K_COLS).astype(np.float32)
-    Wq = O.ref_quantize("q4_0", W)
-    copies = max(2, -(-2 * llc_bytes() // W_BYTES))
-    ws = [Wq] + [Wq.copy() for _ in range(copies - 1)]
-    y = np.empty(N_ROWS, np.float32)
-    state = {"i": 0}
-
-    def call():
-        state["i"] = (state["i"] + 1) % copies
-        R.smkref_gemv_q4_0(-1, N_ROWS, K_COLS, x.ctypes.data, ws[state["i"]].ctypes.data, y.ctypes.data)
-
-    return call, copies, R.smkref_q8_0_path().decode()
-
-
 def cpu_threads() -> int:
     return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count() or 1
 
 
-def time_reference(steps: int | None, warmup: int, budget_s: float):
-    """GB/s of the reference's gemv_q4_0 on the config-0 workload, every host thread."""
-    th = cpu_threads()
-    setup = reference_setup(th)
-    if setup is None:
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+# ---- the reference's CPU kernels ----------------------------------------------------------
+
+class RefCPU:
+    """The reference library compiled from its sources (oracle/_ref), timed on
+    this host: all host threads, or one thread pinned to one core. Each case
+    rotates weight copies past the host's last-level caches (the reference's
+    _Rotor rule, _cli.py:569-581) and is warmed over at least one rotation
+    before it is timed."""
+
+    def __init__(self):
+        sys.path.insert(0, os.path.join(REPO, "oracle"))
+        import oracle as O
+        self.O = O
+        self.ok = O.ref_available()
+        if self.ok:
+            self.R = O.ref()
+            self.path = self.R.smkref_q8_0_path().decode()
+        self.threads = cpu_threads()
+        self.llc = llc_bytes()
+
+    def copies(self, nbytes: int) -> int:
+        return max(2, -(-2 * self.llc // max(1, nbytes)))
+
+    def time(self, calls, nbytes_per_call: int, seconds: float, threads: int | None = None,
+             pin: bool = False) -> dict:
+        """calls: one callable per weight copy (a rotation). GB/s from the median call."""
+        R = self.R
+        th = threads or self.threads
+        old = os.sched_getaffinity(0) if pin else None
+        try:
+            if pin:
+                os.sched_setaffinity(0, {min(old)})
+            R.smkref_set_num_threads(th)
+            n = len(calls)
+            t0 = time.perf_counter()
+            i = 0
+            while i < n or time.perf_counter() - t0 < min(0.2, seconds / 3):   # warm: >= one rotation
+                calls[i % n]()
+                i += 1
+            ts = []
+            t0 = time.perf_counter()
+            while len(ts) < max(n, 3) or time.perf_counter() - t0 < seconds:
+                a = time.perf_counter()
+                calls[len(ts) % n]()
+                ts.append(time.perf_counter() - a)
+        finally:
+            if pin:
+                os.sched_setaffinity(0, old)
+        q = quantiles(ts)
+        return {"gb_s": round(nbytes_per_call / q["median"] / 1e9, 3), "us_median": round(q["median"] * 1e6, 3),
+                "us_p25": round(q["p25"] * 1e6, 3), "us_p75": round(q["p75"] * 1e6, 3), "calls": len(ts),
+                "threads": 1 if pin else th, "pinned": pin, "weight_copies": n}
+
+    def both(self, calls, nbytes: int, seconds: float = 0.3) -> dict:
+        return {"all_threads": self.time(calls, nbytes, seconds), "one_thread": self.time(calls, nbytes, seconds,
+                                                                                           threads=1, pin=True)}
+
+    # Calls of the reference's table entries on host arrays.
+    def gemv_q(self, fmt, ws, x, N, K):
+        fn = self.R.smkref_gemv_q4_0 if fmt == "q4_0" else self.R.smkref_gemv_q8_0
+        X = np.ascontiguousarray(x, np.float32).reshape(-1, K)
+        y = np.empty((X.shape[0], N), np.float32)
+
+        def mk(w):
+            def call():   # the reference has no batched quantized GEMV: one call per row of x
+                for m in range(X.shape[0]):
+                    fn(-1, N, K, X[m].ctypes.data, w.ctypes.data, y[m].ctypes.data)
+            return call
+        return [mk(w) for w in ws]
+
+    def dense(self, kind, ws, X, N, K):
+        M = X.shape[0]
+        C = np.empty((M, N), np.float32)
+        if kind == "float32":
+            A = np.ascontiguousarray(X, np.float32)
+            fn = self.R.smkref_sgemm_tb
+        else:   # the reference's 16-bit GEMV takes x in the same 16-bit type (_cli.py:1189-1194)
+            import torch
+            t = torch.from_numpy(np.ascontiguousarray(X)).to(getattr(torch, kind))
+            A = t.view(torch.int16).numpy().view(np.uint16)
+            fn = self.R.smkref_sgemm_f16_tb if kind == "float16" else self.R.smkref_sgemm_bf16_tb
+        return [lambda w=w: fn(-1, M, N, K, 1.0, A.ctypes.data, w.ctypes.data, 0.0, C.ctypes.data) for w in ws]
+
+
+def time_reference_arm(steps: int, warmup: int, world: int) -> dict | None:
+    """The reference's gemv_q4_0 on the headline workload (the GPU arm's config at
+    this world size), every host thread. A step is a bounded sample: whole
+    rotations over the weight copies, as many as take about 20 ms; exactly
+    `steps` steps are timed after `warmup` untimed ones and at least half a
+    second of untimed calls (the thread team and the core clocks settle)."""
+    ref = RefCPU()
+    if not ref.ok:
         return None
-    call, copies, path = setup
-    for _ in range(max(warmup, 1)):
-        call()
+    wl = config0(world)
+    W, x = wl.full()
+    Wq = ref.O.ref_quantize("q4_0", W)
+    del W
+    N = wl.N
+    wb = q_bytes("q4_0", N, K_COLS)
+    copies = ref.copies(wb)
+    ws = [Wq] + [Wq.copy() for _ in range(copies - 1)]
+    calls = ref.gemv_q("q4_0", ws, x[0], N, K_COLS)
+    ref.R.smkref_set_num_threads(ref.threads)
     t0 = time.perf_counter()
-    n = 0
-    while (steps is not None and n < steps) or (steps is None and time.perf_counter() - t0 < budget_s):
-        call()
-        n += 1
+    rot = 0
+    while rot < 1 or time.perf_counter() - t0 < 0.5:
+        for c in calls:
+            c()
+        rot += 1
+    rots = max(1, round(0.02 / ((time.perf_counter() - t0) / rot)))   # rotations per step
+    for _ in range(warmup * rots):
+        for c in calls:
+            c()
+    t0 = time.perf_counter()
+    for _ in range(steps * rots):
+        for c in calls:
+            c()
     dt = time.perf_counter() - t0
-    return {"value": STEP_BYTES * n / dt / 1e9, "unit": "GB/s", "cores": th, "kind": "reference", "calls": n,
-            "seconds": dt, "sample": f"{n} gemv_q4_0 calls, N=8192 K=2048, {copies} weight copies rotated "
-                                   f"past the host LLC, path {path}, {th} threads"}
+    per_call = STEP_BYTES * world
+    n = steps * rots * copies
+    return {"value": per_call * n / dt / 1e9, "seconds": dt, "calls": n,
+            "ms_per_step": dt / steps * 1e3, "cores": ref.threads, "path": ref.path, "copies": copies,
+            "sample": f"{steps} steps of {rots * copies} gemv_q4_0 calls ({rots} rotations over {copies} weight "
+                      f"copies, past the host LLC of {ref.llc >> 20} MiB), N={N} K={K_COLS}, path {ref.path}, "
+                      f"{ref.threads} threads, {cpu_model()}"}
 
 
-# ---- the GPU arm ---------------------------------------------------------------------------
+def headline_config(world: int) -> dict:
+    """The `config` of the headline line, identical in both arms."""
+    return {"workload": "config 0: Q4_0 decode GEMV M=1 K=2048 N=8192" +
+                        (f" per GPU, rows sharded over {world} GPUs (N={N_ROWS * world} in all), y all-gathered"
+                         if world > 1 else ""),
+            "M": 1, "K": K_COLS, "N": N_ROWS * world, "seed": 0, "weights": "N(0, 0.02) -> ggml Q4_0",
+            "bytes_per_step": STEP_BYTES * world}
+
+
+# ---- GPU timing -------------------------------------------------------------------------------
+
+def chained_ms(torch, dev, stream, step, n: int, period: int, pre: int | None = None, chunk: int = 512,
+               barrier=None, load_s: float = 0.0, sampler=None) -> float:
+    """Device milliseconds of exactly n consecutive calls step(i) on `stream`.
+
+    The calls are captured into CUDA graphs, so consecutive kernels keep their
+    programmatic-dependent-launch edges. The first graph runs `pre` untimed
+    calls (one rotation of the weight copies by default), then records the
+    start event on a forked stream (the next call keeps its edge to the
+    previous one), then timed calls; the last graph ends with the end event.
+    step(i) must use weight copy i % period; graphs hold multiples of `period`
+    calls, so their replays continue the rotation. Every graph is replayed
+    once before the timed replays; `load_s` seconds of untimed replays (with
+    `sampler` running) precede the timed ones. `barrier` (multi-rank) is
+    called with the device synchronised right before and after the timed
+    replays; every rank must pass the same n, period and load count."""
+    pre = period if pre is None else pre
+    chunk = max(period, chunk // period * period)
+    side = torch.cuda.Stream(device=dev)
+    ev0 = torch.cuda.Event(enable_timing=True, external=True)
+    ev1 = torch.cuda.Event(enable_timing=True, external=True)
+    first = min(n, chunk)
+    rest = n - first
+    mids, last = divmod(rest, chunk)
+    if last == 0 and mids > 0:
+        mids, last = mids - 1, chunk
+
+    def capture(base: int, count: int, start: bool, end: bool, lead: int = 0):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            with torch.cuda.graph(g, stream=stream):
+                for i in range(lead):
+                    step(i)
+                if start:
+                    side.wait_stream(stream)
+                    ev0.record(side)
+                for i in range(count):
+                    step(base + i)
+                if end:
+                    ev1.record(stream)
+                if start:
+                    stream.wait_stream(side)
+        return g
+
+    with torch.cuda.stream(stream):
+        step(0)   # first-use set-up (scratch, launch caches) outside any capture
+    torch.cuda.synchronize(dev)
+    g_first = capture(pre, first, True, last == 0, lead=pre)
+    g_mid = capture(pre + first, chunk, False, False) if mids else None
+    g_last = capture(pre + first, last, False, True) if last else None
+    g_load = g_mid or capture(0, chunk, False, False)
+    with torch.cuda.stream(stream):
+        for g in (g_first, g_mid, g_last, g_load):
+            if g is not None:
+                g.replay()
+    torch.cuda.synchronize(dev)
+
+    def run_load():
+        if load_s <= 0:
+            return
+        t0 = time.perf_counter()
+        with torch.cuda.stream(stream):
+            g_load.replay()
+        torch.cuda.synchronize(dev)
+        one = max(time.perf_counter() - t0, 1e-5)
+        reps = int(min(2000, max(1, load_s / one)))
+        if barrier is not None:   # the same count on every rank
+            t = torch.tensor([reps], device=dev)
+            barrier(t)
+            reps = int(t.item())
+        with torch.cuda.stream(stream):
+            for _ in range(reps):
+                g_load.replay()
+
+    outer = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+    if sampler is not None:
+        with sampler:
+            run_load()
+            _timed(torch, dev, stream, g_first, g_mid, mids, g_last, barrier, outer)
+    else:
+        run_load()
+        _timed(torch, dev, stream, g_first, g_mid, mids, g_last, barrier, outer)
+    try:
+        ms = ev0.elapsed_time(ev1)
+    except RuntimeError:   # events recorded by graph nodes not readable: time the replays instead
+        ms = outer[0].elapsed_time(outer[1])
+        CHAINED_FALLBACKS.append(n)
+    del g_first, g_mid, g_last, g_load
+    return ms
+
+
+CHAINED_FALLBACKS: list[int] = []   # chained_ms calls that had to time whole graph replays
+
+
+def _timed(torch, dev, stream, g_first, g_mid, mids, g_last, barrier, outer):
+    torch.cuda.synchronize(dev)
+    if barrier is not None:
+        barrier(None)
+    torch.cuda.synchronize(dev)
+    with torch.cuda.stream(stream):
+        outer[0].record(stream)
+        g_first.replay()
+        for _ in range(mids):
+            g_mid.replay()
+        if g_last is not None:
+            g_last.replay()
+        outer[1].record(stream)
+    torch.cuda.synchronize(dev)
+    if barrier is not None:
+        barrier(None)
+
+
+class Producer:
+    """Draws Workload chunks on worker threads (numpy releases the GIL while it
+    fills arrays), in submission order, at most `ahead` chunks per workload
+    waiting. Consume workloads in the order they were submitted."""
+
+    def __init__(self, workers: int = 6, ahead: int = 2):
+        self.pool = cf.ThreadPoolExecutor(max_workers=workers)
+        self.ahead = ahead
+
+    def submit(self, wl: Workload, lo: int = 0, hi: int | None = None):
+        """Rows [lo, hi) of wl's chunks (the whole stream is still drawn, for x)."""
+        q = queue.Queue(maxsize=self.ahead)
+        hi = wl.N if hi is None else hi
+
+        def run():
+            try:
+                for r0, c in wl.chunks():
+                    r1 = r0 + c.shape[0]
+                    if r1 > lo and r0 < hi:
+                        q.put((max(r0, lo), c[max(r0, lo) - r0:min(r1, hi) - r0]))
+                q.put(None)
+            except BaseException as e:  # noqa: BLE001
+                q.put(e)
+        self.pool.submit(run)
+        return wl, q
+
+    def close(self):
+        self.pool.shutdown(wait=True)
+
+
+def device_weights(torch, sk, dev, job, fmt: str | None, dtype=None):
+    """The rows a Producer job delivers, on the device: quantized to `fmt` by the
+    device quantizer, or rounded (round to nearest even) to `dtype`."""
+    wl, q = job
+    out = []
+    while True:
+        item = q.get()
+        if item is None:
+            break
+        if isinstance(item, BaseException):
+            raise item
+        _, c = item
+        t = torch.from_numpy(c).to(dev)
+        if fmt == "q4_0":
+            out.append(sk.quantize_q4_0(t))
+        elif fmt == "q8_0":
+            out.append(sk.quantize_q8_0(t))
+        else:
+            out.append(t.to(dtype))
+        del t
+    w = torch.cat(out) if len(out) > 1 else out[0]
+    return w, wl.x
+
+
+def roofline(nbytes: int, us: float, peak: dict) -> dict:
+    achieved = nbytes / (us * 1e-6) / 1e9
+    return {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak["hbm_gbs"], "unit": "GB/s",
+            "frac": round(achieved / peak["hbm_gbs"], 4), "of": peak["source"]}
+
 
 def gpu_bench(args, rank: int, world: int, local_rank: int) -> dict | None:
     import torch
     import torch.distributed as dist
 
     import simd_ml_kernels as sk
-    from simd_ml_kernels import shard
+    from simd_ml_kernels import _core, shard
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     sk.set_pdl(True, local_rank)
     props = torch.cuda.get_device_properties(dev)
     l2 = getattr(props, "L2_cache_size", 126 << 20)
+    peak = measured_peaks()
+    stream = torch.cuda.Stream(device=dev)
 
-    # Weights: this rank's 8192 rows of the [8192*world, 2048] matrix (seed 0 for rank 0).
-    g = torch.Generator(device=dev)
-    g.manual_seed(0 + rank)
-    W = torch.randn((N_ROWS, K_COLS), generator=g, device=dev) * 0.02
-    Wq0 = sk.quantize_q4_0(W).reshape(-1)
-    del W
+    def barrier(t):
+        if world > 1:
+            if t is None:
+                dist.barrier()
+            else:
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+
+    full_run = not args.only_gemv
+    prod = Producer()
+    # Headline weights first; the other configs' generators run on worker
+    # threads while the headline is timed.
+    # Jobs are submitted in the order they are consumed below (the producer's
+    # bounded queues need that).
+    lo, hi = rank * N_ROWS, (rank + 1) * N_ROWS
+    j0 = prod.submit(config0(world), lo, hi)
+    jobs = {}
+    if full_run:
+        for N, K in CFG4_SHAPES:
+            slo, shi = shard.row_slice(N, rank, world)
+            jobs[("c4", N, K)] = prod.submit(config4(N, K), slo, shi)
+    if full_run and world == 1:
+        for N, K in CFG1_SHAPES:
+            jobs[("c1", N, K)] = prod.submit(config1(N, K))
+        for N, K in CFG3_SHAPES:
+            jobs[("c3", N, K)] = prod.submit(config3(N, K))
+        for i in range(len(LLAMA_MATRICES)):
+            jobs[("c2", i)] = prod.submit(config2(i))
+
+    Wq0, x0 = device_weights(torch, sk, dev, j0, "q4_0")
+    Wq0 = Wq0.reshape(-1)
     copies = max(2, -(-2 * l2 // W_BYTES) + 1)
     ws = [Wq0] + [Wq0.clone() for _ in range(copies - 1)]
-    x = torch.randn(K_COLS, generator=g, device=dev)
+    x = torch.from_numpy(x0[0]).to(dev)
     y = torch.empty(N_ROWS, device=dev)
-    Ntot = N_ROWS * world
     nvlink = world > 1 and args.gather == "nvlink"
     gathered = torch.empty((world, N_ROWS), device=dev) if world > 1 and not nvlink else None
-    sg = shard.ShardedGemv("q4_0", Wq0, Ntot, K_COLS, gather="nvlink") if nvlink else None
-
-    stream = torch.cuda.Stream(device=dev)
+    sg = shard.ShardedGemv("q4_0", Wq0, N_ROWS * world, K_COLS, gather="nvlink") if nvlink else None
     launches_per_step = 2 if nvlink else 1
-    from simd_ml_kernels import _core
 
     def one_step(i):
         if nvlink:   # GEMV storing its slice into every rank's y over NVLink, then the peers' signals
@@ -234,415 +618,416 @@ def gpu_bench(args, rank: int, world: int, local_rank: int) -> dict | None:
         if world > 1:
             dist.all_gather_into_tensor(gathered, y)
 
-    # CUDA graphs of `chunk` steps, cycling through the weight copies.
-    chunk = copies * max(1, 512 // copies)
-    steps = args.steps
-    full, rem = divmod(steps, chunk)
-
-    def capture(n):
-        gr = torch.cuda.CUDAGraph()
-        with torch.cuda.stream(stream):
-            one_step(0)   # warm the path (first-use allocations) outside capture
-            torch.cuda.synchronize(dev)
-            with torch.cuda.graph(gr, stream=stream):
-                for i in range(n):
-                    one_step(i)
-        return gr
-
-    g_full = capture(chunk) if full else None
-    g_rem = capture(rem) if rem else None
     with torch.cuda.stream(stream):
         for i in range(args.warmup):
             one_step(i)
     torch.cuda.synchronize(dev)
-
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize(dev)
-    with ClockSampler(local_rank) as clocks:
-        with torch.cuda.stream(stream):
-            start.record(stream)
-            for _ in range(full):
-                g_full.replay()
-            if g_rem is not None:
-                g_rem.replay()
-            end.record(stream)
-        torch.cuda.synchronize(dev)
-    if world > 1:
-        dist.barrier()
-    ms = start.elapsed_time(end)
+    clocks = ClockSampler(local_rank)
+    steps = args.steps
+    ms = chained_ms(torch, dev, stream, one_step, steps, copies, barrier=barrier if world > 1 else None,
+                    load_s=0.3, sampler=clocks)
     t = torch.tensor([ms], device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_max = float(t.item())
-    # Kernel-only time per launch (no all-gather), for the roofline: the
-    # same graphs without the collective, on this rank.
+    # Kernel-only time per step (no all-gather), for the roofline.
     kernel_ms = ms
     if world > 1:
-        gk = torch.cuda.CUDAGraph()
-        with torch.cuda.stream(stream):
-            with torch.cuda.graph(gk, stream=stream):
-                for i in range(chunk):
-                    sk.gemv_q4_0(x, ws[i % copies], N_ROWS, K_COLS, out=y)
-            s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            s2.record(stream)
-            reps = max(1, steps // chunk)
-            for _ in range(reps):
-                gk.replay()
-            e2.record(stream)
-        torch.cuda.synchronize(dev)
-        kernel_ms = s2.elapsed_time(e2) * steps / (reps * chunk)
-        del gk
-    del g_full, g_rem
+        kernel_ms = chained_ms(torch, dev, stream, lambda i: sk.gemv_q4_0(x, ws[i % copies], N_ROWS, K_COLS, out=y),
+                               steps, copies)
+    value = STEP_BYTES * world * steps / (ms_max * 1e-3) / 1e9
+    cfg = headline_config(world)
 
     if args.only_gemv:
+        prod.close()
         if rank == 0:
-            out = {"metric": METRIC, "value": round(STEP_BYTES * world * steps / (ms_max * 1e-3) / 1e9, 2),
-                   "unit": "GB/s", "n_gpus": world, "steps": steps, "ms_per_step": ms_max / steps,
-                   "only_gemv": True}
-            if args.case and world == 1:
-                out["configs"] = other_configs(sk, torch, dev, stream, args.case)
+            out = {"metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": steps,
+                   "ms_per_step": ms_max / steps, "only_gemv": True, "config": cfg,
+                   "roofline": roofline(STEP_BYTES, kernel_ms / steps * 1e3, peak)}
             return out
         return None
 
-    # End to end through the public API: x from pinned host memory, y back to
-    # host memory, weights resident on the device (uploaded once, as a model's).
-    e2e_steps = min(max(steps // 10, 200), 2000)
-    xh = torch.randn(K_COLS, generator=torch.Generator().manual_seed(1)).pin_memory()
-    xh_np = xh.numpy()
-    sk.set_pdl(False, local_rank)
+    extra = {}
+    host = {"c0": (Wq0.cpu().numpy(), x0)}   # host copies of the device-quantized weights, for the CPU arms
+    # Config 4 (all ranks: row-sharded over the world at N > 1).
+    c4 = {}
+    for N, K in CFG4_SHAPES:
+        wq, X = device_weights(torch, sk, dev, jobs[("c4", N, K)], "q4_0")
+        c4.update(sharded_case(torch, sk, _core, shard, dev, stream, N, K, wq.reshape(-1), X, rank, world,
+                               local_rank, l2, peak, barrier))
+        if world == 1:
+            host[("c4", N, K)] = (wq.reshape(-1).cpu().numpy(), X)
+        del wq
+    if rank == 0:
+        extra["config4"] = c4
+
     if world == 1:
-        for _ in range(20):
-            sk.gemv_q4_0(xh_np, ws[0], N_ROWS, K_COLS)
-        torch.cuda.synchronize(dev)
-        t0 = time.perf_counter()
-        for i in range(e2e_steps):
-            yh = sk.gemv_q4_0(xh_np, ws[i % copies], N_ROWS, K_COLS)
-        e2e_s = time.perf_counter() - t0
-        assert yh.shape == (N_ROWS,)
-        e2e_bytes_out = 4 * N_ROWS
-    else:
-        if sg is None:
-            sg = shard.ShardedGemv("q4_0", ws[0], Ntot, K_COLS)
-        yfull_h = torch.empty(Ntot).pin_memory()
-        for _ in range(20):
-            yfull_h.copy_(sg.forward(xh.to(dev, non_blocking=True)))
-        torch.cuda.synchronize(dev)
-        dist.barrier()
-        t0 = time.perf_counter()
-        for i in range(e2e_steps):
-            yfull_h.copy_(sg.forward(xh.to(dev, non_blocking=True)))
-        torch.cuda.synchronize(dev)
-        e2e_s = time.perf_counter() - t0
-        tt = torch.tensor([e2e_s], device=dev)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        e2e_s = float(tt.item())
-        e2e_bytes_out = 4 * Ntot
-    sk.set_pdl(True, local_rank)
+        extra["config1_q8_0"] = {}
+        for N, K in CFG1_SHAPES:
+            wq, X = device_weights(torch, sk, dev, jobs[("c1", N, K)], "q8_0")
+            wq = wq.reshape(-1)
+            xd = torch.from_numpy(X[0]).to(dev)
+            yd = torch.empty(N, device=dev)
+            nb = gemv_bytes(q_bytes("q8_0", N, K), 1, N, K)
+            extra["config1_q8_0"][f"q8_0 M=1 N={N} K={K}"] = rotated_case(
+                torch, dev, stream, wq, lambda w, xd=xd, yd=yd, N=N, K=K: sk.gemv_q8_0(xd, w, N, K, out=yd), nb,
+                l2, peak)
+            host[("c1", N, K)] = (wq.cpu().numpy(), X)
+        extra["config3_dense"] = {}
+        for N, K in CFG3_SHAPES:
+            W32, X = device_weights(torch, sk, dev, jobs[("c3", N, K)], None, torch.float32)
+            for wt, es in ((torch.float32, 4), (torch.bfloat16, 2), (torch.float16, 2)):
+                w = W32.to(wt)
+                kind = str(wt).split(".")[-1]
+                host[("c3", kind, N, K)] = w.view(torch.int32 if es == 4 else torch.int16).cpu().numpy()
+                for M in CFG3_ROWS:
+                    xd = torch.from_numpy(X[:M]).to(dev)
+                    yd = torch.empty((M, N), device=dev)
+                    extra["config3_dense"][f"dense {kind} M={M} N={N} K={K}"] = rotated_case(
+                        torch, dev, stream, w, lambda w_, xd=xd, yd=yd: sk.gemv_dense(xd, w_, out=yd),
+                        N * K * es + 4 * M * K + 4 * M * N, l2, peak)
+                del w
+            host[("c3x", N, K)] = X
+            del W32
+        extra["config2_llama_stack"] = llama_stack(torch, sk, dev, stream, args, jobs, peak, host)
+    prod.close()
+
+    # End to end through the public API: x from page-locked host memory, y back to host memory,
+    # weights resident on the device (uploaded once, as a model's).
+    e2e = e2e_headline(torch, sk, shard, dev, local_rank, world, ws, copies, sg, x0[0])
     if sg is not None:
         sg.close()   # release the gather buffers before the process group goes
 
-    extra = {}
-    if not args.only_gemv:
-        sharded = sharded_configs(sk, torch, dev, stream, world, rank, local_rank)
-        if rank == 0:
-            extra["sharded_config4"] = sharded
-    if rank == 0 and world == 1:
-        extra["llama_stack"] = llama_stack(sk, torch, dev, stream, args)
-        extra["llama_decode_swiglu"] = llama_stack(sk, torch, dev, stream, args, swiglu="fused")
-        extra["llama_decode_swiglu_unfused"] = llama_stack(sk, torch, dev, stream, args, swiglu="unfused")
-        if args.all or args.case:
-            extra["configs"] = other_configs(sk, torch, dev, stream, args.case)
-
     if rank != 0:
         return None
-    peaks = measured_peaks()
-    achieved = STEP_BYTES / (kernel_ms / steps * 1e-3) / 1e9
-    value = STEP_BYTES * world * steps / (ms_max * 1e-3) / 1e9
+    if world == 1:
+        extra["cpu_arms"] = cpu_arms(host, extra)
+    us = kernel_ms / steps * 1e3
+    rl = roofline(STEP_BYTES, us, peak)
+    rl.update({"traffic": committed_traffic("gemv_q4_0_cfg0_traffic.json"), "kernel": "gemv_q_fast2<Q4_0, M=1>",
+               "algorithmic_bytes_per_launch": STEP_BYTES,
+               "peak_source": peak["source"] + " (MEASURED_PEAKS.json hbm_gbs, burst copy)"})
     out = {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": steps,
         "warmup": args.warmup, "ms_per_step": ms_max / steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "q4_0 weights x int8 activations (dp4a int32, fp32 accumulate)",
-        "data": "synthetic: W ~ N(0, 0.02) seed 0 quantized ggml Q4_0 on device, x ~ N(0, 1)",
-        "config": {"workload": "config 0: Q4_0 decode GEMV M=1 K=2048 N=8192 per GPU"
-                               + ((f", rows sharded over {world} GPUs, all-gather of y fused into the GEMV "
-                                   "(stores into every rank's y over NVLink, then a wait on the peers' signals)"
-                                   if nvlink else f", rows sharded over {world} GPUs + NCCL all-gather of y")
-                                  if world > 1 else ""),
-                   "M": 1, "K": K_COLS, "N_per_gpu": N_ROWS, "N_total": Ntot,
-                   "bytes_per_step_per_gpu": STEP_BYTES,
-                   "l2_policy": f"{copies} rotated weight copies ({copies * W_BYTES / 2**20:.0f} MiB > 2x L2 "
+        "data": "synthetic: numpy default_rng(0), W ~ N(0, 0.02) quantized ggml Q4_0 on device, x ~ N(0, 1)",
+        "config": cfg,
+        "timing": {"l2_policy": f"{copies} rotated weight copies ({copies * W_BYTES / 2**20:.0f} MiB > 2x L2 "
                                 f"{l2 / 2**20:.0f} MiB): inputs larger than L2",
-                   "launch": f"CUDA graphs of {chunk} steps, programmatic dependent launch"},
-        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                     "frac": round(achieved / peaks["hbm_gbs"], 4),
-                     "traffic": committed_traffic("gemv_q4_0_cfg0_traffic.json"),
-                     "peak_source": peaks["source"] + " (MEASURED_PEAKS.json hbm_gbs, burst copy)",
-                     "kernel": "gemv_q_fast2<Q4_0, M=1>", "algorithmic_bytes_per_launch": STEP_BYTES},
-        "e2e": {"value": round(STEP_BYTES * world * e2e_steps / e2e_s / 1e9, 2), "unit": "GB/s",
-                "h2d_bytes_per_step": 4 * K_COLS, "d2h_bytes_per_step": e2e_bytes_out,
-                "us_per_step": e2e_s / e2e_steps * 1e6, "steps": e2e_steps,
-                "api": "simd_ml_kernels.gemv_q4_0(numpy x in pinned memory, device weights) -> numpy y"
-                       if world == 1 else "ShardedGemv.forward(x host->device) + y device->host"},
+                   "launch": "CUDA graphs, programmatic dependent launch; start/end events recorded inside the "
+                             f"graphs after {copies} untimed steps (steady state)"
+                             + (", NVLink gather fused into the GEMV" if nvlink else "")},
+        "roofline": rl,
+        "e2e": e2e,
         "gpu_launches": steps * launches_per_step,
         "clocks": clocks.summary(),
     }
+    if CHAINED_FALLBACKS:
+        out["timing"]["in_graph_events"] = f"unreadable; {len(CHAINED_FALLBACKS)} cases timed over whole replays"
+
     if world > 1:
         out["kernel_only_ms_per_step"] = kernel_ms / steps
     out.update(extra)
+    if world == 1:
+        cb = extra["cpu_arms"].get("config0")
+        if cb:
+            a = cb["all_threads"]
+            out["cpu_baseline"] = {"value": a["gb_s"], "unit": "GB/s", "cores": a["threads"], "kind": "reference",
+                                   "one_thread_value": cb["one_thread"]["gb_s"],
+                                   "sample": f"{a['calls']} gemv_q4_0 calls (median {a['us_median']} us), "
+                                             f"{a['weight_copies']} weight copies rotated past the host LLC, "
+                                             f"path {cb['path']}, {a['threads']} threads, {cpu_model()}; one "
+                                             f"thread pinned: {cb['one_thread']['gb_s']} GB/s"}
     return out
 
 
-def llama_stack(sk, torch, dev, stream, args, swiglu: str = "") -> dict:
-    """a Llama-3.2-1B decode step's GEMVs — 16 layers of
+def rotated_case(torch, dev, stream, w, call, nbytes: int, l2: int, peak: dict, n: int = 200) -> dict:
+    """One GPU case: `n` chained calls over weight copies totalling more than 2x L2."""
+    wb = w.numel() * w.element_size()
+    copies = max(2, -(-2 * l2 // wb) + 1)
+    ws = [w] + [w.clone() for _ in range(copies - 1)]
+    ms = chained_ms(torch, dev, stream, lambda i: call(ws[i % copies]), n, copies, chunk=max(64, copies))
+    us = ms * 1e3 / n
+    del ws
+    return {"us": round(us, 3), "gb_s": round(nbytes / (us * 1e-6) / 1e9, 1), "bytes": nbytes,
+            "roofline": roofline(nbytes, us, peak), "weight_copies": copies}
+
+
+def sharded_case(torch, sk, _core, shard, dev, stream, N, K, wq, X, rank, world, local_rank, l2, peak,
+                 barrier) -> dict:
+    """Config 4 shape (N, K): this rank's row slice at M = 1 and M = 8. N = 1: the
+    GEMV; N > 1: the GEMV with the all-gather of y (fused NVLink stores at M = 1,
+    NCCL all-gather after the tensor-core GEMV at M = 8), strong scaling, max over
+    ranks."""
+    lo, hi = shard.row_slice(N, rank, world)
+    n = hi - lo
+    copies = max(2, -(-2 * l2 // max(1, wq.numel())) + 1)
+    ws = [wq] + [wq.clone() for _ in range(copies - 1)]
+    res = {}
+    for M in CFG4_ROWS:
+        xd = torch.from_numpy(np.ascontiguousarray(X[:M])).to(dev)
+        yd = torch.empty((M, n), device=dev)
+        sg = None
+        if world > 1:
+            sg = shard.ShardedGemv("q4_0", wq, N, K, gather="nvlink" if M == 1 else "nccl")
+            if M == 1:
+                def step(i, sg=sg, xd=xd):
+                    _core._gemv_q_gather(sg._g, 0, 1, n, K, xd.data_ptr(), K, ws[i % copies].data_ptr(),
+                                         stream.cuda_stream, local_rank)
+            else:
+                recv = torch.empty((world, M, sg.pad), device=dev)
+                send = torch.zeros((M, sg.pad), device=dev)
+                import torch.distributed as dist
+
+                def step(i, xd=xd, send=send, recv=recv):
+                    sk.gemv_q4_0_batch(xd, ws[i % copies], n, K, out=send[:, :n])
+                    dist.all_gather_into_tensor(recv, send)
+        elif M == 1:
+            def step(i, xd=xd, yd=yd):
+                sk.gemv_q4_0(xd[0], ws[i % copies], n, K, out=yd[0])
+        else:
+            def step(i, xd=xd, yd=yd):
+                sk.gemv_q4_0_batch(xd, ws[i % copies], n, K, out=yd)
+        reps = 64 if N < 100000 else 32
+        ms = chained_ms(torch, dev, stream, step, reps, copies, chunk=max(reps, copies),
+                        barrier=barrier if world > 1 else None)
+        t = torch.tensor([ms * 1e3 / reps], device=dev)
+        if world > 1:
+            dist_all_max(t)
+        us = float(t.item())
+        if sg is not None:
+            sg.close()
+        nbytes = gemv_bytes(q_bytes("q4_0", N, K), M, N, K)
+        key = f"q4_0 M={M} N={N} K={K}" + (f" over {world} GPUs" if world > 1 else "")
+        res[key] = {"us": round(us, 3), "gb_s_aggregate": round(nbytes / (us * 1e-6) / 1e9, 1),
+                    "rows_per_gpu": n, "bytes": nbytes, "roofline": roofline(nbytes, us, peak),
+                    "roofline_per_gpu": roofline(nbytes // world, us, peak),
+                    "gather": None if world == 1 else ("fused NVLink stores" if M == 1 else "NCCL all-gather")}
+        del xd, yd
+    del ws
+    return res
+
+
+def dist_all_max(t):
+    import torch.distributed as dist
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+
+
+def llama_stack(torch, sk, dev, stream, args, jobs, peak, host) -> dict:
+    """a Llama-3.2-1B decode step's GEMVs, 16 layers of
     q 2048->2048, k, v 2048->512, o 2048->2048, gate, up 2048->8192, down
-    8192->2048, and the tied 2048->128256 LM head — on random-init Q4_0 weights
-    (seed 2), fresh activations every step, --llama-tokens (128) steps in one
-    CUDA graph.
-    q, k and v read the same activation row within a step, as do gate and up,
-    so each group runs as one GEMV over its concatenated rows (the same bytes
-    and outputs as the separate GEMVs): 4 GEMVs per layer + the LM head.
-    swiglu "fused": the down projection reads silu(gate) * up of the layer's
-    gate/up GEMV instead of fresh activations, as the decoder does, with the
-    SwiGLU product formed inside it (more work than the GEMV-only stack);
-    "unfused": the same step with silu_mul as its own kernel before a plain
-    down-projection GEMV."""
-    g = torch.Generator(device=dev)
-    g.manual_seed(2)
-    groups = []   # (rows N, K, logical GEMVs)
-    for _ in range(LLAMA_LAYERS):
-        groups += [(2048 + 512 + 512, 2048, 3), (2048, 2048, 1), (8192 + 8192, 2048, 2), (2048, 8192, 1)]
+    8192->2048, and the tied 2048->128256 LM head, on random-init Q4_0 weights
+    (seed 2), fresh activations every token, LLAMA_TOKENS tokens in one CUDA
+    graph. q, k and v read the same activation row within a token, as do gate
+    and up, so each group runs as one GEMV over its concatenated rows (the same
+    bytes and outputs as the separate GEMVs): 4 GEMVs per layer + the LM head.
+    Also the decode step with SwiGLU: the down projection reads silu(gate) * up
+    of the layer's gate/up GEMV, formed inside its activation quantization."""
+    mats = []
+    for i in range(len(LLAMA_MATRICES)):
+        w, _ = device_weights(torch, sk, dev, jobs[("c2", i)], "q4_0")
+        mats.append(w)
+    groups, weights = [], []   # (rows N, K, logical GEMVs), concatenated rows
+    for layer in range(LLAMA_LAYERS):
+        m = mats[7 * layer:7 * layer + 7]
+        groups += [(3072, 2048, 3), (2048, 2048, 1), (16384, 2048, 2), (2048, 8192, 1)]
+        weights += [torch.cat(m[0:3]).reshape(-1), m[3].reshape(-1), torch.cat(m[4:6]).reshape(-1),
+                    m[6].reshape(-1)]
     groups.append((LLAMA_VOCAB, 2048, 1))
-    weights = []
-    wbytes = 0
-    for n, k, _ in groups:
-        wq = torch.empty((n, k // 32 * 18), dtype=torch.uint8, device=dev)
-        for r0 in range(0, n, 16384):
-            r1 = min(n, r0 + 16384)
-            sk.quantize_q4_0(torch.randn((r1 - r0, k), generator=g, device=dev) * 0.02, out=wq[r0:r1])
-        weights.append(wq.reshape(-1))
-        wbytes += wq.numel()
+    weights.append(mats[-1].reshape(-1))
+    host["c2"] = [w.cpu().numpy() for w in weights]
+    del mats
+    wbytes = sum(w.numel() for w in weights)
     xs_per_tok = sum(k for _, k, _ in groups)
     ys_per_tok = sum(n for n, _, _ in groups)
     tokens = args.llama_tokens
+    g = torch.Generator(device=dev)
+    g.manual_seed(2)
     X = torch.randn((tokens, xs_per_tok), generator=g, device=dev)
     Y = torch.empty((ys_per_tok,), device=dev)
     act = torch.empty((8192,), device=dev)
-    gr = torch.cuda.CUDAGraph()
-    with torch.cuda.stream(stream):
-        with torch.cuda.graph(gr, stream=stream):
-            for t in range(tokens):
-                xo = yo = 0
-                gate_up = None
-                for (n, k, _), wq in zip(groups, weights):
-                    if swiglu and gate_up is not None and n == 2048 and k == 8192:
-                        # The down projection takes silu(gate) * up of the gate/up GEMV just
-                        # before it, formed while its activations are quantized.
-                        if swiglu == "fused":
-                            sk.gemv_q4_0_silu_mul(gate_up[:8192], gate_up[8192:], wq, n, k, out=Y[yo:yo + n])
-                        else:
-                            sk.silu_mul(gate_up[:8192], gate_up[8192:], out=act)
-                            sk.gemv_q4_0(act, wq, n, k, out=Y[yo:yo + n])
-                        gate_up = None
-                    else:
-                        sk.gemv_q4_0(X[t, xo:xo + k], wq, n, k, out=Y[yo:yo + n])
-                        if n == 16384:
-                            gate_up = Y[yo:yo + n]
-                    xo += k
-                    yo += n
-        for _ in range(3):
-            gr.replay()
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record(stream)
-        gr.replay()
-        e.record(stream)
-    torch.cuda.synchronize(dev)
-    ms = s.elapsed_time(e)
-    per_tok_ms = ms / tokens
-    # Algorithmic bytes of the 113 separate GEMVs: weights, x of each, y of each.
     logical_x = sum(k * c for _, k, c in groups)
     tok_bytes = wbytes + 4 * (logical_x + ys_per_tok)
-    del gr
-    return {"tok_s": round(1e3 / per_tok_ms, 1), "ms_per_token": per_tok_ms,
-            "gemvs_per_token": sum(c for _, _, c in groups),
-            "launches_per_token": len(groups) + (LLAMA_LAYERS if swiglu == "unfused" else 0),
-            "bytes_per_token": tok_bytes, "gb_s": round(tok_bytes / (per_tok_ms * 1e-3) / 1e9, 1),
-            "tokens": tokens,
-            "launch": f"one CUDA graph of {tokens} decode steps, PDL; q/k/v and gate/up as fused row groups"
-                      + {"": "", "fused": "; down projection fed by silu(gate)*up inside its activation quantization",
-                         "unfused": "; silu(gate)*up as a separate kernel before the down projection"}[swiglu]}
-
-
-SHARDED_SHAPES = [(28672, 8192), (8192, 28672), (128256, 8192)]   # config 4: 70B layers, LM head
-
-
-def sharded_configs(sk, torch, dev, stream, world: int, rank: int, local_rank: int) -> dict:
-    """Config 4 (Q4_0, M = 1, W ~ N(0, 0.015) from seed 4) split by rows over
-    the ranks: each step is this rank's GEMV plus the all-gather of y fused
-    into it (world > 1), timed in CUDA graphs as the max over ranks; aggregate
-    GB/s = the whole matrix's algorithmic bytes per step time (strong scaling).
-    Every rank calls this with the same shapes (collectives inside)."""
-    import torch.distributed as dist
-    from simd_ml_kernels import _core, shard
     res = {}
-    l2 = getattr(torch.cuda.get_device_properties(dev), "L2_cache_size", 126 << 20)
-    for N, K in SHARDED_SHAPES:
-        lo, hi = shard.row_slice(N, rank, world)
-        n, rb = hi - lo, K // 32 * 18
-        g = torch.Generator(device=dev)
-        g.manual_seed(4 * 1000 + rank)
-        wq = torch.empty(n * rb, dtype=torch.uint8, device=dev)
-        for r0 in range(0, n, 8192):
-            rows = min(8192, n - r0)
-            wq[r0 * rb:(r0 + rows) * rb] = sk.quantize_q4_0(
-                torch.randn((rows, K), generator=g, device=dev) * 0.015).reshape(-1)
-        copies = max(2, -(-2 * l2 // (n * rb)) + 1)
-        ws = [wq] + [wq.clone() for _ in range(copies - 1)]
-        x = torch.randn(K, generator=g, device=dev)
-        y = torch.empty(n, device=dev)
-        sg = shard.ShardedGemv("q4_0", wq, N, K, gather="nvlink") if world > 1 else None
-
-        def step(i):
-            if sg is not None:
-                _core._gemv_q_gather(sg._g, 0, 1, n, K, x.data_ptr(), K, ws[i % copies].data_ptr(),
-                                     stream.cuda_stream, local_rank)
-            else:
-                sk.gemv_q4_0(x, ws[i % copies], n, K, out=y)
-
-        reps = copies * max(1, 64 // copies)
+    for swiglu in ("", "fused", "unfused"):
         gr = torch.cuda.CUDAGraph()
         with torch.cuda.stream(stream):
-            step(0)
-            torch.cuda.synchronize(dev)
             with torch.cuda.graph(gr, stream=stream):
-                for i in range(reps):
-                    step(i)
-            gr.replay()
-            torch.cuda.synchronize(dev)
-            if world > 1:
-                dist.barrier()
-            s0, e0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            s0.record(stream)
-            for _ in range(5):
+                for t in range(tokens):
+                    xo = yo = 0
+                    gate_up = None
+                    for (n, k, _), wq in zip(groups, weights):
+                        if swiglu and gate_up is not None and n == 2048 and k == 8192:
+                            if swiglu == "fused":
+                                sk.gemv_q4_0_silu_mul(gate_up[:8192], gate_up[8192:], wq, n, k, out=Y[yo:yo + n])
+                            else:
+                                sk.silu_mul(gate_up[:8192], gate_up[8192:], out=act)
+                                sk.gemv_q4_0(act, wq, n, k, out=Y[yo:yo + n])
+                            gate_up = None
+                        else:
+                            sk.gemv_q4_0(X[t, xo:xo + k], wq, n, k, out=Y[yo:yo + n])
+                            if n == 16384:
+                                gate_up = Y[yo:yo + n]
+                        xo += k
+                        yo += n
+            for _ in range(3):
                 gr.replay()
-            e0.record(stream)
-        torch.cuda.synchronize(dev)
-        t = torch.tensor([s0.elapsed_time(e0) * 1e3 / (5 * reps)], device=dev)
-        if world > 1:
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        us = float(t.item())
-        del gr
-        if sg is not None:
-            sg.close()
-        nbytes = N * K // 32 * 18 + 4 * K + 4 * N
-        res[f"q4_0 M=1 N={N} K={K} over {world} GPU(s)"] = {
-            "us_per_step": round(us, 3), "gb_s_aggregate": round(nbytes / (us * 1e-6) / 1e9, 1),
-            "rows_per_gpu": n, "gather": "fused NVLink" if world > 1 else None}
-        del ws, wq
-    return res
-
-
-def other_configs(sk, torch, dev, stream, only: str | None = None) -> dict:
-    """Configs 1 (Q8_0), 3 (dense fp32/bf16/fp16, M in 1,4,8) and 4 (large Q4_0, M 1/8) on one GPU;
-    `only`: time just the cases whose label contains it (for profilers)."""
-    res = {}
-    l2 = getattr(torch.cuda.get_device_properties(dev), "L2_cache_size", 126 << 20)
-
-    def timeit(fn, nbytes, reps=200):
-        copies_needed = max(2, -(-2 * l2 // max(1, nbytes)) + 1)
-        return copies_needed, fn, reps
-
-    def run(label, make_w, call, nbytes):
-        if only is not None and only not in label:
-            return
-        copies = max(2, -(-2 * l2 // nbytes) + 1)
-        ws = [make_w()] + []
-        for _ in range(copies - 1):
-            ws.append(ws[0].clone())
-        gr = torch.cuda.CUDAGraph()
-        reps = copies * max(1, 64 // copies)
-        with torch.cuda.stream(stream):
-            call(ws[0])
-            torch.cuda.synchronize(dev)
-            with torch.cuda.graph(gr, stream=stream):
-                for i in range(reps):
-                    call(ws[i % copies])
-            gr.replay()
             s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             s.record(stream)
-            for _ in range(5):
-                gr.replay()
+            gr.replay()
             e.record(stream)
         torch.cuda.synchronize(dev)
-        us = s.elapsed_time(e) * 1e3 / (5 * reps)
-        res[label] = {"us": round(us, 3), "gb_s": round(nbytes / (us * 1e-6) / 1e9, 1)}
-        del gr, ws
-
-    g = torch.Generator(device=dev)
-    g.manual_seed(1)
-    for n, k in ((512, 2048), (2048, 2048), (8192, 2048), (2048, 8192)):
-        x = torch.randn(k, generator=g, device=dev)
-        y = torch.empty(n, device=dev)
-        nb = n * k // 32 * 34
-        run(f"q8_0 N={n} K={k}", lambda: sk.quantize_q8_0(torch.randn((n, k), generator=g, device=dev) * 0.02).reshape(-1),
-            lambda w: sk.gemv_q8_0(x, w, n, k, out=y), nb + 4 * k + 4 * n)
-    g.manual_seed(3)
-    for wt in (torch.float32, torch.bfloat16, torch.float16):
-        for m in (1, 4, 8):
-            for n in (4096, 14336):
-                k = 4096
-                x = torch.randn((m, k), generator=g, device=dev)
-                y = torch.empty((m, n), device=dev)
-                es = 4 if wt == torch.float32 else 2
-                run(f"dense {str(wt).split('.')[-1]} M={m} N={n} K={k}",
-                    lambda: (torch.randn((n, k), generator=g, device=dev) * 0.02).to(wt),
-                    lambda w: sk.gemv_dense(x, w, out=y), n * k * es + 4 * m * k + 4 * m * n)
-    g.manual_seed(5)
-    for m in (1, 4, 8):   # INT8 sgemm_u8s8 with trans_b: uint8 A, int8 W [N, K], per-row scales
-        for n in (4096, 14336):
-            k = 4096
-            a = torch.randint(0, 256, (m, k), generator=g, device=dev, dtype=torch.uint8)
-            sc = torch.rand(n, generator=g, device=dev) * 0.01
-            y = torch.empty((m, n), device=dev)
-            run(f"u8s8 M={m} N={n} K={k}",
-                lambda n=n, k=k: torch.randint(-128, 128, (n, k), generator=g, device=dev, dtype=torch.int8),
-                lambda w, a=a, sc=sc, y=y: sk.sgemm_u8s8(a, w, 0.02, 128, sc, y, trans_b=True),
-                n * k + m * k + 4 * n + 4 * m * n)
-    g.manual_seed(4)
-    for n, k in ((28672, 8192), (8192, 28672), (128256, 8192)):
-        for m in (1, 8):
-            x = torch.randn((m, k), generator=g, device=dev)
-            y = torch.empty((m, n), device=dev)
-            nb = n * k // 32 * 18
-
-            def mk(n=n, k=k):
-                wq = torch.empty((n, k // 32 * 18), dtype=torch.uint8, device=dev)
-                for r0 in range(0, n, 8192):
-                    r1 = min(n, r0 + 8192)
-                    sk.quantize_q4_0(torch.randn((r1 - r0, k), generator=g, device=dev) * 0.015, out=wq[r0:r1])
-                return wq.reshape(-1)
-            run(f"q4_0 M={m} N={n} K={k}", mk, lambda w, x=x, y=y, n=n, k=k: sk.gemv_q4_0_batch(x, w, n, k, out=y),
-                nb + 4 * m * (k + n))
+        per_tok_ms = s.elapsed_time(e) / tokens
+        del gr
+        name = {"": "gemv_stack", "fused": "decode_swiglu_fused", "unfused": "decode_swiglu_unfused"}[swiglu]
+        res[name] = {"tok_s": round(1e3 / per_tok_ms, 1), "ms_per_token": per_tok_ms,
+                     "gb_s": round(tok_bytes / (per_tok_ms * 1e-3) / 1e9, 1),
+                     "roofline": roofline(tok_bytes, per_tok_ms * 1e3, peak),
+                     "launches_per_token": len(groups) + (LLAMA_LAYERS if swiglu == "unfused" else 0)}
+    res.update({"gemvs_per_token": len(LLAMA_MATRICES), "bytes_per_token": tok_bytes, "tokens": tokens,
+                "weights": "per matrix i numpy default_rng((2, i)), N(0, 0.02) -> Q4_0 on device",
+                "launch": f"one CUDA graph of {tokens} decode steps, PDL; q/k/v and gate/up as fused row groups"})
     return res
+
+
+def e2e_headline(torch, sk, shard, dev, local_rank, world, ws, copies, sg, x_np) -> dict:
+    """The headline metric through the public API with host buffers: every call
+    copies x (page-locked host memory) to the device and returns y in host memory.
+    At least 2,000 timed calls after 200 warm-up calls; per-call times."""
+    import torch.distributed as dist
+    xh = torch.from_numpy(np.ascontiguousarray(x_np)).pin_memory()
+    xh_np = xh.numpy()
+    sk.set_pdl(False, local_rank)
+    calls = 2000
+    ts = []
+    if world == 1:
+        for i in range(200):
+            sk.gemv_q4_0(xh_np, ws[i % copies], N_ROWS, K_COLS)
+        for i in range(calls):
+            t0 = time.perf_counter()
+            yh = sk.gemv_q4_0(xh_np, ws[i % copies], N_ROWS, K_COLS)
+            ts.append(time.perf_counter() - t0)
+        assert yh.shape == (N_ROWS,)
+        d2h = 4 * N_ROWS
+        api = "simd_ml_kernels.gemv_q4_0(numpy x in page-locked memory, device-resident weights) -> numpy y"
+    else:
+        if sg is None:
+            sg = shard.ShardedGemv("q4_0", ws[0], N_ROWS * world, K_COLS)
+        yfull_h = torch.empty(N_ROWS * world).pin_memory()
+        for _ in range(200):
+            yfull_h.copy_(sg.forward(xh.to(dev, non_blocking=True)))
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        for _ in range(calls):
+            t0 = time.perf_counter()
+            yfull_h.copy_(sg.forward(xh.to(dev, non_blocking=True)))   # the copy to host synchronises
+            ts.append(time.perf_counter() - t0)
+        t = torch.tensor([statistics.median(ts)], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        d2h = 4 * N_ROWS * world
+        api = "ShardedGemv.forward(x host->device, fused NVLink gather) + y device->host"
+    sk.set_pdl(True, local_rank)
+    q = quantiles(ts)
+    nb = STEP_BYTES * world
+    return {"value": round(nb / q["median"] / 1e9, 2), "unit": "GB/s", "h2d_bytes_per_step": 4 * K_COLS,
+            "d2h_bytes_per_step": d2h, "us_median": round(q["median"] * 1e6, 3),
+            "us_p25": round(q["p25"] * 1e6, 3), "us_p75": round(q["p75"] * 1e6, 3),
+            "us_mean": round(q["mean"] * 1e6, 3), "steps": calls, "api": api}
+
+
+def cpu_arms(host: dict, extra: dict) -> dict:
+    """The reference's CPU kernels on the same bytes as the GPU cases, all host
+    threads and one pinned thread (after every GPU case and every generator
+    thread has finished)."""
+    ref = RefCPU()
+    if not ref.ok:
+        return {"unavailable": "oracle/_ref/libsmk_ref.so was not built"}
+    out = {"threads": ref.threads, "cpu": cpu_model(), "path": ref.path, "llc_bytes": ref.llc}
+    # Config 0.
+    Wq, x = host["c0"]
+    ws = [Wq] + [Wq.copy() for _ in range(ref.copies(W_BYTES) - 1)]
+    out["config0"] = ref.both(ref.gemv_q("q4_0", ws, x[0], N_ROWS, K_COLS), STEP_BYTES, seconds=2.0)
+    out["config0"]["path"] = ref.path
+    # Config 1.
+    out["config1_q8_0"] = {}
+    for N, K in CFG1_SHAPES:
+        wq, X = host[("c1", N, K)]
+        nb = gemv_bytes(wq.nbytes, 1, N, K)
+        ws = [wq] + [wq.copy() for _ in range(ref.copies(wq.nbytes) - 1)]
+        out["config1_q8_0"][f"q8_0 M=1 N={N} K={K}"] = ref.both(ref.gemv_q("q8_0", ws, X[0], N, K), nb)
+    # Config 3.
+    out["config3_dense"] = {}
+    for N, K in CFG3_SHAPES:
+        X = host[("c3x", N, K)]
+        for kind, es in (("float32", 4), ("bfloat16", 2), ("float16", 2)):
+            w = host[("c3", kind, N, K)]
+            ws = [w] + [w.copy() for _ in range(ref.copies(w.nbytes) - 1)]
+            for M in CFG3_ROWS:
+                nb = N * K * es + es * M * K + 4 * M * N
+                out["config3_dense"][f"dense {kind} M={M} N={N} K={K}"] = ref.both(
+                    ref.dense(kind, ws, X[:M], N, K), nb, seconds=0.25)
+    # Config 4 (the bytes of this GPU, rank 0 = the whole matrix at N = 1).
+    out["config4"] = {}
+    for N, K in CFG4_SHAPES:
+        wq, X = host[("c4", N, K)]
+        ws = [wq] + [wq.copy() for _ in range(ref.copies(wq.nbytes) - 1)]
+        one = None
+        for M in CFG4_ROWS:
+            nb = gemv_bytes(wq.nbytes, M, N, K)
+            calls = ref.gemv_q("q4_0", ws, X[:M], N, K)
+            if M == 1:
+                one = ref.both(calls, nb, seconds=0.5)
+                out["config4"][f"q4_0 M=1 N={N} K={K}"] = one
+                continue
+            # M rows are M separate calls in the reference (no batched quantized GEMV);
+            # on one thread their time is M times the one-row call's, not re-timed.
+            a = ref.time(calls, nb, 0.5)
+            o = dict(one["one_thread"])
+            o.update(us_median=round(M * o["us_median"], 3), us_p25=round(M * o["us_p25"], 3),
+                     us_p75=round(M * o["us_p75"], 3), gb_s=round(nb / (M * o["us_median"] * 1e-6) / 1e9, 3),
+                     derived=f"{M} x the one-row call on one pinned thread")
+            out["config4"][f"q4_0 M={M} N={N} K={K}"] = {"all_threads": a, "one_thread": o}
+        del ws, wq
+    # Config 2: the 113 GEMVs of a token (the fused row groups called as the reference's separate GEMVs).
+    ws = host["c2"]
+    rng = np.random.default_rng(2)
+    calls = []
+    rb = lambda k: k // 32 * 18  # noqa: E731
+    for layer in range(LLAMA_LAYERS):
+        qkv, o, gu, down = ws[4 * layer:4 * layer + 4]
+        for w, n, k, r0 in ((qkv, 2048, 2048, 0), (qkv, 512, 2048, 2048), (qkv, 512, 2048, 2560), (o, 2048, 2048, 0),
+                            (gu, 8192, 2048, 0), (gu, 8192, 2048, 8192), (down, 2048, 8192, 0)):
+            calls.append((w[r0 * rb(k):(r0 + n) * rb(k)], n, k))
+    calls.append((ws[-1], LLAMA_VOCAB, 2048))
+    xs = [rng.standard_normal(k).astype(np.float32) for _, _, k in calls]
+    ys = [np.empty(n, np.float32) for _, n, _ in calls]
+    R = ref.R
+
+    def token():
+        for (w, n, k), xv, yv in zip(calls, xs, ys):
+            R.smkref_gemv_q4_0(-1, n, k, xv.ctypes.data, w.ctypes.data, yv.ctypes.data)
+    tok_bytes = extra["config2_llama_stack"]["bytes_per_token"]
+    c2 = ref.both([token], tok_bytes, seconds=1.0)
+    for v in c2.values():
+        v["tok_s"] = round(1e6 / v["us_median"], 2)
+        v["ms_per_token"] = v["us_median"] / 1e3
+    out["config2_llama_stack"] = c2
+    return out
 
 
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=100000)
-    ap.add_argument("--warmup", type=int, default=2000)
+    ap.add_argument("--steps", type=int, default=20000)
+    ap.add_argument("--warmup", type=int, default=100)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--all", action="store_true", help="also time configs 1, 3 and 4 (one GPU)")
-    ap.add_argument("--cpu-baseline-seconds", type=float, default=8.0)
     ap.add_argument("--gather", choices=["nvlink", "nccl"], default="nvlink",
                     help="N > 1: all-gather of y fused into the GEMV over NVLink, or NCCL's all-gather")
-    ap.add_argument("--case", default=None,
-                    help="time only the config 1/3/4 cases whose label contains this text (after the config-0 line)")
     ap.add_argument("--llama-tokens", type=int, default=LLAMA_TOKENS,
                     help="decode steps per Llama-stack CUDA graph (fewer: shorter profiler launch lists)")
     ap.add_argument("--only-gemv", action="store_true",
-                    help="time the config-0 GEMV only (no e2e, Llama stack or CPU baseline): for profilers")
+                    help="time the headline GEMV only (no other configs, e2e or CPU arms): for profilers")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -653,17 +1038,16 @@ def main() -> None:
     if args.impl == "reference":
         if rank != 0:
             return
-        r = time_reference(args.steps, args.warmup, 0.0)
+        r = time_reference_arm(args.steps, args.warmup, world)
         if r is None:
             print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libsmk_ref.so was not built"}))
             return
         print(json.dumps({"impl": "reference", "metric": METRIC, "value": round(r["value"], 3), "unit": "GB/s",
                           "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-                          "ms_per_step": r["seconds"] / r["calls"] * 1e3, "higher_is_better": True,
-                          "scaling": "weak", "vs_baseline": None, "dtype": "q4_0 x int8 (vpdpbusd), fp32 accumulate",
-                          "data": "synthetic: W ~ N(0, 0.02) seed 0 quantized ggml Q4_0, x ~ N(0, 1)",
-                          "config": {"workload": "config 0: Q4_0 decode GEMV M=1 K=2048 N=8192", "M": 1,
-                                     "K": K_COLS, "N": N_ROWS},
+                          "ms_per_step": r["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+                          "vs_baseline": None, "dtype": "q4_0 weights x int8 activations (vpdpbusd), fp32 accumulate",
+                          "data": "synthetic: numpy default_rng(0), W ~ N(0, 0.02) quantized ggml Q4_0, x ~ N(0, 1)",
+                          "config": headline_config(world),
                           "cpu_baseline": {"value": round(r["value"], 3), "unit": "GB/s", "cores": r["cores"],
                                            "kind": "reference", "sample": r["sample"]},
                           "e2e": {"value": round(r["value"], 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
@@ -680,11 +1064,6 @@ def main() -> None:
     try:
         out = gpu_bench(args, rank, world, local_rank)
         if rank == 0 and out is not None:
-            if world == 1 and not args.only_gemv:
-                cb = time_reference(None, 2, args.cpu_baseline_seconds)
-                out["cpu_baseline"] = None if cb is None else {
-                    "value": round(cb["value"], 3), "unit": "GB/s", "cores": cb["cores"], "kind": "reference",
-                    "sample": cb["sample"] + f", {cb['seconds']:.1f} s"}
             print(json.dumps(out))
     finally:
         if world > 1:

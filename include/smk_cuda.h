@@ -210,7 +210,10 @@ smk_status smk_gemv_q_noalloc(smk_qformat fmt, int M, int N, int K, const float*
  * area over NVLink, and, on the same stream, waits (bounded, about 1 s;
  * smk_device_error reports a timeout) until every peer's slice of the step
  * has arrived. *y_full receives this step's area: [M][world * npad] floats,
- * rank r's rows at r * npad; it stays valid until the call after next. */
+ * rank r's rows at r * npad. It stays valid until this rank's next
+ * smk_gemv_q_gather call: queue every kernel that reads it on `stream` (or
+ * copy it) before making that call. The two areas alternate, and a peer
+ * writes this one again as soon as this rank's next call has signalled it. */
 typedef struct smk_gather smk_gather;
 #define SMK_IPC_HANDLE_BYTES 64
 smk_status smk_gather_create(smk_ctx* ctx, int world, int rank, int npad, int m_max, smk_gather** out,

@@ -279,7 +279,8 @@ smk_status run_q(smk_ctx* c, smk_qformat fmt, int M, int N, int K, const float* 
                 p.stages = st;
             }
         // Otherwise K in P parts across CTAs, each CTA holding its part's slice
-        // of x, when a slice fits (B200, 8 rows, 8192x28672: see the design notes).
+        // of x, when a slice fits (B200, 8 rows, 8192x28672: 39.2 us with P = 2 against
+        // 73.7 us reading x through L1).
         for (int P = 2; !xs && P <= 16 && P <= p.nb / 8; P *= 2) {
             const int xnb = (p.nb / 8 + P - 1) / P * 8;
             for (int st = c->stages > 0 ? c->stages : 4; st >= 2 && !xs; --st)

@@ -61,8 +61,9 @@ class ShardedGemv:
     forward(x) runs the local GEMV (on the current CUDA stream for CUDA
     tensors) and gathers the slices: y [N] (or [M, N] for x [M, K]) on every
     rank. gather="nvlink" (CUDA tensors, world > 1) fuses the gather into the
-    GEMV kernel; its result is a view that stays valid until the call after
-    next. gather="nccl" uses NCCL's all-gather. `local_fn(x, Wq_local, n, K,
+    GEMV kernel; its result is a view into the gather buffer that stays valid
+    until this rank's next forward call: queue its readers on the stream (or
+    clone it) before that call. gather="nccl" uses NCCL's all-gather. `local_fn(x, Wq_local, n, K,
     out)` replaces the GPU GEMV (tests run the CPU oracle there on gloo ranks).
     Every rank must make the same sequence of forward calls.
     """

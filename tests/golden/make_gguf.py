@@ -34,7 +34,14 @@ REPO = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, os.path.join(REPO, "oracle"))
 import oracle as O  # noqa: E402
 
-REF_TREE = os.environ.get("SMK_REFERENCE_TREE", "/root/reference")
+
+
+def ref_tree() -> str:
+    """The reference's source tree, from SMK_REFERENCE_TREE (no default)."""
+    t = os.environ.get("SMK_REFERENCE_TREE")
+    if not t or not os.path.isdir(t):
+        raise SystemExit("set SMK_REFERENCE_TREE to the reference's source tree (Mattral/simd-ml-kernels 0.3.0)")
+    return t
 
 F32, F16, Q4_0, Q8_0, BF16 = 0, 1, 2, 8, 30
 FILES = {"tiny_v3.gguf": (3, None), "tiny_v2_align64.gguf": (2, 64)}
@@ -126,7 +133,7 @@ def _json_value(v):
 
 
 def main() -> None:
-    sys.path.insert(0, os.path.join(REF_TREE, "examples", "llama"))
+    sys.path.insert(0, os.path.join(ref_tree(), "examples", "llama"))
     from gguf_reader import GGUF, dequantize_rows   # the reference's reader
 
     out = {}

@@ -28,7 +28,14 @@ REPO = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, os.path.join(REPO, "oracle"))
 import oracle as O  # noqa: E402
 
-REF_TREE = os.environ.get("SMK_REFERENCE_TREE", "/root/reference")
+
+
+def ref_tree() -> str:
+    """The reference's source tree, from SMK_REFERENCE_TREE (no default)."""
+    t = os.environ.get("SMK_REFERENCE_TREE")
+    if not t or not os.path.isdir(t):
+        raise SystemExit("set SMK_REFERENCE_TREE to the reference's source tree (Mattral/simd-ml-kernels 0.3.0)")
+    return t
 ISA_SCALAR = 0
 
 
@@ -173,7 +180,7 @@ def main() -> None:
     print(meta)
 
     # 1. The llama.cpp fixture of the reference's tests (ggml_quantize_chunk output).
-    fx = np.load(os.path.join(REF_TREE, "tests", "data", "q4_0_ggml_v0.7.0.npz"))
+    fx = np.load(os.path.join(ref_tree(), "tests", "data", "q4_0_ggml_v0.7.0.npz"))
     np.savez_compressed(os.path.join(HERE, "q4_0_llama_cpp_fixture.npz"), w=fx["w"], blocks=fx["blocks"],
                         source=fx["source"])
 

@@ -2,8 +2,10 @@
 2 GPUs, one spawned process each, NCCL only for the set-up handshake. Every
 step's gathered y equals the unsharded GEMV on one GPU (bitwise for one and
 two rows of x, which take the same kernel; within the reference's bound of the
-float64 sums for four rows), a step's result stays intact through the next
-step, and no device error is raised. Needs two GPUs; skipped otherwise."""
+float64 sums for four rows), a reader queued on the stream before the next
+step sees the step's result intact (the contract: y_full is valid until this
+rank's next call), and no device error is raised. Needs two GPUs; skipped
+otherwise."""
 
 from __future__ import annotations
 
@@ -57,15 +59,18 @@ def _rank(rank, world, port, out_dir):
             M = (1, 2, 4)[step % 3]
             X = torch.randn((M, K), generator=torch.Generator(device="cuda").manual_seed(100 + step), device="cuda")
             Y = sg.forward(X if M > 1 else X[0]).reshape(M, N)
+            copy = Y.clone()   # a reader queued on the stream before the next call
             want = sk.gemv_q4_0_batch(X, Wq, N, K)
+            if prev is not None:   # the previous step's reader saw its result whole
+                torch.cuda.synchronize()
+                assert torch.equal(prev[0].view(torch.int32), prev[1].view(torch.int32)), \
+                    f"step {step}: the previous step's copy differs from its own check"
             torch.cuda.synchronize()
             if M <= 2:
-                assert torch.equal(Y.view(torch.int32), want.view(torch.int32)), f"step {step}: not bitwise"
+                assert torch.equal(copy.view(torch.int32), want.view(torch.int32)), f"step {step}: not bitwise"
             else:
-                assert (Y - want).abs().max().item() <= 1e-5 * want.abs().max().item(), f"step {step}"
-            if prev is not None:   # the previous step's result is still intact
-                assert torch.equal(prev[0], prev[1]), f"step {step}: previous result overwritten"
-            prev = (Y.clone(), Y) if M > 0 else None
+                assert (copy - want).abs().max().item() <= 1e-5 * want.abs().max().item(), f"step {step}"
+            prev = (copy, copy.clone())
         torch.cuda.synchronize()
         assert _core._device_error(torch.cuda.current_stream().cuda_stream) == 0
         sg.close()
