@@ -181,7 +181,9 @@ smk_status smk_block_sums(smk_ctx* ctx, smk_qformat fmt, int M, int N, int K, co
  * memory at start-up and allocate nothing per request, plugins inside either.
  * Same result as smk_gemv_q (same kernels), with these differences:
  *   - no smk_ctx: runs on the calling thread's current device; Wq, x and y
- *     are device memory; errors through smk_last_error();
+ *     are device memory; argument and CUDA errors through smk_last_error(),
+ *     errors that kernels report (a bounded wait that ran out) through
+ *     smk_noalloc_device_error;
  *   - the quantized activations go to a fixed scratch array of
  *     SMK_NOALLOC_SCRATCH_BYTES inside the library, which every GPU that loads
  *     the library holds until the process exits; a call needing more
@@ -196,6 +198,11 @@ smk_status smk_block_sums(smk_ctx* ctx, smk_qformat fmt, int M, int N, int K, co
 #define SMK_NOALLOC_SCRATCH_BYTES (1u << 20)
 smk_status smk_gemv_q_noalloc(smk_qformat fmt, int M, int N, int K, const float* x, int64_t ldx, const uint8_t* Wq,
                               float* y, int64_t ldy, void* stream);
+/* The error word of the current device's smk_gemv_q_noalloc kernels (no
+ * reference counterpart): waits for `stream`, stores the word in *code and
+ * clears it. The word collects the bits of every call since the last read;
+ * 0: none of them reported an error. Allocates nothing. */
+smk_status smk_noalloc_device_error(unsigned* code, void* stream);
 
 /* ---- row-sharded GEMV with the all-gather of y fused in (one process per GPU) ----
  * Replaces the row slicing of gemv_slice (src/dispatch/dispatch.cpp:373-379)

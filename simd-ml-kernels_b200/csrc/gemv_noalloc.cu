@@ -35,6 +35,9 @@ namespace {
 constexpr size_t kNoAllocScratchBytes = SMK_NOALLOC_SCRATCH_BYTES;
 
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+// Error bits of the kernels launched by smk_gemv_q_noalloc on this device (a
+// bounded wait that ran out, ...). Zero when the library loads; the kernels
+// OR bits in; smk_noalloc_device_error reads and clears it.
 static __device__ unsigned g_noalloc_error;
 
 struct DeviceState {
@@ -118,10 +121,9 @@ extern "C" smk_status smk_gemv_q_noalloc(smk_qformat fmt, int M, int N, int K, c
         }
         return SMK_OK;
     }
-    // The error word must start at zero; the scratch needs no clearing: the
-    // quantize kernel writes every byte the GEMV kernel reads.
-    e = cudaMemsetAsync(s->error, 0, sizeof(unsigned), strm);
-    if (e != cudaSuccess) return noalloc_fail(SMK_ERR_CUDA, cudaGetErrorString(e));
+    // The scratch needs no clearing: the quantize kernel writes every byte the
+    // GEMV kernel reads. The error word is not cleared here: it keeps the bits
+    // of every call until smk_noalloc_device_error reads it.
 
     smk::LaunchCfg l;
     l.stream = strm;
@@ -136,5 +138,30 @@ extern "C" smk_status smk_gemv_q_noalloc(smk_qformat fmt, int M, int N, int K, c
     if (e != cudaSuccess) return noalloc_fail(SMK_ERR_CUDA, std::string("quantize_x launch: ") + cudaGetErrorString(e));
     e = smk::launch_gemv_q(l, (int)fmt, p, fast, nullptr);
     if (e != cudaSuccess) return noalloc_fail(SMK_ERR_CUDA, std::string("gemv launch: ") + cudaGetErrorString(e));
+    return SMK_OK;
+}
+
+// The device error word of this device's smk_gemv_q_noalloc calls: waits for
+// `stream` (and everything queued on it before), copies the word to *code and
+// clears it. 0 means that no kernel of those calls reported an error since the
+// last read. Allocates nothing: one device-to-host copy, one memset and a
+// stream synchronisation.
+extern "C" smk_status smk_noalloc_device_error(unsigned* code, void* stream) {
+    if (!code) return noalloc_fail(SMK_ERR_ARGUMENT, "code must not be NULL");
+    *code = 0;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return noalloc_fail(SMK_ERR_CUDA, std::string("cudaGetDevice: ") + cudaGetErrorString(e));
+    if (dev < 0 || dev >= kMaxDevices) return noalloc_fail(SMK_ERR_ARGUMENT, "device number out of range");
+    DeviceState* s = nullptr;
+    smk_status st = setup(dev, &s);
+    if (st != SMK_OK) return st;
+    cudaStream_t strm = static_cast<cudaStream_t>(stream);
+    unsigned word = 0;
+    e = cudaMemcpyAsync(&word, s->error, sizeof(unsigned), cudaMemcpyDeviceToHost, strm);
+    if (e == cudaSuccess) e = cudaMemsetAsync(s->error, 0, sizeof(unsigned), strm);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(strm);
+    if (e != cudaSuccess) return noalloc_fail(SMK_ERR_CUDA, std::string("reading the error word: ") + cudaGetErrorString(e));
+    *code = word;
     return SMK_OK;
 }
