@@ -93,8 +93,8 @@ extern "C" smk_status smk_gemv_q_noalloc(smk_qformat fmt, int M, int N, int K, c
     smk::QGemvParams p = {};
     p.x = x; p.ldx = ldx; p.w = Wq; p.y = y; p.ldy = ldy;
     p.M = M; p.N = N; p.K = K;
-    smk::plan_tiles(p, fast);
-    const size_t need = smk::xq_total_bytes(M, p.ksteps);
+    smk::plan_tiles(p, fast, (int)fmt);
+    const size_t need = smk::x_bytes(p);
     if (need > kNoAllocScratchBytes) {
         char buf[256];
         snprintf(buf, sizeof buf,

@@ -57,6 +57,7 @@ __device__ __forceinline__ float4 load_x4(const float* p) {
 
 struct XGeom {
     int M, nb, log2G, ksteps;
+    int r4;   // the four-row layout (one row of x)
 };
 
 // The decode step's SwiGLU input of the down projection, silu(g) * u, with
@@ -120,6 +121,14 @@ __device__ __forceinline__ Q8Quad quantize_quad(float4 v) {
 __device__ __forceinline__ void quantize_x_block(float4 v, int gq, bool valid, const XGeom& xg, int m, int b,
                                                  uint8_t* xb) {
     const Q8Quad q = quantize_quad(v);
+    if (xg.r4) {   // slot (ks·32 + 4g + j) of the four-row layout, b = 64·ks + 8g + 2j + odd
+        const unsigned ks = (unsigned)b >> 6, g = ((unsigned)b >> 3) & 7u, jb = (unsigned)b & 7u;
+        uint8_t* slot = xb + (ks * 32u + g * 4u + (jb >> 1)) * 80u;
+        if (!valid) return;
+        *reinterpret_cast<uint32_t*>(slot + (jb & 1u) * 32u + (unsigned)gq * 4u) = q.word;
+        if (gq == 0) *reinterpret_cast<float2*>(slot + 64u + (jb & 1u) * 8u) = make_float2(q.dx, __int_as_float(-8 * q.s));
+        return;
+    }
     // Offsets in 32 bits (the layout stays far below 4 GiB), no division.
     const unsigned sb = (unsigned)b >> 3, j = (unsigned)b & 7u;
     const unsigned ks = sb >> xg.log2G, g = sb & ((1u << xg.log2G) - 1u);
@@ -407,7 +416,7 @@ __device__ __forceinline__ void gemv_q_fast_body(const QGemvParams& p) {
 
     pdl_wait_primary();
     if constexpr (!kXGlobal) {
-        const XGeom xg{M, p.nb, p.log2G, p.ksteps};
+        const XGeom xg{M, p.nb, p.log2G, p.ksteps, 0};
         quantize_x_rows<M>(p.x, p.ldx, p.up, p.ldu, xg, xs, threadIdx.x, blockDim.x);
         __syncthreads();
     }
@@ -535,6 +544,215 @@ __global__ void __launch_bounds__(32) gather_wait_kernel(const GatherArgs* __res
         if (!ok && err) atomicOr(err, kErrPeerTimeout);
         *reinterpret_cast<volatile unsigned*>(ctrl) = epoch + 1u;
     }
+}
+
+// ---- Q4_0, one row of x, K a multiple of 2048: four weight rows per lane -----------------
+//
+// In the layout above, the TR lanes that share a superblock column (one per row of
+// the tile) each read the same 40 bytes of quantized x per block from shared
+// memory, and those reads (four times the bytes the dots need, ~80 shared-memory
+// wavefronts per 4-row item) set the pace of the block dots: measured on B200 in a
+// config-0 chain, ~1,250 cycles per item against ~530 for its weights. Here a warp
+// item is 4 rows × one k-step of 2048 values (the same 4,608-byte stage), and lane
+// l = 4g + j takes blocks 2j and 2j+1 of superblock g in all four rows: its 80
+// bytes of x (xq_r4_bytes layout) are loaded once and serve four rows from
+// registers, and its weights are 9 words per row at byte 1152·row + 144·g + 36·j
+// of the stage (32 distinct banks across the warp). Per block the arithmetic is the
+// fast kernel's: the exact int32 isum from the −8·Σq start, then
+// acc = fma(float(isum), fp16(dw)·dx, acc); each lane adds its two blocks of every
+// k-step in order, and a fixed shuffle tree adds the 32 lanes, so the result
+// depends on neither the launch shape nor where x was quantized.
+//
+// With K = 2048 and 16 warps (one quad of x per thread), the first item's weights
+// are read from shared memory while the loads of x are in flight: a GEMV chained
+// under programmatic dependent launch waits ~1,200 cycles for x behind the next
+// GEMV's weight stream, and the 36 words per lane fill that wait.
+
+// Two blocks of one row (lane words w[0..8]: block 2j's scale and quants from byte
+// 2, block 2j+1's scale in the high half of w[4] and quants in w[5..8]).
+__device__ __forceinline__ float r4_row(const uint32_t (&w)[9], const uint4& x0l, const uint4& x0h, const uint4& x1l,
+                                        const uint4& x1h, const uint4& dd, float acc) {
+    uint32_t q[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) q[i] = funnel(w[i], w[i + 1], 16);
+    int a = dp4a_us(q[0] & 0x0F0F0F0Fu, x0l.x, (int)dd.y), h = dp4a_us(q[0] & 0xF0F0F0F0u, x0h.x, 0);
+    a = dp4a_us(q[1] & 0x0F0F0F0Fu, x0l.y, a);
+    h = dp4a_us(q[1] & 0xF0F0F0F0u, x0h.y, h);
+    a = dp4a_us(q[2] & 0x0F0F0F0Fu, x0l.z, a);
+    h = dp4a_us(q[2] & 0xF0F0F0F0u, x0h.z, h);
+    a = dp4a_us(q[3] & 0x0F0F0F0Fu, x0l.w, a);
+    h = dp4a_us(q[3] & 0xF0F0F0F0u, x0h.w, h);
+    acc = fmaf((float)(a + (h >> 4)), __fmul_rn(half_bits_to_float(w[0]), __uint_as_float(dd.x)), acc);
+    a = dp4a_us(w[5] & 0x0F0F0F0Fu, x1l.x, (int)dd.w);
+    h = dp4a_us(w[5] & 0xF0F0F0F0u, x1h.x, 0);
+    a = dp4a_us(w[6] & 0x0F0F0F0Fu, x1l.y, a);
+    h = dp4a_us(w[6] & 0xF0F0F0F0u, x1h.y, h);
+    a = dp4a_us(w[7] & 0x0F0F0F0Fu, x1l.z, a);
+    h = dp4a_us(w[7] & 0xF0F0F0F0u, x1h.z, h);
+    a = dp4a_us(w[8] & 0x0F0F0F0Fu, x1l.w, a);
+    h = dp4a_us(w[8] & 0xF0F0F0F0u, x1h.w, h);
+    return fmaf((float)(a + (h >> 4)), __fmul_rn(half_bits_to_float(w[4] >> 16), __uint_as_float(dd.z)), acc);
+}
+
+// Rows of the first item read into registers while x is in flight (the rest of
+// the 64 registers a thread has hold the quantization and the ring's state).
+constexpr int kR4PreRows = 1;
+
+// One item: x slot at xslot (shared or global memory), the rows' words from the
+// stage, the first kPre rows from pre[] (the item loaded ahead).
+template <bool kShX, int kPre>
+__device__ __forceinline__ void r4_item(const uint8_t* stage, const uint8_t* xslot, int lane, float (&acc)[4],
+                                        const uint32_t (&pre)[kR4PreRows * 9]) {
+    const uint4 x0l = ld_x16<kShX>(xslot), x0h = ld_x16<kShX>(xslot + 16), x1l = ld_x16<kShX>(xslot + 32),
+                x1h = ld_x16<kShX>(xslot + 48), dd = ld_x16<kShX>(xslot + 64);
+    const uint32_t* wp = reinterpret_cast<const uint32_t*>(stage + (lane >> 2) * 144 + (lane & 3) * 36);
+#pragma unroll
+    for (int rr = 0; rr < 4; ++rr) {
+        uint32_t w[9];
+#pragma unroll
+        for (int i = 0; i < 9; ++i) w[i] = rr < kPre ? pre[(9 * rr + i) % (kR4PreRows * 9)] : wp[rr * 288 + i];
+        acc[rr] = r4_row(w, x0l, x0h, x1l, x1h, dd, acc[rr]);
+    }
+}
+
+// Sums of the four rows over the 32 lanes; lane l ends with row l >> 3.
+__device__ __forceinline__ float r4_reduce(const float (&a)[4], int lane) {
+    constexpr unsigned kAll = 0xffffffffu;
+    const bool up = lane & 16, up2 = lane & 8;
+    const float k0 = (up ? a[2] : a[0]) + __shfl_xor_sync(kAll, up ? a[0] : a[2], 16);
+    const float k1 = (up ? a[3] : a[1]) + __shfl_xor_sync(kAll, up ? a[1] : a[3], 16);
+    float k = (up2 ? k1 : k0) + __shfl_xor_sync(kAll, up2 ? k0 : k1, 8);
+    k += __shfl_xor_sync(kAll, k, 4);
+    k += __shfl_xor_sync(kAll, k, 2);
+    return k + __shfl_xor_sync(kAll, k, 1);
+}
+
+template <bool kXGlobal>
+__device__ __forceinline__ void gemv_q4_r4_body(const QGemvParams& p) {
+    constexpr int SBB = 144;
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem) + warp * p.stages;
+    size_t off = ((size_t)nwarps * p.stages * 8 + 127) & ~(size_t)127;
+    uint8_t* xs = smem + off;
+    if constexpr (!kXGlobal) off += (xq_r4_bytes(p.ksteps) + 127) & ~(size_t)127;
+    uint8_t* stages = smem + off + (size_t)warp * p.stages * 32 * SBB;
+
+    pdl_launch_dependents();
+
+    int GW, gw, tiles_end;
+    if (p.contiguous) {
+        GW = nwarps;
+        gw = (int)((long long)blockIdx.x * p.ntiles / gridDim.x) + warp;
+        tiles_end = (int)((long long)(blockIdx.x + 1) * p.ntiles / gridDim.x);
+    } else {
+        GW = gridDim.x * nwarps;
+        gw = warp * gridDim.x + blockIdx.x;
+        tiles_end = p.ntiles;
+    }
+    const int my_tiles = gw < tiles_end ? (tiles_end - 1 - gw) / GW + 1 : 0;
+    const int nitems = my_tiles * p.ksteps;
+
+    if (lane == 0) {
+        for (int s = 0; s < p.stages; ++s) mbar_init(&bars[s], 1);
+        fence_mbar_init();
+    }
+    __syncwarp();
+    ItemCursor cur{gw, 0, 0, 0u}, iss{gw, 0, 0, 0u};
+    int issued = 0;
+    for (; issued < min(p.stages, nitems); ++issued) {
+        issue_item<kQ4_0>(p, iss.tile, iss.ks, iss.slot, stages, bars, lane);
+        iss.next(p, GW);
+    }
+
+    pdl_wait_primary();
+    uint32_t pre[kR4PreRows * 9];
+    bool have_pre = false;
+    if constexpr (!kXGlobal) {
+        const XGeom xg{1, p.nb, 3, p.ksteps, 1};
+        if (p.ksteps == 1 && blockDim.x == 512) {
+            // 64 blocks × 8 threads: one quad of x per thread, loaded first.
+            const int gq = threadIdx.x & 7, b = threadIdx.x >> 3;
+            const float4 v = load_act4(p.x, p.up, (size_t)b * kQK + gq * 4);
+            if (nitems > 0) {
+                const bool ok = mbar_wait_bounded(&bars[0], 0, p.err);
+                have_pre = __all_sync(0xffffffffu, ok);
+                if (have_pre) {
+                    const uint32_t* wp = reinterpret_cast<const uint32_t*>(stages + (lane >> 2) * 144 + (lane & 3) * 36);
+#pragma unroll
+                    for (int i = 0; i < kR4PreRows * 9; ++i) pre[i] = wp[(i / 9) * 288 + i % 9];
+                }
+            }
+            quantize_x_block(v, gq, true, xg, 0, b, xs);
+        } else {
+            quantize_x_rows<1>(p.x, p.ldx, p.up, p.ldu, xg, xs, threadIdx.x, blockDim.x);
+        }
+        __syncthreads();
+    }
+    const uint8_t* xb = kXGlobal ? p.xq : xs;
+
+    const int r = lane >> 3, g = lane & 7;
+    long long gather_off = 0;
+    if (p.gather) {
+        const GatherArgs* ga = p.gather;
+        const unsigned epoch = *reinterpret_cast<volatile const unsigned*>(ga->ctrl[ga->rank]);
+        gather_off = (long long)(epoch & 1u) * ga->area + (long long)ga->rank * ga->npad;
+    }
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+
+    for (int it = 0; it < nitems; ++it) {
+        const uint8_t* xslot = xb + ((size_t)cur.ks * 32 + lane) * 80;
+        const uint8_t* st = stages + (size_t)cur.slot * (32 * SBB);
+        if (it == 0 && have_pre) {
+            r4_item<!kXGlobal, kR4PreRows>(st, xslot, lane, acc, pre);
+        } else {
+            if (__any_sync(0xffffffffu, !mbar_wait_bounded(&bars[cur.slot], cur.phase, p.err))) {   // warp-uniform
+                ItemCursor c2 = cur;
+                for (int k = it + 1; k < issued; ++k) {
+                    c2.next(p, GW);
+                    mbar_wait_bounded(&bars[c2.slot], c2.phase, nullptr);
+                }
+                break;
+            }
+            r4_item<!kXGlobal, 0>(st, xslot, lane, acc, pre);
+        }
+        if (cur.ks == p.ksteps - 1) {
+            const float v = r4_reduce(acc, lane);
+            const int row = cur.tile * 4 + r;
+            if (p.gather) {   // this rank's slice in the local area and every peer's, over NVLink
+                const GatherArgs* ga = p.gather;
+                const long long o0 = gather_off + (long long)cur.tile * 4;
+                if ((cur.tile + 1) * 4 <= p.N && (o0 & 3) == 0) {
+                    const float v1 = __shfl_sync(0xffffffffu, v, 8), v2 = __shfl_sync(0xffffffffu, v, 16);
+                    const float v3 = __shfl_sync(0xffffffffu, v, 24);
+                    if (lane == 0)
+                        for (int rk = 0; rk < ga->world; ++rk)
+                            *reinterpret_cast<float4*>(ga->y[rk] + o0) = make_float4(v, v1, v2, v3);
+                } else if (g == 0 && row < p.N) {
+                    for (int rk = 0; rk < ga->world; ++rk) ga->y[rk][o0 + r] = v;
+                }
+            } else if (g == 0 && row < p.N) {
+                p.y[row] = v;
+            }
+#pragma unroll
+            for (int k = 0; k < 4; ++k) acc[k] = 0.0f;
+        }
+        __syncwarp();
+        if (issued < nitems) {
+            fence_proxy_async_smem();
+            issue_item<kQ4_0>(p, iss.tile, iss.ks, iss.slot, stages, bars, lane);
+            iss.next(p, GW);
+            ++issued;
+        }
+        cur.next(p, GW);
+    }
+    if (p.yhost) copy_y_to_host(p);   // every warp gets here, the ones that gave up too
+}
+
+template <bool kXGlobal>
+__global__ void __launch_bounds__(512, 2) gemv_q4_r4(const QGemvParams p) {
+    gemv_q4_r4_body<kXGlobal>(p);
 }
 
 // ---- tensor-core kernel for 3..8 rows of x -------------------------------------------
@@ -1082,7 +1300,12 @@ cudaError_t launch(Kern kernel, dim3 grid, dim3 block, size_t smem, const Launch
 template <int F, int M>
 cudaError_t launch_fast_m(const LaunchCfg& c, const QGemvParams& p, size_t smem, bool dump) {
     void (*k)(QGemvParams);
-    if constexpr (F == 0 && M <= 2) {
+    if constexpr (F == 0 && M == 1) {
+        if (p.r4) k = p.xq ? gemv_q4_r4<true> : gemv_q4_r4<false>;
+        else if (p.xq) k = gemv_q_fast2<F, M, true, false>;
+        else if (dump) k = gemv_q_fast<F, M, false, true>;
+        else k = gemv_q_fast2<F, M, false, false>;
+    } else if constexpr (F == 0 && M <= 2) {
         if (p.xq) k = gemv_q_fast2<F, M, true, false>;
         else if (dump) k = gemv_q_fast<F, M, false, true>;
         else k = gemv_q_fast2<F, M, false, false>;
@@ -1131,9 +1354,18 @@ cudaError_t occupancy(const void* fn, int threads, size_t smem, int* per_sm) {
     return occupancy_cached(fn, threads, smem, per_sm);
 }
 
-void plan_tiles(QGemvParams& p, bool fast) {
+void plan_tiles(QGemvParams& p, bool fast, int fmt, bool allow_r4) {
     p.nb = p.K / kQK;
     p.nsbp = (p.nb + 7) / 8;
+    p.r4 = fast && allow_r4 && fmt == kQ4_0 && p.M == 1 && p.K > 0 && p.K % 2048 == 0;
+    if (p.r4) {
+        p.G = 8;
+        p.log2G = 3;
+        p.TR = 4;
+        p.ksteps = p.K / 2048;
+        p.ntiles = (p.N + 3) / 4;
+        return;
+    }
     int G = 1, lg = 0;
     if (fast) {
         while (G < p.nsbp && G < 32) { G <<= 1; ++lg; }
@@ -1148,9 +1380,9 @@ void plan_tiles(QGemvParams& p, bool fast) {
     p.ntiles = (p.N + p.TR - 1) / p.TR;
 }
 
-size_t gemv_q_smem(int fmt, int M, int ksteps, int warps, int stages, bool x_in_smem) {
+size_t gemv_q_smem(int fmt, const QGemvParams& p, int warps, int stages, bool x_in_smem) {
     size_t off = ((size_t)warps * stages * 8 + 127) & ~(size_t)127;
-    if (x_in_smem) off += (xq_total_bytes(M, ksteps) + 127) & ~(size_t)127;
+    if (x_in_smem) off += (x_bytes(p) + 127) & ~(size_t)127;
     return off + (size_t)warps * stages * 32 * sb_bytes(fmt);
 }
 
@@ -1158,7 +1390,7 @@ cudaError_t launch_quantize_x(const LaunchCfg& c, const QGemvParams& p, uint8_t*
     const long long groups = (long long)p.M * p.nb;
     const long long grid = std::min<long long>((groups + kThreadsQuantX / 8 - 1) / (kThreadsQuantX / 8),
                                                (long long)c.num_sms * 4);
-    const XGeom xg{p.M, p.nb, p.log2G, p.ksteps};
+    const XGeom xg{p.M, p.nb, p.log2G, p.ksteps, p.r4};
     return launch(quantize_x_kernel, dim3((unsigned)std::max<long long>(grid, 1)), dim3(kThreadsQuantX), 0, c, p.x,
                   p.ldx, p.up, p.ldu, xg, xq);
 }
@@ -1173,7 +1405,7 @@ cudaError_t launch_silu_mul(cudaStream_t s, long long n, const float* gate, cons
 cudaError_t launch_gemv_q(const LaunchCfg& c, int fmt, QGemvParams p, bool fast, size_t* smem_used) {
     const bool dump = p.dump != nullptr;
     size_t smem = 0;
-    if (fast) smem = gemv_q_smem(fmt, p.M, p.ksteps, c.warps, p.stages, p.xq == nullptr);
+    if (fast) smem = gemv_q_smem(fmt, p, c.warps, p.stages, p.xq == nullptr);
     if (smem_used) *smem_used = smem;
     return fmt == kQ4_0 ? dispatch_m<kQ4_0>(c, p, fast, smem, dump) : dispatch_m<kQ8_0>(c, p, fast, smem, dump);
 }

@@ -33,6 +33,14 @@ __host__ __device__ constexpr int sb_bytes(int fmt) { return 8 * block_bytes(fmt
 // dx = NaN, which makes every output of that x row NaN, the reference's rule
 // (q8_0_scalar.cpp:142-164).
 __host__ __device__ inline size_t xq_total_bytes(int M, int ksteps) { return (size_t)M * ksteps * 10240; }
+
+// The four-row layout (Q4_0, one row of x, K a multiple of 2048; QGemvParams::r4):
+// a k-step is 2048 values (8 superblocks) and lane l = 4g + j of a warp takes
+// blocks 2j, 2j+1 of superblock g in all four rows of its tile. Its 80 bytes of
+// quantized x sit together: slot (ks·32 + l) at byte slot·80 holds the quants of
+// block 2j (32 bytes), of block 2j+1 (32 bytes), then (dx, bias) of each as float
+// pairs (bias = −8·Σ quants as int bits). 2560 bytes per k-step.
+__host__ __device__ inline size_t xq_r4_bytes(int ksteps) { return (size_t)ksteps * 2560; }
 __host__ __device__ inline size_t xq_off(int ksteps, int m, int ks, int j, int h, int g) {
     return (((((size_t)m * ksteps + ks) * 16 + 2 * j + h) * 32) + g) * 16;
 }
@@ -53,6 +61,7 @@ struct QGemvParams {
     int nsbp;              // ceil(nb / 8)
     int G, log2G, TR, ksteps, ntiles;
     int stages;            // shared-memory stages per warp (fast kernel)
+    int r4;                // fast kernel: the four-row layout (Q4_0, M = 1, K % 2048 == 0); set by plan_tiles
     int contiguous;        // fast kernel: 1 = each CTA takes a contiguous range of tiles, 0 = tiles interleaved over CTAs
     int split;             // tensor-core kernel: K parts per 16-row tile (set by its launcher)
     // Tensor-core kernel with x larger than shared memory: K is cut into
@@ -93,7 +102,11 @@ struct GatherArgs {
 
 // Fill the tiling of p (p.M, p.N, p.K set): the fast kernel's G = the
 // smallest power of two >= nsbp, at most 32; the generic kernel's G = 32.
-void plan_tiles(QGemvParams& p, bool fast);
+// fmt given and the four-row conditions met (fast, Q4_0, M == 1, K % 2048 == 0,
+// allow_r4): the four-row layout, G = 8, TR = 4, one k-step per 2048 values.
+void plan_tiles(QGemvParams& p, bool fast, int fmt = -1, bool allow_r4 = true);
+// Bytes of quantized x of this plan (either layout).
+inline size_t x_bytes(const QGemvParams& p) { return p.r4 ? xq_r4_bytes(p.ksteps) : xq_total_bytes(p.M, p.ksteps); }
 
 // Sets the message smk_last_error() returns on this thread.
 void set_last_error(const char* msg);
@@ -111,8 +124,8 @@ struct LaunchCfg {
     int ctas_per_sm = 1;   // cap on resident CTAs per SM of the fast kernel
 };
 
-// Quantize p.x (or silu(p.x) * p.up) into the layout above at xq (global
-// memory, xq_total_bytes(M, ksteps)).
+// Quantize p.x (or silu(p.x) * p.up) into the layout of the plan (lane-major,
+// or four-row when p.r4) at xq (global memory, x_bytes(p) bytes).
 cudaError_t launch_quantize_x(const LaunchCfg& c, const QGemvParams& p, uint8_t* xq);
 // out[i] = silu(gate[i]) * up[i] for i < n, as the fused GEMV forms its
 // activations (test hook and unfused path).
@@ -121,7 +134,7 @@ cudaError_t launch_silu_mul(cudaStream_t s, long long n, const float* gate, cons
 // stream as whole 16-byte units); otherwise the generic kernel.
 cudaError_t launch_gemv_q(const LaunchCfg& c, int fmt, QGemvParams p, bool fast, size_t* smem_used);
 // Size of the fast kernel's dynamic shared memory for this launch.
-size_t gemv_q_smem(int fmt, int M, int ksteps, int warps, int stages, bool x_in_smem);
+size_t gemv_q_smem(int fmt, const QGemvParams& p, int warps, int stages, bool x_in_smem);
 
 // Wait until every peer delivered this step's slice, then advance the epoch
 // (one warp; bounded wait, kErrPeerTimeout on err). Launched after a fused

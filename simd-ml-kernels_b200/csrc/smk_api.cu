@@ -194,7 +194,9 @@ smk::LaunchCfg cfg_for(smk_ctx* c, cudaStream_t s) {
 // SM (8192x28672: 29.7 µs against 34.1 for 8 warps x 2 stages x 2 CTAs with
 // interleaved tiles; 16384x2048: 5.24 against 5.58 µs for one CTA per SM).
 void auto_shape(smk_ctx* c, smk::QGemvParams& p, smk::LaunchCfg* l, int* stages) {
-    const bool large = (long long)p.ntiles >= 64LL * c->num_sms;
+    // Work items: tiles, or (four-row layout) tiles times their 2048-value k-steps.
+    const long long items = (long long)p.ntiles * (p.r4 ? p.ksteps : 1);
+    const bool large = items >= 64LL * c->num_sms;
     if (c->warps <= 0) l->warps = 16;
     if (c->ctas_per_sm <= 0) l->ctas_per_sm = large ? 1 : 2;
     *stages = c->stages > 0 ? c->stages : (large ? 2 : 1);
@@ -225,23 +227,23 @@ QPlan plan_q(smk_ctx* c, smk::LaunchCfg* l, smk_qformat fmt, int M, int N, int K
     p.M = M; p.N = N; p.K = K;
     p.err = c->d_err;
     q.fast = (K % 256 == 0) && ((reinterpret_cast<uintptr_t>(Wq) & 15) == 0);
-    smk::plan_tiles(p, q.fast);
-    q.x_bytes = smk::xq_total_bytes(M, p.ksteps);
+    smk::plan_tiles(p, q.fast, fmt, !want_dump);
+    q.x_bytes = smk::x_bytes(p);
     if (q.fast) {
         auto_shape(c, p, l, &p.stages);
         // Quantized x in shared memory while it is small; otherwise one
         // quantize kernel writes it to scratch and every CTA reads it there.
         const size_t budget = 64 * 1024;
         q.x_in_smem = q.x_bytes <= budget || want_dump;
-        size_t smem = smk::gemv_q_smem(fmt, M, p.ksteps, l->warps, p.stages, q.x_in_smem);
+        size_t smem = smk::gemv_q_smem(fmt, p, l->warps, p.stages, q.x_in_smem);
         while (smem > c->smem_optin && p.stages > 1) {
             --p.stages;
-            smem = smk::gemv_q_smem(fmt, M, p.ksteps, l->warps, p.stages, q.x_in_smem);
+            smem = smk::gemv_q_smem(fmt, p, l->warps, p.stages, q.x_in_smem);
         }
         if (smem > c->smem_optin) {   // e.g. a dump of a huge M·K: the generic kernel
             q.fast = false;
             smk::plan_tiles(p, false);
-            q.x_bytes = smk::xq_total_bytes(M, p.ksteps);
+            q.x_bytes = smk::x_bytes(p);
         }
     }
     if (!q.fast) q.x_in_smem = false;
