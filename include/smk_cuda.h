@@ -174,6 +174,13 @@ smk_status smk_quantize_x(smk_ctx* ctx, int M, int K, const float* x, int64_t ld
                           void* stream);
 smk_status smk_block_sums(smk_ctx* ctx, smk_qformat fmt, int M, int N, int K, const float* x, int64_t ldx,
                           const uint8_t* Wq, int32_t* out, void* stream);
+/* Test hook, no reference counterpart: the activation quantizer's exact steps
+ * (RN(a/127) by an FMA remainder, RN(1/d) by one Newton-Raphson step from the
+ * hardware approximation, round half away from zero by a biased truncation)
+ * against CUDA's __fdiv_rn, __frcp_rn and roundf over their whole domains
+ * (every finite a >= 0, every 2^-126 <= d <= 2^126, every |t| <= 128): out[0..2]
+ * receive the mismatch counts, all zero on a correct build. Synchronous. */
+smk_status smk_check_x_arith(smk_ctx* ctx, unsigned long long* out /* [3] */);
 
 /* ---- quantized decode GEMV without any allocation -------------------------
  * No counterpart in the reference. For callers that cannot call cudaMalloc:

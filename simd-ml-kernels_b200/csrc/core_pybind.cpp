@@ -756,4 +756,12 @@ PYBIND11_MODULE(_core, m) {
     });
     m.def("_quantize_x", &py_quantize_x);
     m.def("_block_sums", &py_block_sums);
+    m.def("_check_x_arith", []() {
+        unsigned long long bad[3] = {0, 0, 0};
+        {
+            py::gil_scoped_release nogil;
+            check(smk_check_x_arith(ctx_for(current_device_hint), bad));
+        }
+        return py::make_tuple(bad[0], bad[1], bad[2]);
+    });
 }

@@ -90,21 +90,23 @@ struct Q8Quad {
 
 __device__ __forceinline__ Q8Quad quantize_quad(float4 v) {
     constexpr unsigned gmask = 0xffffffffu;
-    unsigned fin = finite_bits(v.x) & finite_bits(v.y) & finite_bits(v.z) & finite_bits(v.w);
-    float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+    // max |v| over the block as integer bits: for non-negative floats the bit
+    // order is the value order, and +inf / NaN lie above every finite value, so
+    // one reduction gives both amax and whether the block is finite.
+    unsigned a = max(max(__float_as_uint(v.x) & 0x7fffffffu, __float_as_uint(v.y) & 0x7fffffffu),
+                     max(__float_as_uint(v.z) & 0x7fffffffu, __float_as_uint(v.w) & 0x7fffffffu));
 #pragma unroll
-    for (int o = 4; o > 0; o >>= 1) {
-        amax = fmaxf(amax, __shfl_xor_sync(gmask, amax, o));
-        fin &= __shfl_xor_sync(gmask, fin, o);
-    }
-    const float d = __fdiv_rn(amax, 127.0f);
-    // IEEE reciprocal, round to nearest: the same value as 1.0f / d.
-    float id = d != 0.0f ? __frcp_rn(d) : 0.0f;
+    for (int o = 4; o > 0; o >>= 1) a = max(a, __shfl_xor_sync(gmask, a, o));
+    const bool fin = a < 0x7f800000u;
+    const float d = div127_rn(__uint_as_float(a));   // RN(amax / 127)
+    // RN(1 / d), 0 when d is 0 or the reciprocal overflows (the reference's id).
+    float id = d != 0.0f ? rcp_rn(d) : 0.0f;
     if (!(id <= FLT_MAX)) id = 0.0f;
-    const int q0 = fin ? (int)roundf(__fmul_rn(v.x, id)) : 0;
-    const int q1 = fin ? (int)roundf(__fmul_rn(v.y, id)) : 0;
-    const int q2 = fin ? (int)roundf(__fmul_rn(v.z, id)) : 0;
-    const int q3 = fin ? (int)roundf(__fmul_rn(v.w, id)) : 0;
+    // |v·id| <= 127·(1 + 2^-22) < 128 for a finite block.
+    const int q0 = fin ? round_half_away(__fmul_rn(v.x, id)) : 0;
+    const int q1 = fin ? round_half_away(__fmul_rn(v.y, id)) : 0;
+    const int q2 = fin ? round_half_away(__fmul_rn(v.z, id)) : 0;
+    const int q3 = fin ? round_half_away(__fmul_rn(v.w, id)) : 0;
     Q8Quad r;
     r.word = (uint32_t)(q0 & 0xff) | ((uint32_t)(q1 & 0xff) << 8) | ((uint32_t)(q2 & 0xff) << 16) |
              ((uint32_t)(q3 & 0xff) << 24);
@@ -189,6 +191,30 @@ __global__ void __launch_bounds__(256) silu_mul_kernel(long long n, const float*
     pdl_wait_primary();
     for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
         out[i] = silu_mul1(g[i], u[i]);
+}
+
+// Test hook: the exact helpers of quantize_quad against CUDA's own operations over
+// their whole domains; bad[0] divisions (every finite a >= 0), bad[1] reciprocals
+// (every 2^-126 <= d <= 2^126), bad[2] roundings (every |t| <= 128) that differ.
+__global__ void __launch_bounds__(256) check_x_arith_kernel(unsigned long long* bad) {
+    unsigned long long b0 = 0, b1 = 0, b2 = 0;
+    const unsigned long long stride = (unsigned long long)gridDim.x * blockDim.x;
+    const unsigned long long t0 = (unsigned long long)blockIdx.x * blockDim.x + threadIdx.x;
+    for (unsigned long long i = t0; i < 0x7f800000ull; i += stride) {
+        const float a = __uint_as_float((unsigned)i);
+        b0 += __float_as_uint(div127_rn(a)) != __float_as_uint(__fdiv_rn(a, 127.0f));
+    }
+    for (unsigned long long i = 0x00800000ull + t0; i <= 0x7e800000ull; i += stride) {
+        const float d = __uint_as_float((unsigned)i);
+        b1 += __float_as_uint(rcp_rn(d)) != __float_as_uint(__frcp_rn(d));
+    }
+    for (unsigned long long i = t0; i <= 0x43000000ull; i += stride) {   // 0 .. 128
+        const float t = __uint_as_float((unsigned)i);
+        b2 += (round_half_away(t) != (int)roundf(t)) + (round_half_away(-t) != (int)roundf(-t));
+    }
+    atomicAdd(&bad[0], b0);
+    atomicAdd(&bad[1], b1);
+    atomicAdd(&bad[2], b2);
 }
 
 // ---- integer block dots -----------------------------------------------------------
@@ -1393,6 +1419,11 @@ cudaError_t launch_quantize_x(const LaunchCfg& c, const QGemvParams& p, uint8_t*
     const XGeom xg{p.M, p.nb, p.log2G, p.ksteps, p.r4};
     return launch(quantize_x_kernel, dim3((unsigned)std::max<long long>(grid, 1)), dim3(kThreadsQuantX), 0, c, p.x,
                   p.ldx, p.up, p.ldu, xg, xq);
+}
+
+cudaError_t launch_check_x_arith(cudaStream_t s, unsigned long long* bad) {
+    check_x_arith_kernel<<<148 * 8, 256, 0, s>>>(bad);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_silu_mul(cudaStream_t s, long long n, const float* gate, const float* up, float* out) {

@@ -127,6 +127,9 @@ struct LaunchCfg {
 // Quantize p.x (or silu(p.x) * p.up) into the layout of the plan (lane-major,
 // or four-row when p.r4) at xq (global memory, x_bytes(p) bytes).
 cudaError_t launch_quantize_x(const LaunchCfg& c, const QGemvParams& p, uint8_t* xq);
+// Test hook: mismatch counts of the x quantizer's exact helpers (bad[3], zeroed
+// by the caller) against CUDA's divide, reciprocal and roundf.
+cudaError_t launch_check_x_arith(cudaStream_t s, unsigned long long* bad);
 // out[i] = silu(gate[i]) * up[i] for i < n, as the fused GEMV forms its
 // activations (test hook and unfused path).
 cudaError_t launch_silu_mul(cudaStream_t s, long long n, const float* gate, const float* up, float* out);

@@ -954,4 +954,19 @@ smk_status smk_block_sums(smk_ctx* c, smk_qformat fmt, int M, int N, int K, cons
     return run_q(c, fmt, M, N, K, x, ldx, Wq, y, N, s, out);
 }
 
+smk_status smk_check_x_arith(smk_ctx* c, unsigned long long* out) {
+    if (!c || !out) return fail(SMK_ERR_ARGUMENT, "ctx and out must not be NULL");
+    DeviceGuard g(c->device);
+    unsigned long long* bad;
+    {
+        std::lock_guard<std::mutex> lock(c->mu_scratch);
+        SMK_CUDA(c->test_buf.reserve(3 * sizeof(unsigned long long)), "cudaMalloc (test)");
+        bad = static_cast<unsigned long long*>(c->test_buf.ptr);
+        SMK_CUDA(cudaMemset(bad, 0, 3 * sizeof(unsigned long long)), "cudaMemset");
+        SMK_CUDA(smk::launch_check_x_arith(nullptr, bad), "check launch");
+        SMK_CUDA(cudaMemcpy(out, bad, 3 * sizeof(unsigned long long), cudaMemcpyDeviceToHost), "cudaMemcpy");
+    }
+    return SMK_OK;
+}
+
 }  // extern "C"

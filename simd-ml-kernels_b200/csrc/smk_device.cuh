@@ -174,6 +174,45 @@ __device__ __forceinline__ uint32_t f32_to_f16_bits(float f) {
     return sign | (bits >= 0x7c00 ? 0x7c00u : (uint32_t)bits);
 }
 
+// ---- exact arithmetic of the activation quantizer (quantize_x_q8: d = amax/127,
+// id = 1/d, q = round-half-away(v·id), each rounded to nearest as IEEE divides,
+// reciprocals and roundf do), in fewer dependent steps. Each is checked bit for bit
+// against CUDA's __fdiv_rn / __frcp_rn / roundf over its whole domain by
+// smk_check_x_arith (a GPU test).
+
+// RN(a / 127) for finite a >= 0: q = RN(a·c), c = RN(1/127); the remainder
+// a − 127·q is exact in one FMA, and RN(q + r·c) is the correctly rounded quotient
+// (Brisebarre, Muller and Raina, "Accelerating correctly rounded floating-point
+// division when the divisor is known in advance", IEEE Trans. Computers 53(8),
+// 2004; for this divisor it holds for every finite a >= 0).
+__device__ __forceinline__ float div127_rn(float a) {
+    constexpr float c = 0x1.020408p-7f;   // RN(1/127)
+    const float q = __fmul_rn(a, c);
+    return __fmaf_rn(__fmaf_rn(-127.0f, q, a), c, q);
+}
+
+// RN(1 / d): the hardware approximation refined by one Newton-Raphson step with
+// the residual e = 1 − d·y formed exactly by an FMA, y' = RN(y + e·y) (Markstein,
+// "Computation of elementary functions on the IBM RISC System/6000 processor",
+// IBM J. Res. Dev. 34(1), 1990). Correctly rounded for 2^-126 <= |d| <= 2^126
+// (every such d checked on B200); outside that range (zero, subnormal, huge,
+// non-finite) it defers to __frcp_rn.
+__device__ __forceinline__ float rcp_rn(float d) {
+    const float a = fabsf(d);
+    if (!(a >= 0x1p-126f && a <= 0x1p126f)) return __frcp_rn(d);
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(d));
+    return __fmaf_rn(__fmaf_rn(-d, y, 1.0f), y, y);
+}
+
+// round-half-away-from-zero(t) as an integer for |t| <= 128: t + copysign(c, t)
+// with c = 1/2 − 2^-25, truncated. Adding exactly 1/2 would round 1/2 − 2^-25 + 1/2
+// up to 1; with c the sum of a value below a half-integer never reaches the next
+// integer, and a half-integer or more always does (checked for every |t| <= 128).
+__device__ __forceinline__ int round_half_away(float t) {
+    return __float2int_rz(__fadd_rn(t, copysignf(0x1.fffffep-2f, t)));
+}
+
 // Bits [s, s+32) of the 64-bit value hi:lo.
 __device__ __forceinline__ uint32_t funnel(uint32_t lo, uint32_t hi, uint32_t s) {
     return __funnelshift_r(lo, hi, s);

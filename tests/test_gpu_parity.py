@@ -84,6 +84,16 @@ def test_quantize_x_bit_exact(sk, torch):
         np.testing.assert_array_equal(dx.cpu().numpy().view(np.uint32), want_dx.view(np.uint32))
 
 
+def test_x_quantizer_arithmetic_exhaustive(sk):
+    """The activation quantizer's shortened steps are CUDA's correctly rounded
+    operations over their whole domains: RN(a/127) for every finite a >= 0,
+    RN(1/d) for every 2^-126 <= d <= 2^126, and round half away from zero for
+    every |t| <= 128 (the range v·(1/d) spans for a finite block), bit for bit."""
+    from simd_ml_kernels import _core
+    div, rcp, rnd = _core._check_x_arith()
+    assert (div, rcp, rnd) == (0, 0, 0), f"mismatches: divide {div}, reciprocal {rcp}, round {rnd}"
+
+
 @pytest.mark.parametrize("fmt", ["q4_0", "q8_0"])
 def test_quantize_weights_byte_exact(sk, fmt):
     g = np.load(os.path.join(GOLD, "ref_quantize.npz"))
