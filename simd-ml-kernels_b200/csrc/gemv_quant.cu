@@ -118,6 +118,14 @@ __device__ __forceinline__ Q8Quad quantize_quad(float4 v) {
     return r;
 }
 
+// int → float without a conversion instruction: for |v| < 2^22 the float with
+// bits 0x4B400000 + v is 1.5·2^23 + v exactly (ulp 1 in [2^23, 2^24)), so
+// subtracting 1.5·2^23 leaves float(v) exactly. A block's bias −8·Σq rides in the
+// same integer add: float(isum) = bits(c + magic − 8Σq) − 1.5·2^23, with
+// |isum| ≤ 32·15·127 + 8·32·127 far below 2^22 (Q8_0: ≤ 32·127·127).
+constexpr int kIntToFloatMagic = 0x4B400000;
+constexpr float kIntToFloatMagicF = 12582912.0f;
+
 // quantize_quad, stored in the lane-major layout; lanes with valid == false
 // compute on their (zero) values and store nothing.
 __device__ __forceinline__ void quantize_x_block(float4 v, int gq, bool valid, const XGeom& xg, int m, int b,
@@ -128,7 +136,11 @@ __device__ __forceinline__ void quantize_x_block(float4 v, int gq, bool valid, c
         uint8_t* slot = xb + (ks * 32u + g * 4u + (jb >> 1)) * 80u;
         if (!valid) return;
         *reinterpret_cast<uint32_t*>(slot + (jb & 1u) * 32u + (unsigned)gq * 4u) = q.word;
-        if (gq == 0) *reinterpret_cast<float2*>(slot + 64u + (jb & 1u) * 8u) = make_float2(q.dx, __int_as_float(-8 * q.s));
+        // The bias carries the magic number: the block's sum leaves dp4a as the bit
+        // pattern of 1.5·2^23 + isum, and one exact subtraction makes it a float.
+        if (gq == 0)
+            *reinterpret_cast<float2*>(slot + 64u + (jb & 1u) * 8u) =
+                make_float2(q.dx, __int_as_float(kIntToFloatMagic - 8 * q.s));
         return;
     }
     // Offsets in 32 bits (the layout stays far below 4 GiB), no division.
@@ -584,8 +596,9 @@ __global__ void __launch_bounds__(32) gather_wait_kernel(const GatherArgs* __res
 // bytes of x (xq_r4_bytes layout) are loaded once and serve four rows from
 // registers, and its weights are 9 words per row at byte 1152·row + 144·g + 36·j
 // of the stage (32 distinct banks across the warp). Per block the arithmetic is the
-// fast kernel's: the exact int32 isum from the −8·Σq start, then
-// acc = fma(float(isum), fp16(dw)·dx, acc); each lane adds its two blocks of every
+// fast kernel's: the exact int32 isum from the −8·Σq start (plus kIntToFloatMagic, so the
+// sum converts to float by one exact subtraction instead of an integer-to-float
+// conversion), then acc = fma(float(isum), fp16(dw)·dx, acc); each lane adds its two blocks of every
 // k-step in order, and a fixed shuffle tree adds the 32 lanes, so the result
 // depends on neither the launch shape nor where x was quantized.
 //
@@ -608,7 +621,8 @@ __device__ __forceinline__ float r4_row(const uint32_t (&w)[9], const uint4& x0l
     h = dp4a_us(q[2] & 0xF0F0F0F0u, x0h.z, h);
     a = dp4a_us(q[3] & 0x0F0F0F0Fu, x0l.w, a);
     h = dp4a_us(q[3] & 0xF0F0F0F0u, x0h.w, h);
-    acc = fmaf((float)(a + (h >> 4)), __fmul_rn(half_bits_to_float(w[0]), __uint_as_float(dd.x)), acc);
+    acc = fmaf(__fsub_rn(__int_as_float(a + (h >> 4)), kIntToFloatMagicF), __fmul_rn(half_bits_to_float(w[0]), __uint_as_float(dd.x)),
+               acc);
     a = dp4a_us(w[5] & 0x0F0F0F0Fu, x1l.x, (int)dd.w);
     h = dp4a_us(w[5] & 0xF0F0F0F0u, x1h.x, 0);
     a = dp4a_us(w[6] & 0x0F0F0F0Fu, x1l.y, a);
@@ -617,7 +631,8 @@ __device__ __forceinline__ float r4_row(const uint32_t (&w)[9], const uint4& x0l
     h = dp4a_us(w[7] & 0xF0F0F0F0u, x1h.z, h);
     a = dp4a_us(w[8] & 0x0F0F0F0Fu, x1l.w, a);
     h = dp4a_us(w[8] & 0xF0F0F0F0u, x1h.w, h);
-    return fmaf((float)(a + (h >> 4)), __fmul_rn(half_bits_to_float(w[4] >> 16), __uint_as_float(dd.z)), acc);
+    return fmaf(__fsub_rn(__int_as_float(a + (h >> 4)), kIntToFloatMagicF),
+                __fmul_rn(half_bits_to_float(w[4] >> 16), __uint_as_float(dd.z)), acc);
 }
 
 // Rows of the first item read into registers while x is in flight (the rest of
@@ -806,13 +821,7 @@ __global__ void __launch_bounds__(512, 2) gemv_q4_r4(const QGemvParams p) {
 // block b the B-fragment words of row m (0..7) for lane t, (word t, word 4+t)
 // side by side at ((b·8 + m)·4 + t)·8 bytes; after nb·256 bytes, the pair
 // (dx, bits of kIntToFloatMagic − 8·Σq) of (b, m) at (b·8 + m)·8.
-//
-// int → float without a conversion instruction: for |v| < 2^22 the float with
-// bits 0x4B400000 + v is 1.5·2^23 + v exactly (ulp 1 in [2^23, 2^24)), so
-// subtracting 1.5·2^23 leaves float(v) exactly. The Q4_0 bias −8·Σq rides in
-// the same integer add: float(isum) = bits(c + magic − 8Σq) − 1.5·2^23, with
-// |isum| ≤ 32·15·127 + 8·32·127 far below 2^22 (Q8_0: ≤ 32·127·127).
-constexpr int kIntToFloatMagic = 0x4B400000;
+// float(isum) comes from the magic-number add (kIntToFloatMagic).
 constexpr int kMmaWarps = 16;
 // A warp item is 16 rows × 8 blocks, fetched as one box of a 2-D tensor map
 // over the weights (rows of nb·block bytes; Q4_0 as bytes, Q8_0 as 16-bit

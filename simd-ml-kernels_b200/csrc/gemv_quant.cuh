@@ -39,7 +39,7 @@ __host__ __device__ inline size_t xq_total_bytes(int M, int ksteps) { return (si
 // blocks 2j, 2j+1 of superblock g in all four rows of its tile. Its 80 bytes of
 // quantized x sit together: slot (ks·32 + l) at byte slot·80 holds the quants of
 // block 2j (32 bytes), of block 2j+1 (32 bytes), then (dx, bias) of each as float
-// pairs (bias = −8·Σ quants as int bits). 2560 bytes per k-step.
+// pairs (bias = 0x4B400000 − 8·Σ quants as int bits). 2560 bytes per k-step.
 __host__ __device__ inline size_t xq_r4_bytes(int ksteps) { return (size_t)ksteps * 2560; }
 __host__ __device__ inline size_t xq_off(int ksteps, int m, int ks, int j, int h, int g) {
     return (((((size_t)m * ksteps + ks) * 16 + 2 * j + h) * 32) + g) * 16;
