@@ -93,7 +93,8 @@ extern "C" smk_status smk_gemv_q_noalloc(smk_qformat fmt, int M, int N, int K, c
     smk::QGemvParams p = {};
     p.x = x; p.ldx = ldx; p.w = Wq; p.y = y; p.ldy = ldy;
     p.M = M; p.N = N; p.K = K;
-    smk::plan_tiles(p, fast, (int)fmt);
+    // The plan (and so the accumulation order) of smk_gemv_q on a 148-SM B200.
+    smk::plan_tiles(p, fast, (int)fmt, true, 148);
     const size_t need = smk::x_bytes(p);
     if (need > kNoAllocScratchBytes) {
         char buf[256];

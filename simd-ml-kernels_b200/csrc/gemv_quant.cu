@@ -1389,10 +1389,21 @@ cudaError_t occupancy(const void* fn, int threads, size_t smem, int* per_sm) {
     return occupancy_cached(fn, threads, smem, per_sm);
 }
 
-void plan_tiles(QGemvParams& p, bool fast, int fmt, bool allow_r4) {
+bool r4_shape(int N, int K, int num_sms) {
+    if (K == 2048) return true;
+    // Longer rows: a warp runs the k-steps of its tiles one after another, so the
+    // layout needs tiles for every warp (8 per SM), and it is used where x is
+    // quantized once into global memory (K >= 8192, N <= 16384). Measured on
+    // B200, graph-chained: 8192x28672 23.6 us against 28.8; the Llama down
+    // projection 2048x8192 (3.5 tiles per SM) and 28672x8192 (x in shared
+    // memory) were slower this way.
+    return K % 2048 == 0 && K >= 8192 && N <= 16384 && (long long)N >= 32LL * num_sms;
+}
+
+void plan_tiles(QGemvParams& p, bool fast, int fmt, bool allow_r4, int num_sms) {
     p.nb = p.K / kQK;
     p.nsbp = (p.nb + 7) / 8;
-    p.r4 = fast && allow_r4 && fmt == kQ4_0 && p.M == 1 && p.K > 0 && p.K % 2048 == 0;
+    p.r4 = fast && allow_r4 && fmt == kQ4_0 && p.M == 1 && p.K > 0 && r4_shape(p.N, p.K, num_sms);
     if (p.r4) {
         p.G = 8;
         p.log2G = 3;

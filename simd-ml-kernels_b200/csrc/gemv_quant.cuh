@@ -102,9 +102,13 @@ struct GatherArgs {
 
 // Fill the tiling of p (p.M, p.N, p.K set): the fast kernel's G = the
 // smallest power of two >= nsbp, at most 32; the generic kernel's G = 32.
-// fmt given and the four-row conditions met (fast, Q4_0, M == 1, K % 2048 == 0,
-// allow_r4): the four-row layout, G = 8, TR = 4, one k-step per 2048 values.
-void plan_tiles(QGemvParams& p, bool fast, int fmt = -1, bool allow_r4 = true);
+// fmt given and the four-row conditions met (fast, Q4_0, M == 1, allow_r4 and
+// r4_shape): the four-row layout, G = 8, TR = 4, one k-step per 2048 values.
+void plan_tiles(QGemvParams& p, bool fast, int fmt = -1, bool allow_r4 = true, int num_sms = 148);
+// Shapes that take the four-row layout: K == 2048; or K a multiple of 2048, at
+// least 8192, with N <= 16384 (x quantized once into global memory) and at
+// least 8 four-row tiles per SM.
+bool r4_shape(int N, int K, int num_sms);
 // Bytes of quantized x of this plan (either layout).
 inline size_t x_bytes(const QGemvParams& p) { return p.r4 ? xq_r4_bytes(p.ksteps) : xq_total_bytes(p.M, p.ksteps); }
 

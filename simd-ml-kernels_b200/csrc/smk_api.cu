@@ -227,7 +227,7 @@ QPlan plan_q(smk_ctx* c, smk::LaunchCfg* l, smk_qformat fmt, int M, int N, int K
     p.M = M; p.N = N; p.K = K;
     p.err = c->d_err;
     q.fast = (K % 256 == 0) && ((reinterpret_cast<uintptr_t>(Wq) & 15) == 0);
-    smk::plan_tiles(p, q.fast, fmt, !want_dump);
+    smk::plan_tiles(p, q.fast, fmt, !want_dump, c->num_sms);
     q.x_bytes = smk::x_bytes(p);
     if (q.fast) {
         auto_shape(c, p, l, &p.stages);

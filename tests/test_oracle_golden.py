@@ -166,3 +166,25 @@ def test_gemv_slice_rules():
                 assert b == c
             for lo, hi in edges:
                 assert lo % 8 == 0 and lo <= hi
+
+
+def test_config_pins_reproduce_on_cpu():
+    """bench.py's generators give, on any host, the bytes the GPU tests pin
+    (tests/golden/config_pins.json, written with the reference's quantizer):
+    config 0's Q4_0 weights through the oracle's quantizer, config 3's
+    float32 weights and their bfloat16 / float16 roundings."""
+    import hashlib
+    import json
+
+    import bench
+
+    pins = json.load(open(os.path.join(os.path.dirname(__file__), "golden", "config_pins.json")))
+    sha = lambda a: hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()  # noqa: E731
+    W, x = bench.config0().full()
+    assert sha(O.quantize("q4_0", W)) == pins["config0"]["w_sha256"] and sha(x) == pins["config0"]["x_sha256"]
+    N, K = bench.CFG3_SHAPES[0]
+    W, X = bench.config3(N, K).full()
+    p3 = pins["config3"][0]
+    assert sha(W) == p3["float32_sha256"] and sha(X) == p3["x_sha256"]
+    assert sha(O.bf16_bits(W)) == p3["bfloat16_sha256"]
+    assert sha(W.astype(np.float16).view(np.uint16)) == p3["float16_sha256"]
