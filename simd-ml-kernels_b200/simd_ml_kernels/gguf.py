@@ -34,22 +34,35 @@ next multiple of general.alignment (default 32) after the infos.
 
 from __future__ import annotations
 
-import struct
 import sys
 from dataclasses import dataclass
+from functools import partial
 
 import numpy as np
 
 from . import _core
 
+# ggml tensor type codes of the format (the public constants of this module).
 GGML_F32, GGML_F16, GGML_Q4_0, GGML_Q8_0, GGML_BF16 = 0, 1, 2, 8, 30
 TYPE_NAMES = {GGML_F32: "F32", GGML_F16: "F16", GGML_Q4_0: "Q4_0", GGML_Q8_0: "Q8_0", GGML_BF16: "BF16"}
-# (bytes, values) per block of each supported ggml type
-BLOCK = {GGML_F32: (4, 1), GGML_F16: (2, 1), GGML_BF16: (2, 1), GGML_Q4_0: (18, 32), GGML_Q8_0: (34, 32)}
 
-# GGUF metadata value types: 0-7, 10-12 scalars, 8 string, 9 array.
-_SCALARS = {0: "<B", 1: "<b", 2: "<H", 3: "<h", 4: "<I", 5: "<i", 6: "<f", 7: "<?", 10: "<Q", 11: "<q", 12: "<d"}
-_HOST_DTYPE = {GGML_F32: "<f4", GGML_F16: "<f2", GGML_BF16: "<u2"}
+
+@dataclass(frozen=True)
+class _TensorKind:
+    """How a ggml type is stored: `block_bytes` bytes hold `block_values`
+    values along the innermost dimension; `host` is the NumPy dtype of a dense
+    type's host view (None: rows of raw blocks)."""
+
+    block_bytes: int
+    block_values: int
+    host: str | None
+
+
+_KINDS = {GGML_F32: _TensorKind(4, 1, "<f4"), GGML_F16: _TensorKind(2, 1, "<f2"),
+          GGML_BF16: _TensorKind(2, 1, "<u2"), GGML_Q4_0: _TensorKind(18, 32, None),
+          GGML_Q8_0: _TensorKind(34, 32, None)}
+# (bytes, values) per block of each supported ggml type
+BLOCK = {t: (k.block_bytes, k.block_values) for t, k in _KINDS.items()}
 _ALIGN = 256   # start of each tensor in the device allocation
 
 
@@ -72,35 +85,95 @@ class GGUFTensor:
         return self.shape[-1] // bvals * bsize
 
 
-class _Reader:
-    def __init__(self, buf, path):
-        self.buf, self.pos, self.path = buf, 0, path
+class _Fields:
+    """Little-endian fields of a mapped file, read at a moving offset. Every read
+    is checked against the end of the file first."""
 
-    def scalar(self, fmt: str):
-        (v,) = struct.unpack_from(fmt, self.buf, self.pos)
-        self.pos += struct.calcsize(fmt)
-        return v
+    def __init__(self, mm: np.ndarray, path: str):
+        self.mm, self.path, self.at = mm, path, 0
 
-    def string(self) -> str:
-        n = self.scalar("<Q")
-        s = bytes(self.buf[self.pos:self.pos + n]).decode("utf-8", errors="replace")
-        self.pos += n
-        return s
+    def _span(self, nbytes: int) -> int:
+        start = self.at
+        if nbytes < 0 or start + nbytes > self.mm.shape[0]:
+            raise ValueError(f"{self.path}: the header runs past the end of the file")
+        self.at = start + nbytes
+        return start
 
-    def value(self, vtype: int):
-        if vtype in _SCALARS:
-            return self.scalar(_SCALARS[vtype])
-        if vtype == 8:
-            return self.string()
-        if vtype == 9:
-            etype, n = self.scalar("<I"), self.scalar("<Q")
-            if etype in _SCALARS and etype != 7:   # numeric arrays as NumPy (token scores, types)
-                dt = np.dtype(_SCALARS[etype])
-                a = np.frombuffer(self.buf, dtype=dt, count=n, offset=self.pos)
-                self.pos += n * dt.itemsize
-                return a
-            return [self.value(etype) for _ in range(n)]
-        raise ValueError(f"{self.path}: unknown GGUF metadata type {vtype}")
+    def number(self, dtype: str):
+        dt = np.dtype(dtype)
+        return np.frombuffer(self.mm, dt, 1, self._span(dt.itemsize))[0].item()
+
+    def u32(self) -> int:
+        return self.number("<u4")
+
+    def u64(self) -> int:
+        return self.number("<u8")
+
+    def text(self) -> str:
+        n = self.u64()
+        start = self._span(n)
+        return self.mm[start:start + n].tobytes().decode("utf-8", errors="replace")
+
+    def vector(self, dtype: str, count: int) -> np.ndarray:
+        dt = np.dtype(dtype)
+        return np.frombuffer(self.mm, dt, count, self._span(dt.itemsize * count))
+
+
+# Metadata value type codes of the format: numbers (little-endian, by NumPy
+# dtype), a string, or an array (element type code, count, elements).
+_NUMBER_DTYPES = {0: "u1", 1: "i1", 2: "<u2", 3: "<i2", 4: "<u4", 5: "<i4", 6: "<f4", 7: "?", 10: "<u8",
+                  11: "<i8", 12: "<f8"}
+_STRING, _ARRAY, _BOOL = 8, 9, 7
+
+
+def _read_array(f: _Fields):
+    """An array value. Numbers come back as one NumPy view of the file (token
+    scores and types of a vocabulary stay zero-copy); strings, booleans and
+    nested arrays as a list, as the reference's reader gives them."""
+    kind, count = f.u32(), f.u64()
+    if kind in _NUMBER_DTYPES and kind != _BOOL:
+        return f.vector(_NUMBER_DTYPES[kind], count)
+    read = _value_reader(kind, f.path)
+    return [read(f) for _ in range(count)]
+
+
+def _value_reader(kind: int, path: str):
+    if kind in _NUMBER_DTYPES:
+        return partial(_Fields.number, dtype=_NUMBER_DTYPES[kind])
+    if kind == _STRING:
+        return _Fields.text
+    if kind == _ARRAY:
+        return _read_array
+    raise ValueError(f"{path}: unknown GGUF metadata type {kind}")
+
+
+@dataclass
+class _Info:
+    name: str
+    dims: list[int]          # innermost first, as stored
+    type: int
+    rel_offset: int          # from the start of the data section
+
+
+def _tensor_view(path: str, mm: np.ndarray, base: int, info: _Info) -> GGUFTensor:
+    kind = _KINDS.get(info.type)
+    if kind is None:
+        raise ValueError(f"{path}: tensor {info.name} has ggml type {info.type} (not F32/F16/BF16/Q8_0/Q4_0)")
+    row_len = info.dims[0] if info.dims else 1
+    if row_len % kind.block_values:
+        raise ValueError(f"{path}: tensor {info.name}: row length {row_len} not a multiple of {kind.block_values}")
+    rows = 1
+    for d in info.dims[1:]:
+        rows *= d
+    row_bytes = row_len // kind.block_values * kind.block_bytes
+    nbytes = rows * row_bytes
+    start = base + info.rel_offset
+    if start + nbytes > mm.shape[0]:
+        raise ValueError(f"{path}: tensor {info.name} runs past the end of the file")
+    raw = mm[start:start + nbytes]
+    shape = tuple(int(d) for d in info.dims[::-1])
+    data = raw.view(kind.host).reshape(shape) if kind.host else raw.reshape(rows, row_bytes)
+    return GGUFTensor(info.name, info.type, shape, data, start, nbytes)
 
 
 class GGUF:
@@ -110,45 +183,27 @@ class GGUF:
     def __init__(self, path: str):
         self.path = path
         self._mm = np.memmap(path, dtype=np.uint8, mode="r")
-        if bytes(self._mm[:4]) != b"GGUF":
+        if self._mm[:4].tobytes() != b"GGUF":
             raise ValueError(f"{path}: not a GGUF file")
-        r = _Reader(self._mm, path)
-        r.pos = 4
-        self.version = r.scalar("<I")
+        f = _Fields(self._mm, path)
+        f.at = 4
+        self.version = f.u32()
         if self.version not in (2, 3):
             raise ValueError(f"{path}: GGUF version {self.version} (2 and 3 are supported)")
-        n_tensors, n_kv = r.scalar("<Q"), r.scalar("<Q")
+        n_tensors, n_values = f.u64(), f.u64()
         self.metadata: dict[str, object] = {}
-        for _ in range(n_kv):
-            key = r.string()
-            self.metadata[key] = r.value(r.scalar("<I"))
+        for _ in range(n_values):
+            key = f.text()
+            self.metadata[key] = _value_reader(f.u32(), path)(f)
         infos = []
         for _ in range(n_tensors):
-            name = r.string()
-            dims = [r.scalar("<Q") for _ in range(r.scalar("<I"))]
-            infos.append((name, dims, r.scalar("<I"), r.scalar("<Q")))
+            name = f.text()
+            dims = [f.u64() for _ in range(f.u32())]
+            infos.append(_Info(name, dims, f.u32(), f.u64()))
         align = int(self.metadata.get("general.alignment", 32))
-        self.data_start = (r.pos + align - 1) // align * align
-        self.tensors: dict[str, GGUFTensor] = {}
-        for name, dims, ttype, offset in infos:
-            if ttype not in BLOCK:
-                raise ValueError(f"{path}: tensor {name} has ggml type {ttype} (not F32/F16/BF16/Q8_0/Q4_0)")
-            bsize, bvals = BLOCK[ttype]
-            k = dims[0]
-            rows = int(np.prod(dims[1:], dtype=np.int64)) if len(dims) > 1 else 1
-            if k % bvals:
-                raise ValueError(f"{path}: tensor {name}: row length {k} not a multiple of {bvals}")
-            nbytes = rows * (k // bvals) * bsize
-            start = self.data_start + offset
-            if start + nbytes > self._mm.shape[0]:
-                raise ValueError(f"{path}: tensor {name} runs past the end of the file")
-            raw = self._mm[start:start + nbytes]
-            shape = tuple(int(d) for d in reversed(dims))
-            if ttype in _HOST_DTYPE:
-                data = raw.view(_HOST_DTYPE[ttype]).reshape(shape)
-            else:
-                data = raw.reshape(rows, (k // bvals) * bsize)
-            self.tensors[name] = GGUFTensor(name, ttype, shape, data, start, nbytes)
+        self.data_start = -(-f.at // align) * align
+        self.tensors: dict[str, GGUFTensor] = {
+            i.name: _tensor_view(path, self._mm, self.data_start, i) for i in infos}
 
     def to_device(self, names=None, device=None, chunk_bytes: int = 32 << 20) -> dict[str, GGUFTensor]:
         """Copy tensors (all, or `names`) into one allocation on a CUDA device
