@@ -704,7 +704,7 @@ def gpu_bench(args, rank: int, world: int, local_rank: int) -> dict | None:
         extra["cpu_arms"] = cpu_arms(host, extra)
     us = kernel_ms / steps * 1e3
     rl = roofline(STEP_BYTES, us, peak)
-    rl.update({"traffic": committed_traffic("gemv_q4_0_cfg0_traffic.json"), "kernel": "gemv_q_fast2<Q4_0, M=1>",
+    rl.update({"traffic": committed_traffic("gemv_q4_0_cfg0_traffic.json"), "kernel": "gemv_q4_r4<x in shared memory>",
                "algorithmic_bytes_per_launch": STEP_BYTES,
                "peak_source": peak["source"] + " (MEASURED_PEAKS.json hbm_gbs, burst copy)"})
     out = {
