@@ -182,6 +182,33 @@ smk_status smk_block_sums(smk_ctx* ctx, smk_qformat fmt, int M, int N, int K, co
  * receive the mismatch counts, all zero on a correct build. Synchronous. */
 smk_status smk_check_x_arith(smk_ctx* ctx, unsigned long long* out /* [3] */);
 
+/* ---- the rest of a Llama decode step, around the GEMVs ----
+ * Replace the NumPy code of the reference's decoder (examples/llama/llama.py):
+ * rms_norm (:184-188) with the residual add before it (step, :414-439), RoPE
+ * (rope_cos_sin / apply_rope :131-178 and Llama._rope) with the KV-cache write,
+ * and Llama._attention (:398-412). Device pointers, asynchronous on `stream`,
+ * programmatic dependent launch when SMK_OPT_PDL is set. */
+
+/* For each of M rows: x += delta (delta may be NULL; x is updated in place), then
+ * h = w * (x * f32(1 / sqrt(f32(sum(x^2) / n) + eps))), n <= 8192. */
+smk_status smk_add_rmsnorm(smk_ctx* ctx, int M, int n, float* x, int64_t ldx, const float* delta, int64_t ldd,
+                           const float* w, double eps, float* h, int64_t ldh, void* stream);
+/* One token's qkv = [q (nh heads) | k (nkv) | v (nkv)] of head_dim hd: q and k
+ * rotated by the angles f32(pos) * inv_freq[i] (pairs (i, i + hd/2), or (2i, 2i+1)
+ * when interleaved), q to q_out [nh][hd], k and v to row pos of k_cache / v_cache
+ * [nkv][capacity][hd]. pos is *pos_dev when pos_dev is not NULL (a graph replayed
+ * for each token; outside the cache: nothing written, smk_device_error set). */
+smk_status smk_rope_kv(smk_ctx* ctx, const float* qkv, const float* inv_freq, const int32_t* pos_dev, int pos, int nh,
+                       int nkv, int hd, int interleaved, float* q_out, float* k_cache, float* v_cache, int capacity,
+                       void* stream);
+/* Grouped-query attention of one token: query head h uses KV head h / (nh/nkv);
+ * out[h] = softmax(scale * q[h] . K[0..len)) . V[0..len), len = *len_dev when
+ * len_dev is not NULL, else len; max_len >= every len (it sizes the grid).
+ * nh/nkv <= 8, hd a multiple of 32 up to 128. */
+smk_status smk_attention_decode(smk_ctx* ctx, const float* q, const float* k_cache, const float* v_cache, float* out,
+                                const int32_t* len_dev, int len, int max_len, int nh, int nkv, int hd, int capacity,
+                                float scale, void* stream);
+
 /* ---- quantized decode GEMV without any allocation -------------------------
  * No counterpart in the reference. For callers that cannot call cudaMalloc:
  * hosts whose memory pools own every device allocation, servers that plan all

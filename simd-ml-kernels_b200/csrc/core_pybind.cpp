@@ -746,6 +746,28 @@ PYBIND11_MODULE(_core, m) {
                                   reinterpret_cast<const int32_t*>(rows), nrows, reinterpret_cast<float*>(out), ldo,
                                   reinterpret_cast<void*>(stream)));
     });
+    m.def("_add_rmsnorm", [](int M, int n, uintptr_t x, long long ldx, uintptr_t delta, long long ldd, uintptr_t w,
+                             double eps, uintptr_t h, long long ldh, uintptr_t stream, int device) {
+        check(smk_add_rmsnorm(ctx_for(device), M, n, reinterpret_cast<float*>(x), ldx,
+                              reinterpret_cast<const float*>(delta), ldd, reinterpret_cast<const float*>(w), eps,
+                              reinterpret_cast<float*>(h), ldh, reinterpret_cast<void*>(stream)));
+    });
+    m.def("_rope_kv", [](uintptr_t qkv, uintptr_t inv_freq, uintptr_t pos_dev, int pos, int nh, int nkv, int hd,
+                         int interleaved, uintptr_t q_out, uintptr_t kc, uintptr_t vc, int cap, uintptr_t stream,
+                         int device) {
+        check(smk_rope_kv(ctx_for(device), reinterpret_cast<const float*>(qkv), reinterpret_cast<const float*>(inv_freq),
+                          reinterpret_cast<const int32_t*>(pos_dev), pos, nh, nkv, hd, interleaved,
+                          reinterpret_cast<float*>(q_out), reinterpret_cast<float*>(kc), reinterpret_cast<float*>(vc),
+                          cap, reinterpret_cast<void*>(stream)));
+    });
+    m.def("_attention_decode", [](uintptr_t q, uintptr_t kc, uintptr_t vc, uintptr_t out, uintptr_t len_dev, int len,
+                                  int max_len, int nh, int nkv, int hd, int cap, float scale, uintptr_t stream,
+                                  int device) {
+        check(smk_attention_decode(ctx_for(device), reinterpret_cast<const float*>(q),
+                                   reinterpret_cast<const float*>(kc), reinterpret_cast<const float*>(vc),
+                                   reinterpret_cast<float*>(out), reinterpret_cast<const int32_t*>(len_dev), len,
+                                   max_len, nh, nkv, hd, cap, scale, reinterpret_cast<void*>(stream)));
+    });
     m.def("version", []() { return std::string(smk_version()); });
     m.def("_set_device", [](int d) { current_device_hint = d; });
     m.def("_ctx_set", [](int option, long long value) { check(smk_ctx_set(ctx_for(current_device_hint), option, value)); });

@@ -7,6 +7,7 @@
 #include "dequant.cuh"
 #include "gemv_dense.cuh"
 #include "gemv_int8.cuh"
+#include "decode.cuh"
 #include "gemv_quant.cuh"
 
 #include <algorithm>
@@ -170,6 +171,7 @@ struct smk_ctx {
     std::mutex mu_scratch;                    // guards scratch and test_buf
     std::map<cudaStream_t, DevBuf> scratch;   // per-stream quantized-x scratch
     DevBuf test_buf;                          // test hooks
+    std::map<cudaStream_t, DevBuf> attn_ws;   // per-stream attention partials and tickets
     std::mutex mu_stage;                      // held for a whole *_host call
     DevBuf staging;                           // *_host operands copied to the device (weights)
     PinnedBuf pinned;                         // *_host activations and outputs in pageable memory
@@ -406,6 +408,7 @@ smk_status smk_ctx_destroy(smk_ctx* c) {
     DeviceGuard g(c->device);
     cudaDeviceSynchronize();
     for (auto& kv : c->scratch) kv.second.release();
+    for (auto& kv : c->attn_ws) kv.second.release();
     c->staging.release();
     c->pinned.release();
     c->test_buf.release();
@@ -640,6 +643,83 @@ smk_status smk_silu_mul(smk_ctx* c, int64_t n, const float* gate, const float* u
     DeviceGuard g(c->device);
     if (!g.ok) return fail(SMK_ERR_CUDA, "cudaSetDevice(%d) failed", c->device);
     SMK_CUDA(smk::launch_silu_mul(static_cast<cudaStream_t>(stream), n, gate, up, out), "silu_mul launch");
+    return SMK_OK;
+}
+
+smk_status smk_add_rmsnorm(smk_ctx* c, int M, int n, float* x, int64_t ldx, const float* delta, int64_t ldd,
+                           const float* w, double eps, float* h, int64_t ldh, void* stream) {
+    if (!c) return fail(SMK_ERR_ARGUMENT, "ctx must not be NULL");
+    if (M < 0 || n < 0) return fail(SMK_ERR_ARGUMENT, "M and n must be >= 0");
+    if (n > smk::add_rmsnorm_max_n())
+        return fail(SMK_ERR_ARGUMENT, "rows of at most %d values (got %d)", smk::add_rmsnorm_max_n(), n);
+    if (M == 0 || n == 0) return SMK_OK;
+    if (!x || !w || !h) return fail(SMK_ERR_ARGUMENT, "x, w and h must not be NULL");
+    if (ldx < n || ldh < n || (delta && ldd < n)) return fail(SMK_ERR_ARGUMENT, "row strides must be >= n");
+    if (!(eps >= 0.0)) return fail(SMK_ERR_ARGUMENT, "eps must be >= 0");
+    DeviceGuard g(c->device);
+    if (!g.ok) return fail(SMK_ERR_CUDA, "cudaSetDevice(%d) failed", c->device);
+    SMK_CUDA(smk::launch_add_rmsnorm(static_cast<cudaStream_t>(stream), c->pdl, M, n, x, ldx, delta, ldd, w, eps, h,
+                                     ldh),
+             "add_rmsnorm launch");
+    return SMK_OK;
+}
+
+smk_status smk_rope_kv(smk_ctx* c, const float* qkv, const float* inv_freq, const int32_t* pos_dev, int pos, int nh,
+                       int nkv, int hd, int interleaved, float* q_out, float* k_cache, float* v_cache, int capacity,
+                       void* stream) {
+    if (!c) return fail(SMK_ERR_ARGUMENT, "ctx must not be NULL");
+    if (nh <= 0 || nkv <= 0 || nh % nkv != 0) return fail(SMK_ERR_ARGUMENT, "heads must be positive, nh a multiple of nkv");
+    if (hd <= 0 || hd % 2 != 0) return fail(SMK_ERR_ARGUMENT, "head_dim must be positive and even");
+    if (capacity <= 0) return fail(SMK_ERR_ARGUMENT, "capacity must be positive");
+    if (!pos_dev && (pos < 0 || pos >= capacity))
+        return fail(SMK_ERR_ARGUMENT, "position %d outside the cache (capacity %d)", pos, capacity);
+    if (!qkv || !inv_freq || !q_out || !k_cache || !v_cache) return fail(SMK_ERR_ARGUMENT, "pointers must not be NULL");
+    DeviceGuard g(c->device);
+    if (!g.ok) return fail(SMK_ERR_CUDA, "cudaSetDevice(%d) failed", c->device);
+    SMK_CUDA(smk::launch_rope_kv(static_cast<cudaStream_t>(stream), c->pdl, qkv, inv_freq, pos_dev, pos, nh, nkv, hd,
+                                 interleaved != 0, q_out, k_cache, v_cache, capacity, c->d_err),
+             "rope_kv launch");
+    return SMK_OK;
+}
+
+smk_status smk_attention_decode(smk_ctx* c, const float* q, const float* k_cache, const float* v_cache, float* out,
+                                const int32_t* len_dev, int len, int max_len, int nh, int nkv, int hd, int capacity,
+                                float scale, void* stream) {
+    if (!c) return fail(SMK_ERR_ARGUMENT, "ctx must not be NULL");
+    if (nh <= 0 || nkv <= 0 || nh % nkv != 0) return fail(SMK_ERR_ARGUMENT, "heads must be positive, nh a multiple of nkv");
+    if (nh / nkv > smk::attention_max_rep())
+        return fail(SMK_ERR_ARGUMENT, "at most %d query heads per KV head (got %d)", smk::attention_max_rep(), nh / nkv);
+    if (hd <= 0 || hd % 32 != 0 || hd > smk::attention_max_hd())
+        return fail(SMK_ERR_ARGUMENT, "head_dim must be a multiple of 32 up to %d (got %d)", smk::attention_max_hd(), hd);
+    if (capacity <= 0 || max_len <= 0 || max_len > capacity)
+        return fail(SMK_ERR_ARGUMENT, "need 0 < max_len <= capacity");
+    if (!len_dev && (len < 1 || len > max_len)) return fail(SMK_ERR_ARGUMENT, "len must be in 1..max_len (got %d)", len);
+    if (!q || !k_cache || !v_cache || !out) return fail(SMK_ERR_ARGUMENT, "pointers must not be NULL");
+    DeviceGuard g(c->device);
+    if (!g.ok) return fail(SMK_ERR_CUDA, "cudaSetDevice(%d) failed", c->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int chunks = smk::attention_chunks(max_len);
+    float* ws = nullptr;
+    unsigned* tickets = nullptr;
+    if (chunks > 1) {
+        // Tickets (one per KV head) at a fixed place at the start of the buffer,
+        // zeroed when the buffer is allocated and reset by every call that used
+        // them; the partials after them, sized by the call.
+        constexpr int kMaxTicketHeads = 256;
+        if (nkv > kMaxTicketHeads) return fail(SMK_ERR_ARGUMENT, "at most %d KV heads", kMaxTicketHeads);
+        const size_t tb = kMaxTicketHeads * sizeof(unsigned);
+        const size_t need = tb + (size_t)nkv * chunks * (nh / nkv) * (hd + 2) * sizeof(float);
+        std::lock_guard<std::mutex> lock(c->mu_scratch);
+        DevBuf& b = c->attn_ws[s];
+        const bool grow = need > b.bytes;
+        SMK_CUDA(b.reserve(need), "cudaMalloc (attention workspace)");
+        tickets = static_cast<unsigned*>(b.ptr);
+        ws = reinterpret_cast<float*>(static_cast<uint8_t*>(b.ptr) + tb);
+        if (grow) SMK_CUDA(cudaMemsetAsync(b.ptr, 0, tb, s), "cudaMemsetAsync");
+    }
+    SMK_CUDA(smk::launch_attention(s, c->pdl, q, k_cache, v_cache, out, len_dev, len, max_len, nh, nkv, hd, capacity,
+                                   scale, ws, tickets, c->d_err),
+             "attention launch");
     return SMK_OK;
 }
 
