@@ -885,10 +885,58 @@ def llama_stack(torch, sk, dev, stream, args, jobs, peak, host) -> dict:
                      "gb_s": round(tok_bytes / (per_tok_ms * 1e-3) / 1e9, 1),
                      "roofline": roofline(tok_bytes, per_tok_ms * 1e3, peak),
                      "launches_per_token": len(groups) + (LLAMA_LAYERS if swiglu == "unfused" else 0)}
+    res["decode_full"] = llama_full_decode(torch, sk, dev, stream, weights, tokens, peak, wbytes)
     res.update({"gemvs_per_token": len(LLAMA_MATRICES), "bytes_per_token": tok_bytes, "tokens": tokens,
                 "weights": "per matrix i numpy default_rng((2, i)), N(0, 0.02) -> Q4_0 on device",
                 "launch": f"one CUDA graph of {tokens} decode steps, PDL; q/k/v and gate/up as fused row groups"})
     return res
+
+
+def llama_full_decode(torch, sk, dev, stream, weights, tokens: int, peak, wbytes: int) -> dict:
+    """Whole decode tokens of config 2's architecture on the GPU (LlamaDecoder):
+    embedding row, per layer RMSNorm, q/k/v GEMV, RoPE (Llama-3 scaling) and
+    KV-cache write, GQA attention over the positions so far, o GEMV, residual
+    RMSNorm, gate/up GEMV, down GEMV on silu(gate)*up; final norm and the tied
+    LM head. The config-2 Q4_0 weights; norm weights 1 + N(0, 0.1^2) from seed 2;
+    `tokens` tokens from position 0 in one CUDA graph."""
+    from simd_ml_kernels import decode as D
+    shape = D.LlamaShape(hidden=2048, layers=LLAMA_LAYERS, heads=32, kv_heads=8, head_dim=64, ffn=8192,
+                         vocab=LLAMA_VOCAB, eps=1e-5)
+    rng = np.random.default_rng([2, 2000])
+    norm = lambda: torch.from_numpy((1 + 0.1 * rng.standard_normal(2048)).astype(np.float32)).to(dev)  # noqa: E731
+    layers = [D.LlamaLayerWeights(attn_norm=norm(), qkv=weights[4 * i], o=weights[4 * i + 1], mlp_norm=norm(),
+                                  gate_up=weights[4 * i + 2], down=weights[4 * i + 3]) for i in range(LLAMA_LAYERS)]
+    w = D.LlamaWeights(layers=layers, norm=norm(), embed=weights[-1], lm_head=weights[-1], fmt="q4_0")
+    inv = D.rope_inv_freq(64, 500000.0, {"factor": 32.0, "high_freq_factor": 4.0, "low_freq_factor": 1.0,
+                                         "original_max_position_embeddings": 8192, "rope_type": "llama3"})
+    cap = max(256, tokens)
+    dec = D.LlamaDecoder(shape, w, inv, capacity=cap)
+    toks = [(7919 * t + 13) % LLAMA_VOCAB for t in range(tokens)]
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        dec.step(toks[0])   # first-use set-up outside the capture
+        dec.reset()
+        with torch.cuda.graph(gr, stream=stream):
+            for t in toks:
+                dec.step(t)
+        for _ in range(2):
+            dec.reset()
+            gr.replay()
+        dec.reset()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        gr.replay()
+        e.record(stream)
+    torch.cuda.synchronize(dev)
+    per_tok_ms = s.elapsed_time(e) / tokens
+    del gr
+    # Bytes a token reads: the weights once, the KV cache rows so far (average position), x/y of the GEMVs.
+    kv = 2 * LLAMA_LAYERS * 8 * 64 * 4 * (tokens + 1) / 2
+    nbytes = wbytes + kv
+    return {"tok_s": round(1e3 / per_tok_ms, 1), "ms_per_token": per_tok_ms,
+            "roofline": roofline(nbytes, per_tok_ms * 1e3, peak), "bytes_per_token": int(nbytes),
+            "launches_per_token": dec.launches_per_token(), "tokens": tokens,
+            "launch": f"one CUDA graph of {tokens} whole decode steps from position 0, PDL"}
 
 
 def e2e_headline(torch, sk, shard, dev, local_rank, world, ws, copies, sg, x_np) -> dict:
