@@ -622,6 +622,21 @@ def gpu_bench(args, rank: int, world: int, local_rank: int) -> dict | None:
         for i in range(args.warmup):
             one_step(i)
     torch.cuda.synchronize(dev)
+    signal = None
+    if nvlink:   # the fused gather's fixed cost: NVLink flag round trips, and data-free gather steps
+        iters = 20000
+        ns = _core._gather_pingpong(sg._g, iters, 0, stream.cuda_stream)
+        ns_relaxed = _core._gather_pingpong(sg._g, iters, 1, stream.cuda_stream)
+        bar_ms = chained_ms(torch, dev, stream, lambda i: _core._gather_barrier(sg._g, stream.cuda_stream), 2000, 1,
+                            chunk=500, barrier=barrier)
+        t = torch.tensor([bar_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        signal = {"pingpong_round_trip_us": round(ns / (iters - iters // 8) / 1e3, 3) if rank == 0 else None,
+                  "pingpong_relaxed_round_trip_us": round(ns_relaxed / (iters - iters // 8) / 1e3, 3)
+                  if rank == 0 else None,
+                  "gather_barrier_step_us": round(float(t.item()) * 1e3 / 2000, 3),
+                  "note": "round trip of a flag between ranks 0 and 1 inside one kernel each; a chain of data-free "
+                          "gather steps (signal every peer, wait for every peer), one launch per step"}
     clocks = ClockSampler(local_rank)
     steps = args.steps
     ms = chained_ms(torch, dev, stream, one_step, steps, copies, barrier=barrier if world > 1 else None,
@@ -728,6 +743,8 @@ def gpu_bench(args, rank: int, world: int, local_rank: int) -> dict | None:
 
     if world > 1:
         out["kernel_only_ms_per_step"] = kernel_ms / steps
+        if signal is not None:
+            out["nvlink_signal"] = signal
     out.update(extra)
     if world == 1:
         cb = extra["cpu_arms"].get("config0")
@@ -1107,6 +1124,7 @@ def main() -> None:
     from datetime import timedelta
 
     if world > 1:
+        os.environ.setdefault("NCCL_DEBUG", "WARN")   # stdout carries only the JSON line
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local_rank))
     try:

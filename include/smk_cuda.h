@@ -82,8 +82,15 @@ smk_status smk_ctx_destroy(smk_ctx* ctx);
  *                   per SM.
  *   SMK_OPT_TILE_ORDER  how that kernel's row tiles are spread over its CTAs:
  *                   1 interleaved, 2 or 0 (default) a contiguous range per
- *                   CTA. */
-enum { SMK_OPT_PDL = 1, SMK_OPT_WARPS = 2, SMK_OPT_STAGES = 3, SMK_OPT_CTAS_PER_SM = 4, SMK_OPT_TILE_ORDER = 5 };
+ *                   CTA.
+ *   SMK_OPT_HOST_GRAPHS  1 (default): a smk_gemv_q_host call with device
+ *                   weights that repeats the shape and operand addresses of
+ *                   one of the last 64 keys replays a CUDA graph of its copy
+ *                   and kernel (captured on its second occurrence); 0: every
+ *                   call launches directly. Setting any option drops the
+ *                   captured graphs. */
+enum { SMK_OPT_PDL = 1, SMK_OPT_WARPS = 2, SMK_OPT_STAGES = 3, SMK_OPT_CTAS_PER_SM = 4, SMK_OPT_TILE_ORDER = 5,
+       SMK_OPT_HOST_GRAPHS = 6 };
 smk_status smk_ctx_set(smk_ctx* ctx, int option, long long value);
 smk_status smk_ctx_get(smk_ctx* ctx, int option, long long* value);
 /* The CUDA device that owns `ptr` (device or managed memory), or -1 for host memory. */
@@ -208,6 +215,13 @@ smk_status smk_rope_kv(smk_ctx* ctx, const float* qkv, const float* inv_freq, co
 smk_status smk_attention_decode(smk_ctx* ctx, const float* q, const float* k_cache, const float* v_cache, float* out,
                                 const int32_t* len_dev, int len, int max_len, int nh, int nkv, int hd, int capacity,
                                 float scale, void* stream);
+/* smk_rope_kv and smk_attention_decode as one kernel (the decode step's form):
+ * this token's qkv (not rotated) at position pos (*pos_dev when pos_dev is not
+ * NULL), k and v written to row pos of the caches, attention over positions
+ * 0 .. pos, pos < max_len <= capacity. The same outputs as the two calls. */
+smk_status smk_rope_attention(smk_ctx* ctx, const float* qkv, const float* inv_freq, const int32_t* pos_dev, int pos,
+                              int max_len, int nh, int nkv, int hd, int interleaved, float* k_cache, float* v_cache,
+                              int capacity, float scale, float* out, void* stream);
 
 /* ---- quantized decode GEMV without any allocation -------------------------
  * No counterpart in the reference. For callers that cannot call cudaMalloc:
@@ -242,19 +256,21 @@ smk_status smk_noalloc_device_error(unsigned* code, void* stream);
  * Replaces the row slicing of gemv_slice (src/dispatch/dispatch.cpp:373-379)
  * across GPUs, plus an all-gather of the y slices; an addition with no
  * reference counterpart beyond that slicing. Each rank creates one gather
- * object (a device buffer holding two full-y areas [m_max][world * npad] and
- * a control block), passes its 64-byte IPC handle to every peer (any host
+ * object (a device buffer holding two full-y areas [m_max][world * npad],
+ * two receive areas of the same entries as 64-bit words, a staging slice and a
+ * control block), passes its 64-byte IPC handle to every peer (any host
  * channel: torch.distributed, MPI, ...), and connects with all ranks'
  * handles in rank order. Every rank then makes the same sequence of
  * smk_gemv_q_gather calls on the same shapes: each computes this rank's
- * npad-row slice (N_local <= npad valid rows), stores it into every rank's
- * area over NVLink, and, on the same stream, waits (bounded, about 1 s;
- * smk_device_error reports a timeout) until every peer's slice of the step
- * has arrived. *y_full receives this step's area: [M][world * npad] floats,
- * rank r's rows at r * npad. It stays valid until this rank's next
+ * npad-row slice (N_local <= npad valid rows; the padding rows read 0) and
+ * stores it over NVLink into every peer's receive area, each value with the
+ * step's tag in one 64-bit store; on the same stream a wait kernel polls the
+ * tags (bounded, about 1 s; smk_device_error reports a timeout) and copies the
+ * peers' slices into this rank's full-y area. *y_full receives this step's
+ * area: [M][world * npad] floats, rank r's rows at r * npad. Only this rank
+ * writes it, on `stream`; it stays valid until this rank's next
  * smk_gemv_q_gather call: queue every kernel that reads it on `stream` (or
- * copy it) before making that call. The two areas alternate, and a peer
- * writes this one again as soon as this rank's next call has signalled it. */
+ * copy it) before making that call. The two areas alternate between steps. */
 typedef struct smk_gather smk_gather;
 #define SMK_IPC_HANDLE_BYTES 64
 smk_status smk_gather_create(smk_ctx* ctx, int world, int rank, int npad, int m_max, smk_gather** out,
@@ -263,6 +279,18 @@ smk_status smk_gather_connect(smk_gather* g, const void* ipc_handles /* world * 
 smk_status smk_gather_destroy(smk_gather* g);
 smk_status smk_gemv_q_gather(smk_ctx* ctx, smk_gather* g, smk_qformat fmt, int M, int N_local, int K, const float* x,
                              int64_t ldx, const uint8_t* Wq, float** y_full, void* stream);
+/* A gather step that carries no data (no reference counterpart): signals every
+ * peer and waits (bounded) for their signals, on the device; every rank makes
+ * the same calls. A cross-GPU barrier in stream order, and with
+ * smk_gather_pingpong the measure of the gather's fixed cost. */
+smk_status smk_gather_barrier(smk_gather* g, void* stream);
+/* Diagnostic (no reference counterpart): ranks 0 and 1 bounce a flag over
+ * NVLink `iters` times inside one kernel each; rank 0 gets in *ns the
+ * nanoseconds of the last iters - iters/8 round trips (the first ones absorb
+ * the launches' skew; other ranks get 0). Both ranks call it together;
+ * synchronous. relaxed: plain system-scope stores and loads instead of
+ * release / acquire ones. */
+smk_status smk_gather_pingpong(smk_gather* g, int iters, int relaxed, unsigned long long* ns, void* stream);
 
 #ifdef __cplusplus
 }

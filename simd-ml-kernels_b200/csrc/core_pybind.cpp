@@ -709,6 +709,17 @@ PYBIND11_MODULE(_core, m) {
         check(smk_gather_connect(reinterpret_cast<smk_gather*>(g), hs.data()));
     });
     m.def("_gather_destroy", [](uintptr_t g) { check(smk_gather_destroy(reinterpret_cast<smk_gather*>(g))); });
+    m.def("_gather_barrier", [](uintptr_t g, uintptr_t stream) {
+        check(smk_gather_barrier(reinterpret_cast<smk_gather*>(g), reinterpret_cast<void*>(stream)));
+    });
+    m.def("_gather_pingpong", [](uintptr_t g, int iters, int relaxed, uintptr_t stream) {
+        unsigned long long ns = 0;
+        {
+            py::gil_scoped_release nogil;
+            check(smk_gather_pingpong(reinterpret_cast<smk_gather*>(g), iters, relaxed, &ns, reinterpret_cast<void*>(stream)));
+        }
+        return ns;
+    });
     m.def("_gemv_q_gather", [](uintptr_t g, int fmt, int M, int N, int K, uintptr_t x, long long ldx, uintptr_t w,
                                uintptr_t stream, int device) {
         smk_ctx* c = ctx_for(device);
@@ -767,6 +778,15 @@ PYBIND11_MODULE(_core, m) {
                                    reinterpret_cast<const float*>(kc), reinterpret_cast<const float*>(vc),
                                    reinterpret_cast<float*>(out), reinterpret_cast<const int32_t*>(len_dev), len,
                                    max_len, nh, nkv, hd, cap, scale, reinterpret_cast<void*>(stream)));
+    });
+    m.def("_rope_attention", [](uintptr_t qkv, uintptr_t inv_freq, uintptr_t pos_dev, int pos, int max_len, int nh,
+                                int nkv, int hd, int interleaved, uintptr_t kc, uintptr_t vc, int cap, float scale,
+                                uintptr_t out, uintptr_t stream, int device) {
+        check(smk_rope_attention(ctx_for(device), reinterpret_cast<const float*>(qkv),
+                                 reinterpret_cast<const float*>(inv_freq), reinterpret_cast<const int32_t*>(pos_dev),
+                                 pos, max_len, nh, nkv, hd, interleaved, reinterpret_cast<float*>(kc),
+                                 reinterpret_cast<float*>(vc), cap, scale, reinterpret_cast<float*>(out),
+                                 reinterpret_cast<void*>(stream)));
     });
     m.def("version", []() { return std::string(smk_version()); });
     m.def("_set_device", [](int d) { current_device_hint = d; });

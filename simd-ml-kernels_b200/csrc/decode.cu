@@ -92,6 +92,18 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(float* __rest
 // the layer's caches [nkv][cap][hd]. pos comes from *pos_dev when given (a
 // graph replayed for every token), else from pos; pos outside [0, cap) writes
 // nothing and sets kErrBadLaunch.
+// Pair i of one head of hd values at position pos: (a, b) = (src[ia], src[ib])
+// rotated by the angle fl(pos·inv_freq[i]) into dst[ia], dst[ib].
+__device__ __forceinline__ void rope_pair(const float* src, float* dst, const float* inv_freq, int pos, int i, int hd,
+                                          int interleaved) {
+    const float ang = __fmul_rn((float)pos, inv_freq[i]);
+    const float c = cosf(ang), s = sinf(ang);
+    const int ia = interleaved ? 2 * i : i, ib = interleaved ? 2 * i + 1 : i + hd / 2;
+    const float a = src[ia], b = src[ib];
+    dst[ia] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));   // a·cos − b·sin
+    dst[ib] = __fadd_rn(__fmul_rn(b, c), __fmul_rn(a, s));   // b·cos + a·sin
+}
+
 __global__ void __launch_bounds__(512) rope_kv_kernel(const float* __restrict__ qkv, const float* __restrict__ inv_freq,
                                                       const int* __restrict__ pos_dev, int pos_imm, int nh, int nkv,
                                                       int hd, int interleaved, float* __restrict__ qout,
@@ -108,17 +120,9 @@ __global__ void __launch_bounds__(512) rope_kv_kernel(const float* __restrict__ 
     const int pairs = (nh + nkv) * half;
     for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < pairs; t += gridDim.x * blockDim.x) {
         const int head = t / half, i = t - head * half;
-        const float ang = __fmul_rn((float)pos, inv_freq[i]);
-        const float c = cosf(ang), s = sinf(ang);
-        const float* src = qkv + (size_t)head * hd;   // q heads, then k heads
-        const int ia = interleaved ? 2 * i : i, ib = interleaved ? 2 * i + 1 : i + half;
-        const float a = src[ia], b = src[ib];
-        const float ra = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));   // a·cos − b·sin
-        const float rb = __fadd_rn(__fmul_rn(b, c), __fmul_rn(a, s));   // b·cos + a·sin
         float* dst = head < nh ? qout + (size_t)head * hd
                                : kc + ((size_t)(head - nh) * cap + pos) * hd;
-        dst[ia] = ra;
-        dst[ib] = rb;
+        rope_pair(qkv + (size_t)head * hd, dst, inv_freq, pos, i, hd, interleaved);   // q heads, then k heads
     }
     const float* vsrc = qkv + (size_t)(nh + nkv) * hd;
     for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < nkv * hd; t += gridDim.x * blockDim.x) {
@@ -148,8 +152,8 @@ constexpr int kAttnMaxHd = 128;
 
 struct AttnArgs {
     const float* q;        // [nh][hd] (rotated)
-    const float* kc;       // [nkv][cap][hd] (this layer)
-    const float* vc;
+    float* kc;             // [nkv][cap][hd] (this layer)
+    float* vc;
     float* out;            // [nh][hd]
     const int* len_dev;    // positions attended: *len_dev (device), else len
     int len, nh, nkv, hd, cap;
@@ -157,8 +161,21 @@ struct AttnArgs {
     float* ws;             // [nkv][chunks][rep][hd + 2] partials (chunks > 1)
     unsigned* tickets;     // [nkv], zero between calls
     unsigned* err;
+    // RoPE fused in (attention_kernel<true>): q is this token's qkv
+    // [q (nh) | k (nkv) | v (nkv)] before rotation, the position is *pos_dev
+    // (or pos), and the length pos + 1.
+    const float* inv_freq;
+    const int* pos_dev;
+    int pos, interleaved;
 };
 
+// kRope: RoPE and the KV-cache write fused in. Every CTA rotates the q heads of
+// its KV head into shared memory itself; the CTA whose chunk holds the token's
+// position rotates the token's k and writes k and v to that row of the caches
+// before it reads them (no other CTA reads that row in this call). The
+// rotations are rope_kv_kernel's, so the outputs equal rope_kv followed by
+// attention bit for bit.
+template <bool kRope>
 __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnArgs a) {
     __shared__ __align__(16) float qs[kAttnMaxRep * kAttnMaxHd];
     __shared__ float ps[kAttnMaxRep * kAttnChunk];                      // scores, then exp
@@ -169,15 +186,39 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnArgs 
     pdl_wait_primary();
     const int g = blockIdx.x, chunk = blockIdx.y, nchunks = gridDim.y;
     const int rep = a.nh / a.nkv, hd = a.hd;
-    int L = a.len_dev ? *a.len_dev : a.len;
-    if (L > a.cap) {   // only a device-side length can get here (the host checks its own)
-        if (threadIdx.x == 0 && a.err) atomicOr(a.err, kErrBadLaunch);
-        L = a.cap;
+    int L;
+    if constexpr (kRope) {
+        const int pos = a.pos_dev ? *a.pos_dev : a.pos;
+        if (pos < 0 || pos >= a.cap) {   // only a device-side position can get here
+            if (threadIdx.x == 0 && chunk == 0 && a.err) atomicOr(a.err, kErrBadLaunch);
+            return;   // every CTA of the launch returns alike: no ticket is taken
+        }
+        L = pos + 1;
+        const int half = hd / 2;
+        for (int t = threadIdx.x; t < rep * half; t += kAttnThreads) {
+            const int h = t / half, i = t - h * half;
+            rope_pair(a.q + (size_t)(g * rep + h) * hd, qs + h * hd, a.inv_freq, pos, i, hd, a.interleaved);
+        }
+        if (pos / kAttnChunk == chunk) {
+            const float* ksrc = a.q + (size_t)(a.nh + g) * hd;
+            float* krow = a.kc + ((size_t)g * a.cap + pos) * hd;
+            for (int i = threadIdx.x; i < half; i += kAttnThreads)
+                rope_pair(ksrc, krow, a.inv_freq, pos, i, hd, a.interleaved);
+            const float* vsrc = a.q + (size_t)(a.nh + a.nkv + g) * hd;
+            float* vrow = a.vc + ((size_t)g * a.cap + pos) * hd;
+            for (int d = threadIdx.x; d < hd; d += kAttnThreads) vrow[d] = vsrc[d];
+        }
+    } else {
+        L = a.len_dev ? *a.len_dev : a.len;
+        if (L > a.cap) {   // only a device-side length can get here (the host checks its own)
+            if (threadIdx.x == 0 && a.err) atomicOr(a.err, kErrBadLaunch);
+            L = a.cap;
+        }
+        for (int t = threadIdx.x; t < rep * hd; t += kAttnThreads) qs[t] = a.q[(size_t)g * rep * hd + t];
     }
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = kAttnThreads / 32;
     const int p0 = chunk * kAttnChunk, p1 = min(L, p0 + kAttnChunk), np = max(0, p1 - p0);
-    for (int t = threadIdx.x; t < rep * hd; t += kAttnThreads) qs[t] = a.q[(size_t)g * rep * hd + t];
-    __syncthreads();
+    __syncthreads();   // q in shared memory; the token's k and v rows written (kRope)
     const float* K = a.kc + (size_t)g * a.cap * hd;
     const float* V = a.vc + (size_t)g * a.cap * hd;
     // Scores: position p0 + j at thread j (kAttnChunk <= threads · passes).
@@ -361,12 +402,24 @@ int attention_max_hd() { return kAttnMaxHd; }
 cudaError_t launch_attention(cudaStream_t s, bool pdl, const float* q, const float* kc, const float* vc, float* out,
                              const int* len_dev, int len, int max_len, int nh, int nkv, int hd, int cap, float scale,
                              float* ws, unsigned* tickets, unsigned* err) {
-    AttnArgs a;
-    a.q = q; a.kc = kc; a.vc = vc; a.out = out; a.len_dev = len_dev; a.len = len;
-    a.nh = nh; a.nkv = nkv; a.hd = hd; a.cap = cap; a.scale = scale;
+    AttnArgs a = {};
+    a.q = q; a.kc = const_cast<float*>(kc); a.vc = const_cast<float*>(vc); a.out = out; a.len_dev = len_dev;
+    a.len = len; a.nh = nh; a.nkv = nkv; a.hd = hd; a.cap = cap; a.scale = scale;
     a.ws = ws; a.tickets = tickets; a.err = err;
     const int chunks = attention_chunks(max_len);
-    return launch_pdl(attention_kernel, dim3(nkv, chunks), dim3(kAttnThreads), s, pdl, a);
+    return launch_pdl(attention_kernel<false>, dim3(nkv, chunks), dim3(kAttnThreads), s, pdl, a);
+}
+
+cudaError_t launch_rope_attention(cudaStream_t s, bool pdl, const float* qkv, const float* inv_freq, const int* pos_dev,
+                                  int pos, int max_len, int nh, int nkv, int hd, bool interleaved, float* kc, float* vc,
+                                  int cap, float scale, float* out, float* ws, unsigned* tickets, unsigned* err) {
+    AttnArgs a = {};
+    a.q = qkv; a.kc = kc; a.vc = vc; a.out = out; a.len_dev = nullptr; a.len = 0;
+    a.nh = nh; a.nkv = nkv; a.hd = hd; a.cap = cap; a.scale = scale;
+    a.ws = ws; a.tickets = tickets; a.err = err;
+    a.inv_freq = inv_freq; a.pos_dev = pos_dev; a.pos = pos; a.interleaved = interleaved ? 1 : 0;
+    const int chunks = attention_chunks(max_len);
+    return launch_pdl(attention_kernel<true>, dim3(nkv, chunks), dim3(kAttnThreads), s, pdl, a);
 }
 
 }  // namespace smk

@@ -25,5 +25,11 @@ int attention_max_hd();
 cudaError_t launch_attention(cudaStream_t s, bool pdl, const float* q, const float* kc, const float* vc, float* out,
                              const int* len_dev, int len, int max_len, int nh, int nkv, int hd, int cap, float scale,
                              float* ws, unsigned* tickets, unsigned* err);
+// The two above in one kernel: RoPE of this token's qkv at position pos (or
+// *pos_dev), k and v written to that row of the caches, attention over
+// positions 0 .. pos; max_len > pos bounds the chunks (ws and tickets as above).
+cudaError_t launch_rope_attention(cudaStream_t s, bool pdl, const float* qkv, const float* inv_freq, const int* pos_dev,
+                                  int pos, int max_len, int nh, int nkv, int hd, bool interleaved, float* kc, float* vc,
+                                  int cap, float scale, float* out, float* ws, unsigned* tickets, unsigned* err);
 
 }  // namespace smk

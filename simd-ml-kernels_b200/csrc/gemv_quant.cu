@@ -208,6 +208,26 @@ __global__ void __launch_bounds__(256) silu_mul_kernel(long long n, const float*
 // Test hook: the exact helpers of quantize_quad against CUDA's own operations over
 // their whole domains; bad[0] divisions (every finite a >= 0), bad[1] reciprocals
 // (every 2^-126 <= d <= 2^126), bad[2] roundings (every |t| <= 128) that differ.
+// A host-memory call's activations: n floats from page-locked host memory
+// mapped into the device's address space (src) to device memory (dst), 16
+// bytes per thread when both are aligned. A kernel rather than a copy-engine
+// transfer: the GEMV after it launches at once under programmatic dependent
+// launch and streams its weights while these loads cross the bus, and a CUDA
+// graph of the call holds kernels only.
+__global__ void __launch_bounds__(512) stage_x_kernel(const float* __restrict__ src, float* __restrict__ dst,
+                                                      long long n) {
+    pdl_launch_dependents();
+    pdl_wait_primary();
+    const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x, nt = (long long)gridDim.x * blockDim.x;
+    if (((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) == 0) {
+        for (long long i = t; i < n / 4; i += nt)
+            reinterpret_cast<float4*>(dst)[i] = reinterpret_cast<const float4*>(src)[i];
+        for (long long i = n / 4 * 4 + t; i < n; i += nt) dst[i] = src[i];
+    } else {
+        for (long long i = t; i < n; i += nt) dst[i] = src[i];
+    }
+}
+
 __global__ void __launch_bounds__(256) check_x_arith_kernel(unsigned long long* bad) {
     unsigned long long b0 = 0, b1 = 0, b2 = 0;
     const unsigned long long stride = (unsigned long long)gridDim.x * blockDim.x;
@@ -408,6 +428,71 @@ struct ItemCursor {
     }
 };
 
+// Fused all-gather, this rank's side of a step: the entry of its output row 0,
+// slice row 0 in area (epoch & 1), and the step's tag. Read after
+// griddepcontrol.wait: the previous step's wait kernel, which advances the
+// epoch, has completed by then.
+struct GatherStep {
+    long long off;
+    unsigned tag;
+};
+__device__ __forceinline__ GatherStep gather_step(const GatherArgs* ga) {
+    const unsigned epoch = *reinterpret_cast<volatile const unsigned*>(ga->ctrl[ga->rank]);
+    return {(long long)(epoch & 1u) * ga->area + (long long)ga->rank * ga->npad, epoch + 1u};
+}
+// The padding rows [n, npad) of this rank's slice, output rows 0 .. M-1: zeros
+// in this rank's area and, tagged, in every peer's (the peers wait for every
+// entry of the slice), by thread t of nt.
+__device__ __forceinline__ void gather_pad(const GatherArgs* ga, int M, int n, int t, int nt) {
+    const int pad = ga->npad - n;
+    if (pad <= 0) return;
+    const GatherStep gs = gather_step(ga);
+    const long long cols = (long long)ga->world * ga->npad;
+    const unsigned long long w = tagged_word(0.0f, gs.tag);
+    for (int i = t; i < M * pad; i += nt) {
+        const int m = i / pad, row = n + i % pad;
+        const long long o = gs.off + m * cols + row;
+        ga->y[o] = 0.0f;
+        for (int rk = 0; rk < ga->world; ++rk)
+            if (rk != ga->rank) st_relaxed_sys_u64(ga->ll[rk] + o, w);
+    }
+}
+
+// After a warp's last item. With a fused gather the kernel's y is this rank's
+// staging slice (p.y, output rows p.ldy apart): the loop stores exactly as
+// without a gather, and nothing of the gather stays live in its registers.
+// Here the values of the warp's finished tiles (TR rows each, M output rows)
+// go from there into this rank's full-y area and, as tagged words, into every
+// peer's receive area, one entry per lane. The tiles are the ones before
+// `end` (the warp's cursor after its loop) in steps of `step`, down to the
+// CTA's first tile (p.contiguous) or 0; ctaid is read anew so that nothing
+// from before the loop has to be kept. The receivers wait for the step's last
+// tile in any case, so sending after the loop costs them nothing.
+__device__ __forceinline__ void gather_send(const QGemvParams& p, int M, int TR, int end, int step, int lane) {
+    const GatherArgs* ga = p.gather;
+    __syncwarp();   // the lanes' stores to p.y are visible to the whole warp
+    unsigned bx, nbx;
+    asm volatile("mov.u32 %0, %%ctaid.x;" : "=r"(bx));
+    asm volatile("mov.u32 %0, %%nctaid.x;" : "=r"(nbx));
+    const int lo = p.contiguous ? (int)((long long)bx * p.ntiles / nbx) : 0;
+    const GatherStep gs = gather_step(ga);
+    const long long cols = (long long)ga->world * ga->npad;
+    const int per = M * TR;
+    for (int tile = end - step; tile >= lo; tile -= step) {
+        for (int e = lane; e < per; e += 32) {
+            const int m = e / TR, row = tile * TR + (e - m * TR);
+            if (row < p.N) {
+                const float v = p.y[(size_t)m * p.ldy + row];
+                const long long o = gs.off + m * cols + row;
+                ga->y[o] = v;
+                const unsigned long long w = tagged_word(v, gs.tag);
+                for (int rk = 0; rk < ga->world; ++rk)
+                    if (rk != ga->rank) st_relaxed_sys_u64(ga->ll[rk] + o, w);
+            }
+        }
+    }
+}
+
 template <int F, int M, bool kXGlobal, bool kDump>
 __device__ __forceinline__ void gemv_q_fast_body(const QGemvParams& p) {
     constexpr int SBB = sb_bytes(F);
@@ -420,7 +505,9 @@ __device__ __forceinline__ void gemv_q_fast_body(const QGemvParams& p) {
     if constexpr (!kXGlobal) off += (xq_total_bytes(M, p.ksteps) + 127) & ~(size_t)127;
     uint8_t* stages = smem + off + (size_t)warp * p.stages * 32 * SBB;
 
-    pdl_launch_dependents();
+    // A fused gather's wait kernel reads the epoch when it starts, so it may
+    // only launch once the previous one has completed: after griddepcontrol.wait.
+    if (!p.gather) pdl_launch_dependents();
 
     // Tiles of this warp: gw, gw + GW, ...; each tile is ksteps items. With
     // p.contiguous the CTA owns a contiguous, even share of the tiles (each SM
@@ -453,6 +540,7 @@ __device__ __forceinline__ void gemv_q_fast_body(const QGemvParams& p) {
     }
 
     pdl_wait_primary();
+    if (p.gather) pdl_launch_dependents();
     if constexpr (!kXGlobal) {
         const XGeom xg{M, p.nb, p.log2G, p.ksteps, 0};
         quantize_x_rows<M>(p.x, p.ldx, p.up, p.ldu, xg, xs, threadIdx.x, blockDim.x);
@@ -461,15 +549,9 @@ __device__ __forceinline__ void gemv_q_fast_body(const QGemvParams& p) {
     const uint8_t* xb = kXGlobal ? p.xq : xs;
 
     const int r = lane >> p.log2G, g = lane & (p.G - 1);
-    // Fused all-gather: this step's y goes into full-y area (epoch & 1) of
-    // every rank, at this rank's slice. The previous kernel (the gather wait)
-    // completed before griddepcontrol.wait returned, so the epoch is settled.
-    long long gather_off = 0;
-    if (p.gather) {
-        const GatherArgs* ga = p.gather;
-        const unsigned epoch = *reinterpret_cast<volatile const unsigned*>(ga->ctrl[ga->rank]);
-        gather_off = (long long)(epoch & 1u) * ga->area + (long long)ga->rank * ga->npad;
-    }
+    // Fused all-gather: this step's y goes into this rank's full-y area
+    // (epoch & 1) and, tagged, into every peer's receive area, at this rank's slice.
+    if (p.gather && blockIdx.x == 0) gather_pad(p.gather, M, p.N, threadIdx.x, blockDim.x);
     XPtr xp;
     xp.mstride_q = (size_t)p.ksteps * 8192;
     xp.mstride_d = (size_t)p.ksteps * 2048;
@@ -505,22 +587,7 @@ __device__ __forceinline__ void gemv_q_fast_body(const QGemvParams& p) {
             for (int m = 0; m < M; ++m) {
                 float v = acc[m];
                 for (int o = p.G >> 1; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-                if (p.gather) {   // this rank's slice in the local area and every peer's, over NVLink
-                    const GatherArgs* ga = p.gather;
-                    const long long o0 = gather_off + (long long)m * ga->world * ga->npad + (long long)cur.tile * p.TR;
-                    if (p.TR == 4 && (cur.tile + 1) * 4 <= p.N && (o0 & 3) == 0) {
-                        // The 4 rows of the tile (lanes 0, 8, 16, 24) as one 16-byte store per rank.
-                        const float v1 = __shfl_sync(0xffffffffu, v, 8), v2 = __shfl_sync(0xffffffffu, v, 16);
-                        const float v3 = __shfl_sync(0xffffffffu, v, 24);
-                        if (lane == 0)
-                            for (int rk = 0; rk < ga->world; ++rk)
-                                *reinterpret_cast<float4*>(ga->y[rk] + o0) = make_float4(v, v1, v2, v3);
-                    } else if (g == 0 && row < p.N) {
-                        for (int rk = 0; rk < ga->world; ++rk) ga->y[rk][o0 + r] = v;
-                    }
-                } else if (g == 0 && row < p.N) {
-                    p.y[(size_t)m * p.ldy + row] = v;
-                }
+                if (g == 0 && row < p.N) p.y[(size_t)m * p.ldy + row] = v;
                 acc[m] = 0.0f;
             }
         }
@@ -533,6 +600,7 @@ __device__ __forceinline__ void gemv_q_fast_body(const QGemvParams& p) {
         }
         cur.next(p, GW);
     }
+    if (p.gather) gather_send(p, M, p.TR, cur.tile, GW, lane);
     if (p.yhost) copy_y_to_host(p);   // every warp gets here, the ones that gave up too
 }
 
@@ -548,29 +616,98 @@ __global__ void __launch_bounds__(512, 2) gemv_q_fast2(const QGemvParams p) {
     gemv_q_fast_body<F, M, kXGlobal, kDump>(p);
 }
 
-// One warp, after this rank's GEMV of the step: tell every peer that this
-// rank's slice has landed in its buffer, wait (bounded) until every peer's
-// counter for this rank shows the step, then advance the epoch, so the next
-// GEMV writes the other full-y area. The GEMV's stores to the peers were
-// performed when it completed (griddepcontrol.wait returns after that), so
-// one system-scope release per peer publishes them. On a timeout the epoch
-// still advances and the error word gets kErrPeerTimeout (the gathered y of
-// that step is then incomplete).
-__global__ void __launch_bounds__(32) gather_wait_kernel(const GatherArgs* __restrict__ ga, unsigned* err) {
+// After this rank's fused-gather GEMV of a step: poll this rank's receive area
+// until every peer entry of the step (M output rows × (world − 1) slices of
+// npad) shows the step's tag, copy the values into the full-y area, then, once
+// the GEMV has completed (its own slice is in the area by then), advance the
+// epoch: the last CTA to finish, counted on the ticket word. The polling
+// starts as soon as the CTAs find room, while the GEMV may still run, and a
+// peer's word is usable the moment it lands. Each thread polls eight entries
+// at a time with independent loads. A wait longer than kWaitLimitNs sets
+// kErrPeerTimeout and leaves the remaining entries of that thread as they
+// were; the epoch still advances.
+__global__ void __launch_bounds__(kGatherWaitThreads) gather_wait_kernel(const GatherArgs* __restrict__ ga, int M,
+                                                                          unsigned* err) {
     pdl_launch_dependents();
+    const int W = ga->world, me = ga->rank;
+    const unsigned np = (unsigned)ga->npad;
+    unsigned* ctrl = ga->ctrl[me];
+    const unsigned epoch = *reinterpret_cast<volatile const unsigned*>(ctrl);
+    const unsigned tag = epoch + 1u;
+    const long long base = (long long)(epoch & 1u) * ga->area, cols = (long long)W * np;
+    const unsigned seg = (unsigned)(W - 1) * np, total = (unsigned)M * seg;
+    const unsigned nthr = gridDim.x * blockDim.x;
+    const unsigned long long* src = ga->ll[me];
+    float* dst = ga->y;
+    bool ok = true;
+    constexpr int kPer = 8;
+    for (unsigned e0 = blockIdx.x * blockDim.x + threadIdx.x; ok && e0 < total; e0 += kPer * nthr) {
+        long long off[kPer];
+        unsigned need = 0;
+#pragma unroll
+        for (int j = 0; j < kPer; ++j) {
+            const unsigned e = e0 + j * nthr;
+            off[j] = 0;
+            if (e < total) {
+                const unsigned m = e / seg, rem = e - m * seg, pi = rem / np, row = rem - pi * np;
+                const unsigned rk = pi + (pi >= (unsigned)me ? 1u : 0u);
+                off[j] = base + m * cols + (long long)rk * np + row;
+                need |= 1u << j;
+            }
+        }
+        const unsigned long long t0 = globaltimer();
+        for (uint32_t it = 0; need; ++it) {
+            unsigned long long w[kPer];
+#pragma unroll
+            for (int j = 0; j < kPer; ++j) w[j] = (need >> j & 1u) ? ld_relaxed_sys_u64(src + off[j]) : 0ull;
+#pragma unroll
+            for (int j = 0; j < kPer; ++j)
+                if ((need >> j & 1u) && (unsigned)(w[j] >> 32) == tag) {
+                    dst[off[j]] = __uint_as_float((unsigned)w[j]);
+                    need &= ~(1u << j);
+                }
+            if (need && (it & 15u) == 15u && globaltimer() - t0 > kWaitLimitNs) ok = false;
+            if (!ok) break;
+        }
+    }
     pdl_wait_primary();   // this rank's GEMV of the step has completed
+    ok = __syncthreads_and(ok);
+    if (threadIdx.x == 0) {
+        if (!ok && err) atomicOr(err, kErrPeerTimeout);
+        bool last = true;
+        if (gridDim.x > 1) {
+            __threadfence();
+            last = atomicAdd(ctrl + kGatherTicket, 1u) == gridDim.x - 1;
+        }
+        if (last) {
+            if (gridDim.x > 1) ctrl[kGatherTicket] = 0u;
+            *reinterpret_cast<volatile unsigned*>(ctrl) = epoch + 1u;
+        }
+    }
+}
+
+// A gather step without data, one warp: a cross-GPU barrier in stream order.
+// After the previous kernel on the stream has completed, signal every peer
+// (this rank's word in its control block: the step's tag, a system-scope
+// release that also publishes the earlier kernels' stores), wait (bounded)
+// until every peer's word here has reached the tag, then advance the epoch.
+// A peer is at most one step ahead, and its words only grow, so ≥ (in
+// wrap-around arithmetic) is the test. On a timeout the epoch still advances
+// and the error word gets kErrPeerTimeout.
+__global__ void __launch_bounds__(32) gather_barrier_kernel(const GatherArgs* __restrict__ ga, unsigned* err) {
+    pdl_launch_dependents();
+    pdl_wait_primary();
     const int lane = threadIdx.x;
     unsigned* ctrl = ga->ctrl[ga->rank];
     const unsigned epoch = *reinterpret_cast<volatile unsigned*>(ctrl);
-    if (lane < ga->world && lane != ga->rank) {
-        __threadfence_system();
-        red_release_sys_add(ga->ctrl[lane] + kGatherCounters + ga->rank, 1u);
-    }
+    const unsigned want = epoch + 1u;
     bool ok = true;
     if (lane < ga->world && lane != ga->rank) {
-        const unsigned* cnt = ctrl + kGatherCounters + lane;
+        __threadfence_system();
+        st_release_sys_u32(ga->ctrl[lane] + kGatherSignals + ga->rank, want);
+        const unsigned* sig = ctrl + kGatherSignals + lane;
         const unsigned long long t0 = globaltimer();
-        for (uint32_t i = 0; ld_acquire_sys(cnt) < epoch + 1u; ++i) {
+        for (uint32_t i = 0; (int)(ld_acquire_sys(sig) - want) < 0; ++i) {
             if ((i & 63u) == 0 && globaltimer() - t0 > kWaitLimitNs) {
                 ok = false;
                 break;
@@ -580,8 +717,54 @@ __global__ void __launch_bounds__(32) gather_wait_kernel(const GatherArgs* __res
     ok = __all_sync(0xffffffffu, ok);
     if (lane == 0) {
         if (!ok && err) atomicOr(err, kErrPeerTimeout);
-        *reinterpret_cast<volatile unsigned*>(ctrl) = epoch + 1u;
+        *reinterpret_cast<volatile unsigned*>(ctrl) = want;
     }
+}
+
+// Release / acquire at system scope (what orders data stores before a flag), or
+// relaxed (a lone flag, or data that carries its own step tag).
+__device__ __forceinline__ void pingpong_store(unsigned* p, unsigned v, int relaxed) {
+    if (relaxed) asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+    else asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned pingpong_load(const unsigned* p, int relaxed) {
+    unsigned v;
+    if (relaxed) asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    else v = ld_acquire_sys(p);
+    return v;
+}
+
+// The NVLink signalling floor: ranks 0 and 1 bounce a flag `iters` times inside
+// one kernel each (one warp), rank 0 timing the last iters − iters/8 round trips
+// with %globaltimer.
+// The flag goes into the peer's control word kGatherPingWord, as a
+// system-scope release store read back with acquire loads (what a barrier
+// signal costs) or as relaxed ones (what a tagged data word costs).
+__global__ void __launch_bounds__(32) gather_pingpong_kernel(const GatherArgs* __restrict__ ga, unsigned base,
+                                                             int iters, int relaxed, unsigned* err,
+                                                             unsigned long long* ns) {
+    if (threadIdx.x != 0 || ga->world < 2 || ga->rank > 1) return;
+    const int me = ga->rank, peer = 1 - me;
+    unsigned* mine = ga->ctrl[me] + kGatherPingWord;
+    unsigned* theirs = ga->ctrl[peer] + kGatherPingWord;
+    // The first eighth of the round trips absorbs the two launches' skew; the
+    // time covers the rest (iters − iters/8).
+    const int warm = iters / 8;
+    unsigned long long t0 = globaltimer();
+    for (int i = 1; i <= iters; ++i) {
+        if (i == warm + 1) t0 = globaltimer();
+        const unsigned v = base + (unsigned)i;
+        if (me == 0) pingpong_store(theirs, v, relaxed);
+        const unsigned long long tw = globaltimer();
+        for (uint32_t k = 0; pingpong_load(mine, relaxed) != v; ++k) {
+            if ((k & 63u) == 0 && globaltimer() - tw > kWaitLimitNs) {
+                if (err) atomicOr(err, kErrPeerTimeout);
+                return;
+            }
+        }
+        if (me == 1) pingpong_store(theirs, v, relaxed);
+    }
+    if (me == 0 && ns) *ns = globaltimer() - t0;
 }
 
 // ---- Q4_0, one row of x, K a multiple of 2048: four weight rows per lane -----------------
@@ -680,7 +863,7 @@ __device__ __forceinline__ void gemv_q4_r4_body(const QGemvParams& p) {
     if constexpr (!kXGlobal) off += (xq_r4_bytes(p.ksteps) + 127) & ~(size_t)127;
     uint8_t* stages = smem + off + (size_t)warp * p.stages * 32 * SBB;
 
-    pdl_launch_dependents();
+    if (!p.gather) pdl_launch_dependents();   // with a gather: after griddepcontrol.wait (as above)
 
     int GW, gw, tiles_end;
     if (p.contiguous) {
@@ -708,6 +891,7 @@ __device__ __forceinline__ void gemv_q4_r4_body(const QGemvParams& p) {
     }
 
     pdl_wait_primary();
+    if (p.gather) pdl_launch_dependents();
     uint32_t pre[kR4PreRows * 9];
     bool have_pre = false;
     if constexpr (!kXGlobal) {
@@ -734,12 +918,7 @@ __device__ __forceinline__ void gemv_q4_r4_body(const QGemvParams& p) {
     const uint8_t* xb = kXGlobal ? p.xq : xs;
 
     const int r = lane >> 3, g = lane & 7;
-    long long gather_off = 0;
-    if (p.gather) {
-        const GatherArgs* ga = p.gather;
-        const unsigned epoch = *reinterpret_cast<volatile const unsigned*>(ga->ctrl[ga->rank]);
-        gather_off = (long long)(epoch & 1u) * ga->area + (long long)ga->rank * ga->npad;
-    }
+    if (p.gather && blockIdx.x == 0) gather_pad(p.gather, 1, p.N, threadIdx.x, blockDim.x);
     float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 
     for (int it = 0; it < nitems; ++it) {
@@ -761,21 +940,7 @@ __device__ __forceinline__ void gemv_q4_r4_body(const QGemvParams& p) {
         if (cur.ks == p.ksteps - 1) {
             const float v = r4_reduce(acc, lane);
             const int row = cur.tile * 4 + r;
-            if (p.gather) {   // this rank's slice in the local area and every peer's, over NVLink
-                const GatherArgs* ga = p.gather;
-                const long long o0 = gather_off + (long long)cur.tile * 4;
-                if ((cur.tile + 1) * 4 <= p.N && (o0 & 3) == 0) {
-                    const float v1 = __shfl_sync(0xffffffffu, v, 8), v2 = __shfl_sync(0xffffffffu, v, 16);
-                    const float v3 = __shfl_sync(0xffffffffu, v, 24);
-                    if (lane == 0)
-                        for (int rk = 0; rk < ga->world; ++rk)
-                            *reinterpret_cast<float4*>(ga->y[rk] + o0) = make_float4(v, v1, v2, v3);
-                } else if (g == 0 && row < p.N) {
-                    for (int rk = 0; rk < ga->world; ++rk) ga->y[rk][o0 + r] = v;
-                }
-            } else if (g == 0 && row < p.N) {
-                p.y[row] = v;
-            }
+            if (g == 0 && row < p.N) p.y[row] = v;
 #pragma unroll
             for (int k = 0; k < 4; ++k) acc[k] = 0.0f;
         }
@@ -788,6 +953,7 @@ __device__ __forceinline__ void gemv_q4_r4_body(const QGemvParams& p) {
         }
         cur.next(p, GW);
     }
+    if (p.gather) gather_send(p, 1, 4, cur.tile, GW, lane);
     if (p.yhost) copy_y_to_host(p);   // every warp gets here, the ones that gave up too
 }
 
@@ -861,18 +1027,22 @@ __global__ void __launch_bounds__(kThreadsQuantX) quantize_x_mma_kernel(const fl
     }
 }
 
+// c = A·B + (m0, m1, m0, m1): the int32 sums of rows (g, g+8) × x rows (2t, 2t+1)
+// start from the magic-number bits of their x row (kIntToFloatMagic, with the
+// Q4_0 bias −8·Σq folded in), so c comes out as the bits of a float whose
+// value is 2^23 + 2^22 + isum: one exact subtraction converts it.
 template <int F>
-__device__ __forceinline__ void mma_q(const uint32_t (&a)[4], uint2 b, int (&c)[4]) {
+__device__ __forceinline__ void mma_q(const uint32_t (&a)[4], uint2 b, int m0, int m1, int (&c)[4]) {
     if constexpr (F == kQ4_0)
         asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-                     "{%10,%10,%10,%10};"
+                     "{%10,%11,%10,%11};"
                      : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
-                     : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b.x), "r"(b.y), "r"(0));
+                     : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b.x), "r"(b.y), "r"(m0), "r"(m1));
     else
         asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-                     "{%10,%10,%10,%10};"
+                     "{%10,%11,%10,%11};"
                      : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
-                     : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b.x), "r"(b.y), "r"(0));
+                     : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b.x), "r"(b.y), "r"(m0), "r"(m1));
 }
 
 template <int F>
@@ -918,20 +1088,24 @@ __device__ __forceinline__ void mma_frag_pair(const uint8_t* st, int pair, int g
 }
 
 // acc[rr] += isum · (dw · dx) for rows g + 8·rr and x rows (2t, 2t+1), in the
-// reference's order and roundings: __fmul_rn / __fadd_rn, never contracted.
-// float(isum) comes exactly from the magic-number add (see kIntToFloatMagic).
-template <int F>
-__device__ __forceinline__ void mma_accumulate(const int (&c)[4], const uint32_t (&sc)[2], float4 db,
+// reference's order and roundings: every product and sum rounded on its own,
+// never contracted. c holds the magic-number bits (mma_q), so float(isum) is
+// one exact subtraction. The subtraction and dw·dx of a lane's two x rows go
+// through the packed FP32 unit (fadd2_rn / fmul2_rn: two IEEE operations each).
+// The product that is added to acc is a scalar __fmul_rn: a packed product
+// feeding a packed sum is contracted into a fused multiply-add by the code
+// generator even with explicit rounding (measured on B200: 44 % of such
+// pairs differ from the two roundings), which would break the reference's order.
+__device__ __forceinline__ void mma_accumulate(const int (&c)[4], const uint32_t (&sc)[2], float2 dx,
                                                float2 (&acc)[2]) {
-    const int m0 = F == kQ4_0 ? __float_as_int(db.y) : kIntToFloatMagic;
-    const int m1 = F == kQ4_0 ? __float_as_int(db.w) : kIntToFloatMagic;
+    const float2 unmagic = make_float2(-12582912.0f, -12582912.0f);
 #pragma unroll
     for (int rr = 0; rr < 2; ++rr) {
         const float dw = half_bits_to_float(sc[rr]);
-        const float i0 = __fadd_rn(__int_as_float(c[2 * rr] + m0), -12582912.0f);
-        const float i1 = __fadd_rn(__int_as_float(c[2 * rr + 1] + m1), -12582912.0f);
-        acc[rr].x = __fadd_rn(acc[rr].x, __fmul_rn(i0, __fmul_rn(dw, db.x)));
-        acc[rr].y = __fadd_rn(acc[rr].y, __fmul_rn(i1, __fmul_rn(dw, db.z)));
+        const float2 i = fadd2_rn(make_float2(__int_as_float(c[2 * rr]), __int_as_float(c[2 * rr + 1])), unmagic);
+        const float2 sc2 = fmul2_rn(make_float2(dw, dw), dx);
+        acc[rr].x = __fadd_rn(acc[rr].x, __fmul_rn(i.x, sc2.x));
+        acc[rr].y = __fadd_rn(acc[rr].y, __fmul_rn(i.y, sc2.y));
     }
 }
 
@@ -965,7 +1139,7 @@ __device__ __forceinline__ T ld_xfrag(const T* p) {
 // is deterministic but rounded differently. The launcher splits K only when
 // the tiles alone cannot fill the GPU.
 template <int F, bool kXS>
-__global__ void __launch_bounds__(kMmaWarps * 32) gemv_q_mma(const QGemvParams p, const __grid_constant__ CUtensorMap wmap) {
+__global__ void __launch_bounds__(kMmaWarps * 32, 1) gemv_q_mma(const QGemvParams p, const __grid_constant__ CUtensorMap wmap) {
     constexpr int KB = mma_kb<F>(), RS = mma_rs<F>(), ITEM = 16 * RS;
     extern __shared__ __align__(128) uint8_t smem[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
@@ -1062,23 +1236,29 @@ __global__ void __launch_bounds__(kMmaWarps * 32) gemv_q_mma(const QGemvParams p
                 // All MMAs of the item first, then the scaling in block order.
                 int c[KB][4];
                 uint32_t sc[KB][2];
+                float2 dxs[KB];
 #pragma unroll
                 for (int pr = 0; pr < KB / 2; ++pr) {
                     const int b = b0 + 2 * pr - xoff;   // index within the x held at xbase
                     const uint2 xe = ld_xfrag<kXS>(xf + ((size_t)b * 8 + g) * 4 + t);
                     const uint2 xo = ld_xfrag<kXS>(xf + ((size_t)(b + 1) * 8 + g) * 4 + t);
+                    const float4 de = ld_xfrag<kXS>(xd + (size_t)b * 4 + t);
+                    const float4 dn = ld_xfrag<kXS>(xd + (size_t)(b + 1) * 4 + t);
                     uint32_t ae[4], ao[4], s2[2][2];
                     mma_frag_pair<F>(st, pr, g, t, ae, ao, s2);
-                    mma_q<F>(ae, xe, c[2 * pr]);
-                    mma_q<F>(ao, xo, c[2 * pr + 1]);
+                    mma_q<F>(ae, xe, F == kQ4_0 ? __float_as_int(de.y) : kIntToFloatMagic,
+                             F == kQ4_0 ? __float_as_int(de.w) : kIntToFloatMagic, c[2 * pr]);
+                    mma_q<F>(ao, xo, F == kQ4_0 ? __float_as_int(dn.y) : kIntToFloatMagic,
+                             F == kQ4_0 ? __float_as_int(dn.w) : kIntToFloatMagic, c[2 * pr + 1]);
+                    dxs[2 * pr] = make_float2(de.x, de.z);
+                    dxs[2 * pr + 1] = make_float2(dn.x, dn.z);
                     sc[2 * pr][0] = s2[0][0];
                     sc[2 * pr][1] = s2[0][1];
                     sc[2 * pr + 1][0] = s2[1][0];
                     sc[2 * pr + 1][1] = s2[1][1];
                 }
 #pragma unroll
-                for (int j = 0; j < KB; ++j)
-                    mma_accumulate<F>(c[j], sc[j], ld_xfrag<kXS>(xd + (size_t)(b0 - xoff + j) * 4 + t), acc);
+                for (int j = 0; j < KB; ++j) mma_accumulate(c[j], sc[j], dxs[j], acc);
                 __syncwarp();
                 if (issued < nitems) {
                     fence_proxy_async_smem();
@@ -1441,6 +1621,13 @@ cudaError_t launch_quantize_x(const LaunchCfg& c, const QGemvParams& p, uint8_t*
                   p.ldx, p.up, p.ldu, xg, xq);
 }
 
+cudaError_t launch_stage_x(cudaStream_t s, const float* src, float* dst, long long n, int num_sms) {
+    if (n <= 0) return cudaSuccess;
+    const long long grid = std::min<long long>((n / 4 + 511) / 512 + 1, (long long)num_sms);
+    stage_x_kernel<<<(unsigned)grid, 512, 0, s>>>(src, dst, n);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_check_x_arith(cudaStream_t s, unsigned long long* bad) {
     check_x_arith_kernel<<<148 * 8, 256, 0, s>>>(bad);
     return cudaGetLastError();
@@ -1461,8 +1648,18 @@ cudaError_t launch_gemv_q(const LaunchCfg& c, int fmt, QGemvParams p, bool fast,
     return fmt == kQ4_0 ? dispatch_m<kQ4_0>(c, p, fast, smem, dump) : dispatch_m<kQ8_0>(c, p, fast, smem, dump);
 }
 
-cudaError_t launch_gather_wait(const LaunchCfg& c, const GatherArgs* g_dev, unsigned* err) {
-    return launch(gather_wait_kernel, dim3(1), dim3(32), 0, c, g_dev, err);
+cudaError_t launch_gather_wait(const LaunchCfg& c, const GatherArgs* g_dev, int M, int blocks, unsigned* err) {
+    return launch(gather_wait_kernel, dim3(blocks), dim3(kGatherWaitThreads), 0, c, g_dev, M, err);
+}
+
+cudaError_t launch_gather_barrier(const LaunchCfg& c, const GatherArgs* g_dev, unsigned* err) {
+    return launch(gather_barrier_kernel, dim3(1), dim3(32), 0, c, g_dev, err);
+}
+
+cudaError_t launch_gather_pingpong(cudaStream_t s, const GatherArgs* g_dev, unsigned base, int iters, bool relaxed,
+                                   unsigned* err, unsigned long long* ns) {
+    gather_pingpong_kernel<<<1, 32, 0, s>>>(g_dev, base, iters, relaxed ? 1 : 0, err, ns);
+    return cudaGetLastError();
 }
 
 size_t xmma_bytes(int nb) { return (size_t)nb * 320; }

@@ -88,15 +88,25 @@ struct QGemvParams {
 
 // All-gather of y fused into the fast kernel's epilogue (row-sharded GEMV,
 // one process per GPU). Every rank owns one buffer, mapped into its peers'
-// address spaces: two full-y areas [M][world·npad] (alternate steps) and a
-// control block of 32-bit words: [0] epoch (completed gathers),
-// [kGatherCounters + s] steps whose slice rank s has delivered here.
+// address spaces: two full-y areas [M_max][world·npad] of floats (alternate
+// steps; only this rank writes them), two receive areas of the same entries
+// as 64-bit words (the peers' slices: value bits low, step tag high) and a
+// control block of 32-bit words: [0] epoch (completed gather steps),
+// [kGatherTicket] the wait kernel's CTA count, [kGatherSignals + s] rank s's
+// latest barrier step.
+//
+// A step's tag is epoch + 1. A word that shows the tag holds that step's
+// value (one 64-bit store is single-copy atomic), so the receiver polls the
+// data itself: no fence, no flag, no second NVLink crossing.
 constexpr int kMaxRanks = 8;
-constexpr int kGatherCounters = 8;
+constexpr int kGatherTicket = 1;
+constexpr int kGatherSignals = 8;
+constexpr int kGatherPingWord = 32;   // control word of the NVLink ping-pong diagnostic
 struct GatherArgs {
-    float* y[kMaxRanks];         // rank r's full-y areas (this rank's own at [rank])
-    unsigned* ctrl[kMaxRanks];   // rank r's control block
-    long long area;              // floats per full-y area (M_max · world · npad)
+    float* y;                               // this rank's full-y areas
+    unsigned long long* ll[kMaxRanks];      // rank r's receive areas
+    unsigned* ctrl[kMaxRanks];              // rank r's control block
+    long long area;                         // entries per area (≥ M_max · world · npad)
     int world, rank, npad;
 };
 
@@ -131,6 +141,10 @@ struct LaunchCfg {
 // Quantize p.x (or silu(p.x) * p.up) into the layout of the plan (lane-major,
 // or four-row when p.r4) at xq (global memory, x_bytes(p) bytes).
 cudaError_t launch_quantize_x(const LaunchCfg& c, const QGemvParams& p, uint8_t* xq);
+// n floats from device-mapped page-locked host memory to device memory (a host
+// call's x), by a kernel: a GEMV launched after it with programmatic dependent
+// launch streams its weights meanwhile.
+cudaError_t launch_stage_x(cudaStream_t s, const float* src, float* dst, long long n, int num_sms);
 // Test hook: mismatch counts of the x quantizer's exact helpers (bad[3], zeroed
 // by the caller) against CUDA's divide, reciprocal and roundf.
 cudaError_t launch_check_x_arith(cudaStream_t s, unsigned long long* bad);
@@ -143,10 +157,21 @@ cudaError_t launch_gemv_q(const LaunchCfg& c, int fmt, QGemvParams p, bool fast,
 // Size of the fast kernel's dynamic shared memory for this launch.
 size_t gemv_q_smem(int fmt, const QGemvParams& p, int warps, int stages, bool x_in_smem);
 
-// Wait until every peer delivered this step's slice, then advance the epoch
-// (one warp; bounded wait, kErrPeerTimeout on err). Launched after a fused
-// GEMV on the same stream.
-cudaError_t launch_gather_wait(const LaunchCfg& c, const GatherArgs* g_dev, unsigned* err);
+// After a fused GEMV of M rows on the same stream: wait (bounded,
+// kErrPeerTimeout on err) until every peer's slice of the step shows the
+// step's tag in this rank's receive area, copy it into the full-y area, and
+// advance the epoch once the GEMV has completed. blocks: 1 .. number of SMs
+// (kGatherWaitThreads threads each).
+constexpr int kGatherWaitThreads = 256;
+cudaError_t launch_gather_wait(const LaunchCfg& c, const GatherArgs* g_dev, int M, int blocks, unsigned* err);
+// A gather step without data: a cross-GPU barrier in stream order (one warp;
+// system-scope release / acquire signals, bounded wait).
+cudaError_t launch_gather_barrier(const LaunchCfg& c, const GatherArgs* g_dev, unsigned* err);
+// Diagnostic: `iters` round trips of a flag between ranks 0 and 1 over NVLink
+// inside one kernel (one warp each; other ranks return at once); rank 0 writes
+// the elapsed nanoseconds to *ns. Values base+1 .. base+iters; bounded waits.
+cudaError_t launch_gather_pingpong(cudaStream_t s, const GatherArgs* g_dev, unsigned base, int iters, bool relaxed,
+                                   unsigned* err, unsigned long long* ns);
 
 // Tensor-core path for kMmaMinRows..8 rows of x (fast-kernel conditions):
 // x quantized by launch_quantize_x_mma into xmma_bytes(nb) bytes at p.xq,

@@ -17,11 +17,13 @@
 #include <cstring>
 #include <limits>
 #include <map>
+#include <unordered_map>
 #include <mutex>
 #include <string>
 #include <vector>
 
 #include <cuda_runtime.h>
+#include <functional>
 
 #define SMK_VERSION "0.1.0 (sm_100a)"
 
@@ -151,6 +153,34 @@ struct PinnedBuf {
     }
 };
 
+// A synchronous host call captured as a CUDA graph: its operands' addresses
+// (the effective ones: a page-locked host source or destination, or the
+// context's staging buffer for pageable memory), its shape, and how often it
+// has been seen.
+struct HostKey {
+    int fmt, M, N, K;
+    const void* xsrc;
+    const void* w;
+    const void* yout;
+    bool operator==(const HostKey& o) const {
+        return fmt == o.fmt && M == o.M && N == o.N && K == o.K && xsrc == o.xsrc && w == o.w && yout == o.yout;
+    }
+};
+struct HostKeyHash {
+    size_t operator()(const HostKey& k) const {
+        size_t h = std::hash<const void*>()(k.xsrc);
+        for (size_t v : {std::hash<const void*>()(k.w), std::hash<const void*>()(k.yout), (size_t)k.fmt,
+                         (size_t)k.M, (size_t)k.N, (size_t)k.K})
+            h = h * 0x9E3779B97F4A7C15ull + v;
+        return h;
+    }
+};
+struct HostGraph {
+    cudaGraphExec_t exec = nullptr;
+    unsigned long long used = 0;   // the context's call count at the last use (LRU)
+    int seen = 0;                  // calls with this key; < 0: capture failed, never retried
+};
+
 }  // namespace
 
 void smk::set_last_error(const char* msg) { g_last_error = msg; }
@@ -175,6 +205,17 @@ struct smk_ctx {
     std::mutex mu_stage;                      // held for a whole *_host call
     DevBuf staging;                           // *_host operands copied to the device (weights)
     PinnedBuf pinned;                         // *_host activations and outputs in pageable memory
+    // Synchronous quantized GEMVs repeated with the same operands replay a
+    // CUDA graph of their copy and kernel (guarded by mu_stage).
+    bool host_graphs = true;
+    cudaStream_t capture_stream = nullptr;   // non-blocking: captures never touch the legacy stream
+    std::unordered_map<HostKey, HostGraph, HostKeyHash> graphs;
+    unsigned long long host_calls = 0;
+    void clear_graphs() {
+        for (auto& kv : graphs)
+            if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
+        graphs.clear();
+    }
 };
 
 namespace {
@@ -255,7 +296,7 @@ QPlan plan_q(smk_ctx* c, smk::LaunchCfg* l, smk_qformat fmt, int M, int N, int K
 smk_status run_q(smk_ctx* c, smk_qformat fmt, int M, int N, int K, const float* x, int64_t ldx, const uint8_t* Wq,
                  float* y, int64_t ldy, cudaStream_t s, int32_t* dump,
                  const smk::GatherArgs* gather = nullptr, const float* up = nullptr, int64_t ldu = 0,
-                 float* yhost = nullptr) {
+                 float* yhost = nullptr, bool force_pdl = false) {
     // yhost: the device-mapped address of a page-locked output. The fast
     // kernel then writes y (device memory, same ldy) and copies it there at
     // its end; the other kernels write yhost directly.
@@ -267,6 +308,7 @@ smk_status run_q(smk_ctx* c, smk_qformat fmt, int M, int N, int K, const float* 
         return SMK_OK;
     }
     smk::LaunchCfg l = cfg_for(c, s);
+    if (force_pdl) l.pdl = true;   // the previous kernel writes x only (a host call's stage_x_kernel)
     if (!gather && M >= smk::kMmaMinRows && !dump && K % 256 == 0 && (reinterpret_cast<uintptr_t>(Wq) & 15) == 0) {
         // Several rows of x: integer tensor-core kernel (bitwise the reference's
         // scalar order), x quantized once into scratch by its own kernel.
@@ -394,10 +436,11 @@ smk_status smk_ctx_create(int device, smk_ctx** out) {
     c->d_reject = c->d_err + 1;
     c->d_ticket = c->d_err + 2;
     e = cudaMemset(c->d_err, 0, 4 * sizeof(unsigned));
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&c->capture_stream, cudaStreamNonBlocking);
     if (e != cudaSuccess) {
         cudaFree(c->d_err);
         delete c;
-        return cuda_fail(e, "cudaMemset");
+        return cuda_fail(e, "context set-up");
     }
     *out = c;
     return SMK_OK;
@@ -407,6 +450,8 @@ smk_status smk_ctx_destroy(smk_ctx* c) {
     if (!c) return SMK_OK;
     DeviceGuard g(c->device);
     cudaDeviceSynchronize();
+    c->clear_graphs();
+    if (c->capture_stream) cudaStreamDestroy(c->capture_stream);
     for (auto& kv : c->scratch) kv.second.release();
     for (auto& kv : c->attn_ws) kv.second.release();
     c->staging.release();
@@ -419,7 +464,13 @@ smk_status smk_ctx_destroy(smk_ctx* c) {
 
 smk_status smk_ctx_set(smk_ctx* c, int option, long long v) {
     if (!c) return fail(SMK_ERR_ARGUMENT, "ctx must not be NULL");
+    {
+        // Captured host calls hold the launch settings of their capture.
+        std::lock_guard<std::mutex> lock(c->mu_stage);
+        c->clear_graphs();
+    }
     switch (option) {
+        case SMK_OPT_HOST_GRAPHS: c->host_graphs = v != 0; return SMK_OK;
         case SMK_OPT_PDL: c->pdl = v != 0; return SMK_OK;
         case SMK_OPT_WARPS:
             if (v < 0 || v > 16) return fail(SMK_ERR_ARGUMENT, "warps must be in 0..16 (0: automatic)");
@@ -449,6 +500,7 @@ smk_status smk_ctx_get(smk_ctx* c, int option, long long* v) {
         case SMK_OPT_STAGES: *v = c->stages; return SMK_OK;
         case SMK_OPT_CTAS_PER_SM: *v = c->ctas_per_sm; return SMK_OK;
         case SMK_OPT_TILE_ORDER: *v = c->tile_order; return SMK_OK;
+        case SMK_OPT_HOST_GRAPHS: *v = c->host_graphs; return SMK_OK;
         default: return fail(SMK_ERR_ARGUMENT, "unknown option %d", option);
     }
 }
@@ -509,12 +561,14 @@ smk_status smk_gemv_q(smk_ctx* c, smk_qformat fmt, int M, int N, int K, const fl
 struct smk_gather {
     smk_ctx* c = nullptr;
     int world = 0, rank = 0, npad = 0, m_max = 0;
-    void* base = nullptr;                      // this rank's buffer: two full-y areas, control block
-    size_t area_bytes = 0;
+    void* base = nullptr;                      // this rank's buffer: full-y areas, receive areas, staging, control
+    size_t area_bytes = 0;                     // one full-y area (floats); a receive area is twice that
+    size_t staging_bytes = 0;                  // the GEMV's own output [m_max][npad], before it is sent
     void* peer[smk::kMaxRanks] = {};           // mapped peer buffers (peer[rank] = base)
     smk::GatherArgs host = {};
     smk::GatherArgs* dev = nullptr;            // the same, in device memory (kernel argument)
     unsigned long long steps = 0;              // calls so far: which area the next one writes
+    unsigned pings = 0;                        // ping-pong values used so far
     bool connected = false;
 };
 
@@ -540,8 +594,11 @@ smk_status smk_gather_create(smk_ctx* c, int world, int rank, int npad, int m_ma
     g->rank = rank;
     g->npad = npad;
     g->m_max = m_max;
+    if ((size_t)m_max * world * npad > (size_t)INT32_MAX / 2)
+        return fail(SMK_ERR_ARGUMENT, "m_max * world * npad too large");
     g->area_bytes = align256((size_t)m_max * world * npad * sizeof(float));
-    const size_t bytes = 2 * g->area_bytes + kGatherCtrlBytes;
+    g->staging_bytes = align256((size_t)m_max * npad * sizeof(float));
+    const size_t bytes = 6 * g->area_bytes + g->staging_bytes + kGatherCtrlBytes;
     cudaError_t e = cudaMalloc(&g->base, bytes);
     if (e == cudaSuccess) e = cudaMemset(g->base, 0, bytes);
     if (e == cudaSuccess) e = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(ipc_handle), g->base);
@@ -575,9 +632,11 @@ smk_status smk_gather_connect(smk_gather* g, const void* ipc_handles) {
         g->peer[r] = p;
     }
     smk::GatherArgs& a = g->host;
+    a.y = static_cast<float*>(g->base);
     for (int r = 0; r < g->world; ++r) {
-        a.y[r] = static_cast<float*>(g->peer[r]);
-        a.ctrl[r] = reinterpret_cast<unsigned*>(static_cast<char*>(g->peer[r]) + 2 * g->area_bytes);
+        char* b = static_cast<char*>(g->peer[r]);
+        a.ll[r] = reinterpret_cast<unsigned long long*>(b + 2 * g->area_bytes);
+        a.ctrl[r] = reinterpret_cast<unsigned*>(b + 6 * g->area_bytes + g->staging_bytes);
     }
     a.area = (long long)(g->area_bytes / sizeof(float));
     a.world = g->world;
@@ -613,12 +672,49 @@ smk_status smk_gemv_q_gather(smk_ctx* c, smk_gather* g, smk_qformat fmt, int M, 
     DeviceGuard dg(c->device);
     if (!dg.ok) return fail(SMK_ERR_CUDA, "cudaSetDevice(%d) failed", c->device);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    st = run_q(c, fmt, M, N_local, K, x, ldx, Wq, nullptr, 0, s, nullptr, g->dev);
+    float* staging = reinterpret_cast<float*>(static_cast<char*>(g->base) + 6 * g->area_bytes);
+    st = run_q(c, fmt, M, N_local, K, x, ldx, Wq, staging, g->npad, s, nullptr, g->dev);
     if (st != SMK_OK) return st;
     smk::LaunchCfg l = cfg_for(c, s);
-    SMK_CUDA(smk::launch_gather_wait(l, g->dev, c->d_err), "gather wait launch");
+    // Enough CTAs that each thread polls about eight peer entries, at most one per SM.
+    const long long entries = (long long)M * (g->world - 1) * g->npad;
+    const int blocks = (int)std::max(1LL, std::min<long long>(c->num_sms, (entries + 8 * smk::kGatherWaitThreads - 1) /
+                                                                            (8 * smk::kGatherWaitThreads)));
+    SMK_CUDA(smk::launch_gather_wait(l, g->dev, M, blocks, c->d_err), "gather wait launch");
     *y_full = reinterpret_cast<float*>(static_cast<char*>(g->base) + (g->steps & 1) * g->area_bytes);
     ++g->steps;
+    return SMK_OK;
+}
+
+smk_status smk_gather_barrier(smk_gather* g, void* stream) {
+    if (!g) return fail(SMK_ERR_ARGUMENT, "gather must not be NULL");
+    if (!g->connected) return fail(SMK_ERR_ARGUMENT, "gather not connected");
+    DeviceGuard dg(g->c->device);
+    if (!dg.ok) return fail(SMK_ERR_CUDA, "cudaSetDevice(%d) failed", g->c->device);
+    SMK_CUDA(smk::launch_gather_barrier(cfg_for(g->c, static_cast<cudaStream_t>(stream)), g->dev, g->c->d_err),
+             "gather barrier launch");
+    ++g->steps;
+    return SMK_OK;
+}
+
+smk_status smk_gather_pingpong(smk_gather* g, int iters, int relaxed, unsigned long long* ns, void* stream) {
+    if (!g || !ns) return fail(SMK_ERR_ARGUMENT, "gather and ns must not be NULL");
+    if (!g->connected) return fail(SMK_ERR_ARGUMENT, "gather not connected");
+    if (iters < 1 || iters > (1 << 20)) return fail(SMK_ERR_ARGUMENT, "iters must be in 1..2^20");
+    DeviceGuard dg(g->c->device);
+    if (!dg.ok) return fail(SMK_ERR_CUDA, "cudaSetDevice(%d) failed", g->c->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    unsigned long long* d_ns = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g->c->mu_scratch);
+        SMK_CUDA(g->c->test_buf.reserve(sizeof(unsigned long long)), "cudaMalloc (test)");
+        d_ns = static_cast<unsigned long long*>(g->c->test_buf.ptr);
+        SMK_CUDA(cudaMemsetAsync(d_ns, 0, sizeof *d_ns, s), "cudaMemsetAsync");
+        SMK_CUDA(smk::launch_gather_pingpong(s, g->dev, g->pings, iters, relaxed != 0, g->c->d_err, d_ns), "ping-pong launch");
+        SMK_CUDA(cudaMemcpyAsync(ns, d_ns, sizeof *ns, cudaMemcpyDeviceToHost, s), "cudaMemcpyAsync");
+        SMK_CUDA(cudaStreamSynchronize(s), "cudaStreamSynchronize");
+    }
+    g->pings += (unsigned)iters;
     return SMK_OK;
 }
 
@@ -682,6 +778,32 @@ smk_status smk_rope_kv(smk_ctx* c, const float* qkv, const float* inv_freq, cons
     return SMK_OK;
 }
 
+namespace {
+// The attention workspace of `stream` when max_len takes more than one chunk:
+// tickets (one per KV head) at a fixed place at the start of the buffer, zeroed
+// when the buffer is allocated and reset by every call that used them; the
+// partials after them, sized by the call. One chunk: no workspace (nullptr).
+smk_status attention_workspace(smk_ctx* c, cudaStream_t s, int max_len, int nh, int nkv, int hd, float** ws,
+                               unsigned** tickets) {
+    *ws = nullptr;
+    *tickets = nullptr;
+    const int chunks = smk::attention_chunks(max_len);
+    if (chunks <= 1) return SMK_OK;
+    constexpr int kMaxTicketHeads = 256;
+    if (nkv > kMaxTicketHeads) return fail(SMK_ERR_ARGUMENT, "at most %d KV heads", kMaxTicketHeads);
+    const size_t tb = kMaxTicketHeads * sizeof(unsigned);
+    const size_t need = tb + (size_t)nkv * chunks * (nh / nkv) * (hd + 2) * sizeof(float);
+    std::lock_guard<std::mutex> lock(c->mu_scratch);
+    DevBuf& b = c->attn_ws[s];
+    const bool grow = need > b.bytes;
+    SMK_CUDA(b.reserve(need), "cudaMalloc (attention workspace)");
+    *tickets = static_cast<unsigned*>(b.ptr);
+    *ws = reinterpret_cast<float*>(static_cast<uint8_t*>(b.ptr) + tb);
+    if (grow) SMK_CUDA(cudaMemsetAsync(b.ptr, 0, tb, s), "cudaMemsetAsync");
+    return SMK_OK;
+}
+}  // namespace
+
 smk_status smk_attention_decode(smk_ctx* c, const float* q, const float* k_cache, const float* v_cache, float* out,
                                 const int32_t* len_dev, int len, int max_len, int nh, int nkv, int hd, int capacity,
                                 float scale, void* stream) {
@@ -698,28 +820,40 @@ smk_status smk_attention_decode(smk_ctx* c, const float* q, const float* k_cache
     DeviceGuard g(c->device);
     if (!g.ok) return fail(SMK_ERR_CUDA, "cudaSetDevice(%d) failed", c->device);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    const int chunks = smk::attention_chunks(max_len);
     float* ws = nullptr;
     unsigned* tickets = nullptr;
-    if (chunks > 1) {
-        // Tickets (one per KV head) at a fixed place at the start of the buffer,
-        // zeroed when the buffer is allocated and reset by every call that used
-        // them; the partials after them, sized by the call.
-        constexpr int kMaxTicketHeads = 256;
-        if (nkv > kMaxTicketHeads) return fail(SMK_ERR_ARGUMENT, "at most %d KV heads", kMaxTicketHeads);
-        const size_t tb = kMaxTicketHeads * sizeof(unsigned);
-        const size_t need = tb + (size_t)nkv * chunks * (nh / nkv) * (hd + 2) * sizeof(float);
-        std::lock_guard<std::mutex> lock(c->mu_scratch);
-        DevBuf& b = c->attn_ws[s];
-        const bool grow = need > b.bytes;
-        SMK_CUDA(b.reserve(need), "cudaMalloc (attention workspace)");
-        tickets = static_cast<unsigned*>(b.ptr);
-        ws = reinterpret_cast<float*>(static_cast<uint8_t*>(b.ptr) + tb);
-        if (grow) SMK_CUDA(cudaMemsetAsync(b.ptr, 0, tb, s), "cudaMemsetAsync");
-    }
+    smk_status st = attention_workspace(c, s, max_len, nh, nkv, hd, &ws, &tickets);
+    if (st != SMK_OK) return st;
     SMK_CUDA(smk::launch_attention(s, c->pdl, q, k_cache, v_cache, out, len_dev, len, max_len, nh, nkv, hd, capacity,
                                    scale, ws, tickets, c->d_err),
              "attention launch");
+    return SMK_OK;
+}
+
+smk_status smk_rope_attention(smk_ctx* c, const float* qkv, const float* inv_freq, const int32_t* pos_dev, int pos,
+                              int max_len, int nh, int nkv, int hd, int interleaved, float* k_cache, float* v_cache,
+                              int capacity, float scale, float* out, void* stream) {
+    if (!c) return fail(SMK_ERR_ARGUMENT, "ctx must not be NULL");
+    if (nh <= 0 || nkv <= 0 || nh % nkv != 0) return fail(SMK_ERR_ARGUMENT, "heads must be positive, nh a multiple of nkv");
+    if (nh / nkv > smk::attention_max_rep())
+        return fail(SMK_ERR_ARGUMENT, "at most %d query heads per KV head (got %d)", smk::attention_max_rep(), nh / nkv);
+    if (hd <= 0 || hd % 32 != 0 || hd > smk::attention_max_hd())
+        return fail(SMK_ERR_ARGUMENT, "head_dim must be a multiple of 32 up to %d (got %d)", smk::attention_max_hd(), hd);
+    if (capacity <= 0 || max_len <= 0 || max_len > capacity)
+        return fail(SMK_ERR_ARGUMENT, "need 0 < max_len <= capacity");
+    if (!pos_dev && (pos < 0 || pos >= max_len))
+        return fail(SMK_ERR_ARGUMENT, "position %d outside 0..max_len-1 (max_len %d)", pos, max_len);
+    if (!qkv || !inv_freq || !k_cache || !v_cache || !out) return fail(SMK_ERR_ARGUMENT, "pointers must not be NULL");
+    DeviceGuard g(c->device);
+    if (!g.ok) return fail(SMK_ERR_CUDA, "cudaSetDevice(%d) failed", c->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    float* ws = nullptr;
+    unsigned* tickets = nullptr;
+    smk_status st = attention_workspace(c, s, max_len, nh, nkv, hd, &ws, &tickets);
+    if (st != SMK_OK) return st;
+    SMK_CUDA(smk::launch_rope_attention(s, c->pdl, qkv, inv_freq, pos_dev, pos, max_len, nh, nkv, hd, interleaved != 0,
+                                        k_cache, v_cache, capacity, scale, out, ws, tickets, c->d_err),
+             "rope + attention launch");
     return SMK_OK;
 }
 
@@ -741,9 +875,10 @@ smk_status smk_gemv_q_host(smk_ctx* c, smk_qformat fmt, int M, int N, int K, con
     DeviceGuard g(c->device);
     if (!g.ok) return fail(SMK_ERR_CUDA, "cudaSetDevice(%d) failed", c->device);
     const size_t xb = (size_t)M * K * 4, wb = (size_t)N * (K / 32) * smk::block_bytes(fmt), yb = (size_t)M * N * 4;
-    // Host activations reach the device by one DMA copy (from page-locked
-    // memory: the caller's, or this context's page-locked buffer for a
-    // pageable array); reading them in the kernel over the bus costs the same.
+    // Host activations reach the device through stage_x_kernel, which reads
+    // them from page-locked memory (the caller's, or this context's
+    // page-locked buffer for a pageable array) over the bus while the GEMV
+    // after it already streams its weights (programmatic dependent launch).
     // Host outputs are written by the GEMV into page-locked memory (mapped
     // into the device's address space under unified addressing), which costs
     // less than a copy back; the fast kernel does it from one CTA at its end.
@@ -763,21 +898,17 @@ smk_status smk_gemv_q_host(smk_ctx* c, smk_qformat fmt, int M, int N, int K, con
     const size_t dev_bytes = dyo + align256(yb);
     SMK_CUDA(c->staging.reserve(dev_bytes), "cudaMalloc (staging)");
     char* dst = static_cast<char*>(c->staging.ptr);
-    const float* dx = x;
-    if (xk != Mem::kDevice) {
-        const void* src = x;
-        if (xk == Mem::kPageable) {
-            std::memcpy(pin, x, xb);
-            src = pin;
-        }
-        SMK_CUDA(cudaMemcpyAsync(dst + dxo, src, xb, cudaMemcpyHostToDevice, s), "cudaMemcpyAsync (x)");
-        dx = reinterpret_cast<const float*>(dst + dxo);
+    const void* xsrc = x;   // where the copy of x reads (host memory)
+    const float* xdev = static_cast<const float*>(xmap);   // the same, device-mapped
+    if (xk == Mem::kPageable) {
+        std::memcpy(pin, x, xb);
+        xsrc = pin;
+        void* dm = nullptr;
+        SMK_CUDA(cudaHostGetDevicePointer(&dm, pin, 0), "cudaHostGetDevicePointer");
+        xdev = static_cast<const float*>(dm);
     }
-    const uint8_t* dw = Wq;
-    if (wk != Mem::kDevice) {
-        SMK_CUDA(cudaMemcpyAsync(dst + dwo, Wq, wb, cudaMemcpyHostToDevice, s), "cudaMemcpyAsync (Wq)");
-        dw = reinterpret_cast<const uint8_t*>(dst + dwo);
-    }
+    const float* dx = xk != Mem::kDevice ? reinterpret_cast<const float*>(dst + dxo) : x;
+    const uint8_t* dw = wk != Mem::kDevice ? reinterpret_cast<const uint8_t*>(dst + dwo) : Wq;
     float* dy = y;
     float* yhost = nullptr;
     if (yk == Mem::kPinned) yhost = static_cast<float*>(ymap);
@@ -787,8 +918,62 @@ smk_status smk_gemv_q_host(smk_ctx* c, smk_qformat fmt, int M, int N, int K, con
         yhost = static_cast<float*>(dm);
     }
     if (yhost) dy = reinterpret_cast<float*>(dst + dyo);
-    st = run_q(c, fmt, M, N, K, dx, K, dw, dy, N, s, nullptr, nullptr, nullptr, 0, yhost);
-    if (st != SMK_OK) return st;
+    // The call's device work: the copies of host operands, then the GEMV.
+    auto enqueue = [&](cudaStream_t q) -> smk_status {
+        if (wk != Mem::kDevice)
+            SMK_CUDA(cudaMemcpyAsync(dst + dwo, Wq, wb, cudaMemcpyHostToDevice, q), "cudaMemcpyAsync (Wq)");
+        if (xk != Mem::kDevice)
+            SMK_CUDA(smk::launch_stage_x(q, xdev, reinterpret_cast<float*>(dst + dxo), (long long)M * K, c->num_sms),
+                     "stage_x launch");
+        return run_q(c, fmt, M, N, K, dx, K, dw, dy, N, q, nullptr, nullptr, nullptr, 0, yhost, xk != Mem::kDevice);
+    };
+    // A call whose operands (effective addresses) and shape repeat a recent
+    // one replays a CUDA graph of that work: one launch instead of a copy and
+    // a kernel launch, and no host-side planning (the weights stay on the
+    // device, where the graph reads them at replay). The graph is captured on
+    // the second call with a key, on a private non-blocking stream, and
+    // launched into the legacy default stream like the direct path.
+    HostGraph* hg = nullptr;
+    if (c->host_graphs && wk == Mem::kDevice && K > 0) {
+        const HostKey key{(int)fmt, M, N, K, xsrc, Wq, yhost ? static_cast<const void*>(yhost) : y};
+        auto it = c->graphs.find(key);
+        if (it == c->graphs.end()) {
+            constexpr size_t kMaxHostGraphs = 64;
+            if (c->graphs.size() >= kMaxHostGraphs) {   // drop the least recently used
+                auto lru = c->graphs.begin();
+                for (auto j = c->graphs.begin(); j != c->graphs.end(); ++j)
+                    if (j->second.used < lru->second.used) lru = j;
+                if (lru->second.exec) cudaGraphExecDestroy(lru->second.exec);
+                c->graphs.erase(lru);
+            }
+            it = c->graphs.emplace(key, HostGraph{}).first;
+        }
+        hg = &it->second;
+        hg->used = ++c->host_calls;
+        if (!hg->exec && hg->seen >= 0 && ++hg->seen >= 2) {
+            cudaStream_t q = c->capture_stream;
+            cudaGraph_t graph = nullptr;
+            SMK_CUDA(cudaStreamBeginCapture(q, cudaStreamCaptureModeThreadLocal), "cudaStreamBeginCapture");
+            st = enqueue(q);
+            const cudaError_t e = cudaStreamEndCapture(q, &graph);
+            if (st != SMK_OK) {
+                if (graph) cudaGraphDestroy(graph);
+                return st;
+            }
+            if (e == cudaSuccess && cudaGraphInstantiate(&hg->exec, graph, 0) != cudaSuccess) hg->exec = nullptr;
+            if (graph) cudaGraphDestroy(graph);
+            if (!hg->exec) {   // not capturable here: this key takes the direct path from now on
+                cudaGetLastError();
+                hg->seen = -1;
+            }
+        }
+    }
+    if (hg && hg->exec) {
+        SMK_CUDA(cudaGraphLaunch(hg->exec, s), "cudaGraphLaunch");
+    } else {
+        st = enqueue(s);
+        if (st != SMK_OK) return st;
+    }
     SMK_CUDA(cudaStreamSynchronize(s), "cudaStreamSynchronize");
     if (yk == Mem::kPageable) std::memcpy(y, pin + px, yb);
     return SMK_OK;

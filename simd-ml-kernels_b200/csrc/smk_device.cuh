@@ -120,6 +120,51 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
     return v;
 }
 
+// A float and a 32-bit tag as one 64-bit word (value bits low), and the
+// system-scope relaxed accesses that move such words between GPUs: each
+// 64-bit element is single-copy atomic, so a reader that sees the tag sees
+// the value stored with it.
+__device__ __forceinline__ unsigned long long tagged_word(float v, unsigned tag) {
+    return (unsigned long long)__float_as_uint(v) | ((unsigned long long)tag << 32);
+}
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsigned long long a) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(a) : "memory");
+}
+__device__ __forceinline__ void st_relaxed_sys_v2_u64(unsigned long long* p, unsigned long long a,
+                                                      unsigned long long b) {
+    asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(a), "l"(b) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_sys_u32(unsigned* p, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Two IEEE float32 products / sums in one packed instruction (sm_100), each
+// rounded to nearest on its own. A packed product that feeds a packed sum is
+// fused into one multiply-add by the code generator, explicit .rn or not
+// (checked on B200), so use them only where no sum consumes a product whose
+// rounding matters.
+__device__ __forceinline__ unsigned long long pack_f2(float2 v) {
+    return (unsigned long long)__float_as_uint(v.x) | ((unsigned long long)__float_as_uint(v.y) << 32);
+}
+__device__ __forceinline__ float2 unpack_f2(unsigned long long v) {
+    return make_float2(__uint_as_float((unsigned)v), __uint_as_float((unsigned)(v >> 32)));
+}
+__device__ __forceinline__ float2 fmul2_rn(float2 a, float2 b) {
+    unsigned long long d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(pack_f2(a)), "l"(pack_f2(b)));
+    return unpack_f2(d);
+}
+__device__ __forceinline__ float2 fadd2_rn(float2 a, float2 b) {
+    unsigned long long d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(pack_f2(a)), "l"(pack_f2(b)));
+    return unpack_f2(d);
+}
+
 // Programmatic dependent launch. Both are no-ops when the kernel was not
 // launched with the programmatic-serialization attribute.
 __device__ __forceinline__ void pdl_launch_dependents() {

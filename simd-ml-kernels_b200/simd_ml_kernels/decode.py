@@ -9,14 +9,16 @@ Functions (CUDA tensors, queued on torch's current stream):
     add_rmsnorm(x, w, eps, delta=None, out=None)     x += delta; out = RMSNorm(x) * w
     rope_kv(qkv, inv_freq, pos, nh, nkv, hd, k_cache, v_cache, q_out=None, interleaved=False)
     attention_decode(q, k_cache, v_cache, length, nkv, out=None)
+    rope_attention(qkv, inv_freq, pos, nh, nkv, hd, k_cache, v_cache, out=None, interleaved=False)
+                                                     the two above as one kernel
     rope_inv_freq(head_dim, theta, scaling=None)     the frequencies (float32, host)
 
 `LlamaDecoder` holds one model's weights on the device (Q4_0 or Q8_0 blocks,
 q/k/v and gate/up as concatenated row groups), its KV cache and buffers, and
 runs `step(token)`: the embedding row, per layer RMSNorm -> qkv GEMV -> RoPE +
-cache write -> attention -> o GEMV -> residual RMSNorm -> gate/up GEMV -> down
-GEMV on silu(gate)*up, then the final norm and the LM-head GEMV. Every launch
-is asynchronous, so a run of steps can be captured in a CUDA graph.
+cache write + attention (one kernel) -> o GEMV -> residual RMSNorm -> gate/up
+GEMV -> down GEMV on silu(gate)*up, then the final norm and the LM-head GEMV.
+Every launch is asynchronous, so a run of steps can be captured in a CUDA graph.
 """
 
 from __future__ import annotations
@@ -108,6 +110,30 @@ def attention_decode(q, k_cache, v_cache, length: int, nkv: int, out=None, max_l
     s = float(np.float32(1.0 / math.sqrt(hd))) if scale is None else float(scale)
     _core._attention_decode(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), out.data_ptr(), 0, int(length),
                             int(max_len or length), nh, nkv, hd, cap, s, _stream(q), _dev(q))
+    return out
+
+
+def rope_attention(qkv, inv_freq, pos: int, nh: int, nkv: int, hd: int, k_cache, v_cache, out=None,
+                   interleaved: bool = False, max_len: int | None = None, scale: float | None = None):
+    """rope_kv and attention_decode in one kernel: rotates this token's q and k
+    (qkv = [q | k | v], not rotated) at position pos, writes k and v to row pos
+    of the caches [nkv, capacity, hd] and returns the attention of q over
+    positions 0 .. pos, [nh, hd]. The same values as the two calls."""
+    torch = _torch()
+    for t, nm in ((qkv, "qkv"), (inv_freq, "inv_freq"), (k_cache, "k_cache"), (v_cache, "v_cache")):
+        _check(t, nm, torch.float32)
+    if qkv.numel() != (nh + 2 * nkv) * hd or inv_freq.numel() != hd // 2:
+        raise ValueError("qkv must hold (nh + 2*nkv) * hd values and inv_freq hd/2")
+    cap = k_cache.shape[-2]
+    if k_cache.numel() != nkv * cap * hd or v_cache.numel() != k_cache.numel():
+        raise ValueError("caches must be [nkv, capacity, hd]")
+    if out is None:
+        out = torch.empty((nh, hd), dtype=torch.float32, device=qkv.device)
+    _check(out, "out", torch.float32)
+    s = float(np.float32(1.0 / math.sqrt(hd))) if scale is None else float(scale)
+    _core._rope_attention(qkv.data_ptr(), inv_freq.data_ptr(), 0, int(pos), int(max_len or pos + 1), nh, nkv, hd,
+                          int(interleaved), k_cache.data_ptr(), v_cache.data_ptr(), cap, s, out.data_ptr(),
+                          _stream(qkv), _dev(qkv))
     return out
 
 
@@ -212,7 +238,7 @@ class LlamaDecoder:
             x=torch.zeros(s.hidden, **f32), h=torch.empty(s.hidden, **f32), qkv=torch.empty(qkv_rows, **f32),
             q=torch.empty((s.heads, s.head_dim), **f32), att=torch.empty((s.heads, s.head_dim), **f32),
             delta=torch.zeros(s.hidden, **f32), gate_up=torch.empty(2 * s.ffn, **f32),
-            logits=torch.empty(s.vocab, **f32), tok=torch.zeros(1, dtype=torch.int32, device=self.device),
+            logits=torch.empty(s.vocab, **f32), tok=torch.arange(s.vocab, dtype=torch.int32, device=self.device),
             k_cache=torch.zeros((s.layers, s.kv_heads, capacity, s.head_dim), **f32),
             v_cache=torch.zeros((s.layers, s.kv_heads, capacity, s.head_dim), **f32))
         self.pos = 0
@@ -226,13 +252,21 @@ class LlamaDecoder:
         self.buf.v_cache.zero_()
 
     def _embed(self, token) -> None:
+        """x = the token's embedding row. A host token id selects its entry of
+        the device table tok = 0 .. vocab-1 (no copy or fill kernel); a device
+        tensor is passed through as the row index."""
         torch = _torch()
         s, b = self.shape, self.buf
         if isinstance(token, torch.Tensor):
-            b.tok.copy_(token.reshape(1).to(torch.int32))
+            rows = token.reshape(1).to(torch.int32)
+            b.extra["tok"] = rows   # alive until the launch has read it
+            ptr = rows.data_ptr()
         else:
-            b.tok.fill_(int(token))
-        _core._dequantize_rows(self._fmt, s.vocab, s.hidden, self.w.embed.data_ptr(), b.tok.data_ptr(), 1,
+            t = int(token)
+            if not 0 <= t < s.vocab:
+                raise IndexError(f"token {t} outside the vocabulary ({s.vocab})")
+            ptr = b.tok.data_ptr() + 4 * t
+        _core._dequantize_rows(self._fmt, s.vocab, s.hidden, self.w.embed.data_ptr(), ptr, 1,
                                b.x.data_ptr(), s.hidden, _stream(b.x), _dev(b.x))
 
     def step(self, token, logits: bool = True):
@@ -248,9 +282,8 @@ class LlamaDecoder:
         for li, L in enumerate(w.layers):
             add_rmsnorm(b.x, L.attn_norm, s.eps, delta=delta, out=b.h)
             self._gemv(b.h, L.qkv, b.qkv.numel(), s.hidden, out=b.qkv)
-            kc, vc = b.k_cache[li], b.v_cache[li]
-            rope_kv(b.qkv, self.inv_freq, pos, nh, nkv, hd, kc, vc, q_out=b.q, interleaved=self.interleaved)
-            attention_decode(b.q, kc, vc, pos + 1, nkv, out=b.att, max_len=self.cap)
+            rope_attention(b.qkv, self.inv_freq, pos, nh, nkv, hd, b.k_cache[li], b.v_cache[li], out=b.att,
+                           interleaved=self.interleaved, max_len=self.cap)
             self._gemv(b.att.reshape(-1), L.o, s.hidden, nh * hd, out=b.delta)
             add_rmsnorm(b.x, L.mlp_norm, s.eps, delta=b.delta, out=b.h)
             self._gemv(b.h, L.gate_up, 2 * s.ffn, s.hidden, out=b.gate_up)
@@ -265,4 +298,4 @@ class LlamaDecoder:
         return b.logits
 
     def launches_per_token(self) -> int:
-        return 1 + 8 * self.shape.layers + 2
+        return 1 + 7 * self.shape.layers + 2

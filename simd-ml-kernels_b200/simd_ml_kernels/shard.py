@@ -8,9 +8,9 @@ one rank with the same kernel and order as unsharded, so the gathered y is
 bitwise identical for any rank count. x is replicated (every rank quantizes
 it itself, deterministically); y slices are all-gathered over NVLink, either
 by the GEMV kernel itself (gather="nvlink": each rank's kernel stores its
-slice into every rank's buffer through CUDA IPC mappings and signals it;
-a one-warp kernel waits for the peers' signals) or by NCCL's all-gather
-(gather="nccl"). One process per GPU. No reduction: K is never split across
+slice into every peer's receive buffer through CUDA IPC mappings, each value
+paired with the step's tag in one 64-bit store, and a wait kernel polls the
+tags and assembles the full y) or by NCCL's all-gather (gather="nccl"). One process per GPU. No reduction: K is never split across
 ranks.
 """
 

@@ -141,6 +141,45 @@ def test_attention_decode(torch, nh, nkv, hd, length):
     assert _core._device_error(torch.cuda.current_stream().cuda_stream) == 0
 
 
+@pytest.mark.gpu
+@pytest.mark.parametrize("nh,nkv,hd,interleaved", [(32, 8, 64, False), (8, 8, 128, True), (16, 2, 32, False)])
+@pytest.mark.parametrize("pos,max_len", [(0, 1), (6, 300), (255, 256), (256, 600), (1500, 2112)])
+def test_rope_attention_equals_unfused(torch, nh, nkv, hd, interleaved, pos, max_len):
+    """The fused kernel (RoPE, cache write and attention in one launch) gives the
+    bits of rope_kv followed by attention_decode: the same attention output,
+    the same k and v rows at pos, and nothing else of the caches touched; with
+    one chunk and with several (the position in the first, a middle or the
+    last chunk)."""
+    cap = 2112
+    rng = np.random.default_rng(pos + nh + hd)
+    inv = torch.from_numpy(dec.rope_inv_freq(hd, 500000.0, LLAMA3)).cuda()
+    qkv = torch.from_numpy(rng.standard_normal((nh + 2 * nkv) * hd).astype(np.float32)).cuda()
+    k0 = rng.standard_normal((nkv, cap, hd)).astype(np.float32)
+    v0 = rng.standard_normal((nkv, cap, hd)).astype(np.float32)
+    kc1, vc1 = torch.from_numpy(k0).cuda(), torch.from_numpy(v0).cuda()
+    kc2, vc2 = kc1.clone(), vc1.clone()
+    q = dec.rope_kv(qkv, inv, pos, nh, nkv, hd, kc1, vc1, interleaved=interleaved)
+    want = dec.attention_decode(q, kc1, vc1, pos + 1, nkv, max_len=max_len).cpu().numpy()
+    for _ in range(2):   # twice: the combine tickets start from zero again
+        got = dec.rope_attention(qkv, inv, pos, nh, nkv, hd, kc2, vc2, interleaved=interleaved,
+                                 max_len=max_len).cpu().numpy()
+        np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32))
+    assert torch.equal(kc1.view(torch.int32), kc2.view(torch.int32))
+    assert torch.equal(vc1.view(torch.int32), vc2.view(torch.int32))
+    from simd_ml_kernels import _core
+    assert _core._device_error(torch.cuda.current_stream().cuda_stream) == 0
+
+
+@pytest.mark.gpu
+def test_rope_attention_host_errors(torch):
+    """A position outside 0 .. max_len-1 is refused on the host, before a launch."""
+    qkv = torch.zeros(6 * 32, device="cuda")
+    inv = torch.ones(16, device="cuda")
+    kc = torch.zeros((1, 8, 32), device="cuda")
+    with pytest.raises(Exception, match="outside"):
+        dec.rope_attention(qkv, inv, 5, 4, 1, 32, kc, kc.clone(), max_len=4)
+
+
 def _small_model(torch, fmt, seed=11, interleaved=False):
     import simd_ml_kernels as sk
     sh = dec.LlamaShape(hidden=256, layers=2, heads=4, kv_heads=2, head_dim=64, ffn=512, vocab=512, eps=1e-5)

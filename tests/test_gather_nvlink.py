@@ -73,6 +73,17 @@ def _rank(rank, world, port, out_dir):
             prev = (copy, copy.clone())
         torch.cuda.synchronize()
         assert _core._device_error(torch.cuda.current_stream().cuda_stream) == 0
+        # Data-free gather steps (a device-side barrier across the ranks) and the
+        # NVLink ping-pong diagnostic: both end, in time, without a device error.
+        stream = torch.cuda.current_stream().cuda_stream
+        for _ in range(50):
+            _core._gather_barrier(sg._g, stream)
+        ns = _core._gather_pingpong(sg._g, 1000, 0, stream) + _core._gather_pingpong(sg._g, 1000, 1, stream)
+        assert (ns > 0) if rank == 0 else (ns == 0)
+        Y = sg.forward(X).reshape(M, N)   # the gather still works after them
+        torch.cuda.synchronize()
+        assert (Y - sk.gemv_q4_0_batch(X, Wq, N, K)).abs().max().item() <= 1e-5 * Y.abs().max().item()
+        assert _core._device_error(stream) == 0
         sg.close()
     except Exception as exc:  # noqa: BLE001 - reported to the parent
         status = f"error: {type(exc).__name__}: {exc}"

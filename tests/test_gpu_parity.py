@@ -536,6 +536,44 @@ def test_host_io_paths_bitwise_equal(sk, torch, fmt):
         fn(x[:-32], wd, N, K)
 
 
+@pytest.mark.parametrize("M", [1, 3])
+def test_host_call_graph_replay_tracks_operands(sk, torch, M):
+    """A synchronous call that repeats its operands' addresses and shape replays
+    a captured CUDA graph (from the second call on). Every call must still use
+    that call's values: x is rewritten in place and the weights on the device
+    change between calls, for pageable and page-locked x and y. Each result
+    equals the all-device call bitwise, with the graphs on (the default) and
+    off (SMK_OPT_HOST_GRAPHS = 0)."""
+    from simd_ml_kernels import _core
+    N, K = 4096, 2048
+    rng = np.random.default_rng(90 + M)
+    W = (rng.standard_normal((2, N, K)) * 0.02).astype(np.float32)
+    wq = [torch.from_numpy(O.quantize("q4_0", W[i]).ravel()).cuda() for i in range(2)]
+    wd = wq[0].clone()
+    xs_pinned = torch.empty((M, K)).pin_memory().numpy()
+    xs_page = np.empty((M, K), np.float32)
+    y_pinned = torch.empty((M, N)).pin_memory().numpy()
+    y_page = np.empty((M, N), np.float32)
+    try:
+        for graphs in (1, 0):
+            _core._ctx_set(6, graphs)
+            for xs in (xs_page, xs_pinned):
+                for ys in (y_page, y_pinned):
+                    for call in range(5):
+                        xs[:] = rng.standard_normal((M, K)).astype(np.float32)
+                        wd.copy_(wq[call % 2])
+                        want = sk.gemv_q4_0_batch(torch.from_numpy(xs.copy()).cuda(), wd, N, K).cpu().numpy()
+                        ys[:] = np.nan
+                        sk.gemv_q4_0_batch(xs, wd, N, K, out=ys)
+                        np.testing.assert_array_equal(ys.view(np.uint32), want.view(np.uint32),
+                                                      err_msg=f"graphs={graphs} call {call}")
+                        y = sk.gemv_q4_0_batch(xs, wd, N, K)
+                        np.testing.assert_array_equal(y.view(np.uint32), want.view(np.uint32))
+    finally:
+        _core._ctx_set(6, 1)
+    assert _core._device_error(torch.cuda.current_stream().cuda_stream) == 0
+
+
 @pytest.mark.parametrize("N,K", [(1003, 2048), (8192, 2048), (517, 2080), (4096, 4096)])
 def test_host_output_copy_bitwise_equal(sk, torch, N, K):
     """Host outputs from the fast kernel are copied to page-locked memory by
