@@ -88,9 +88,12 @@ smk_status smk_ctx_destroy(smk_ctx* ctx);
  *                   one of the last 64 keys replays a CUDA graph of its copy
  *                   and kernel (captured on its second occurrence); 0: every
  *                   call launches directly. Setting any option drops the
- *                   captured graphs. */
+ *                   captured graphs.
+ *   SMK_OPT_DENSE_MMA  1 (default): smk_gemv_dense with bfloat16 weights and
+ *                   4..8 rows of x takes the tensor-core kernel (x split
+ *                   exactly into bf16 parts); 0: the CUDA-core kernel. */
 enum { SMK_OPT_PDL = 1, SMK_OPT_WARPS = 2, SMK_OPT_STAGES = 3, SMK_OPT_CTAS_PER_SM = 4, SMK_OPT_TILE_ORDER = 5,
-       SMK_OPT_HOST_GRAPHS = 6 };
+       SMK_OPT_HOST_GRAPHS = 6, SMK_OPT_DENSE_MMA = 7 };
 smk_status smk_ctx_set(smk_ctx* ctx, int option, long long value);
 smk_status smk_ctx_get(smk_ctx* ctx, int option, long long* value);
 /* The CUDA device that owns `ptr` (device or managed memory), or -1 for host memory. */
@@ -215,6 +218,19 @@ smk_status smk_rope_kv(smk_ctx* ctx, const float* qkv, const float* inv_freq, co
 smk_status smk_attention_decode(smk_ctx* ctx, const float* q, const float* k_cache, const float* v_cache, float* out,
                                 const int32_t* len_dev, int len, int max_len, int nh, int nkv, int hd, int capacity,
                                 float scale, void* stream);
+/* A quantized GEMV with the decode step's neighbours fused in (device
+ * pointers, asynchronous; the fast kernels' conditions: K % 256 == 0, Wq
+ * 16-byte aligned):
+ *   w_norm != NULL: y = (RMSNorm(x) * w_norm) @ W^T, the reference's rms_norm
+ *                   (examples/llama/llama.py:184-188) applied to each row of
+ *                   x inside the GEMV's x quantization (x is not modified);
+ *   up != NULL:     x replaced by silu(x) * up (as smk_gemv_q_silu_mul);
+ *   r != NULL:      y = r + (...) @ W^T, the residual add of Llama.step
+ *                   (:414-439) in the GEMV's store; r may be y (in place).
+ * w_norm and up exclude each other. */
+smk_status smk_gemv_q_fused(smk_ctx* ctx, smk_qformat fmt, int M, int N, int K, const float* x, int64_t ldx,
+                            const float* up, int64_t ldu, const float* w_norm, double eps, const uint8_t* Wq,
+                            const float* r, int64_t ldr, float* y, int64_t ldy, void* stream);
 /* smk_rope_kv and smk_attention_decode as one kernel (the decode step's form):
  * this token's qkv (not rotated) at position pos (*pos_dev when pos_dev is not
  * NULL), k and v written to row pos of the caches, attention over positions

@@ -34,8 +34,8 @@ CUDA_HOME = os.path.dirname(os.path.dirname(NVCC))
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-std=c++17", "-O3", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
               "--expt-relaxed-constexpr", "-I" + INCLUDE] + ARCH
-CU_SOURCES = ["gemv_quant.cu", "gemv_dense.cu", "gemv_int8.cu", "dequant.cu", "decode.cu", "smk_api.cu",
-              "gemv_noalloc.cu"]
+CU_SOURCES = ["gemv_quant.cu", "gemv_dense.cu", "gemv_dense_mma.cu", "gemv_int8.cu", "dequant.cu", "decode.cu",
+              "smk_api.cu", "gemv_noalloc.cu"]
 HEADERS = glob.glob(os.path.join(CSRC, "*.cuh")) + glob.glob(os.path.join(INCLUDE, "*.h"))
 
 LIB = os.path.join(PKG, "libsmk_cuda.so")

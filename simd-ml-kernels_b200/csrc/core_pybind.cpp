@@ -779,6 +779,20 @@ PYBIND11_MODULE(_core, m) {
                                    reinterpret_cast<float*>(out), reinterpret_cast<const int32_t*>(len_dev), len,
                                    max_len, nh, nkv, hd, cap, scale, reinterpret_cast<void*>(stream)));
     });
+    m.def("_gemv_q_fused", [](int fmt, int M, int N, int K, uintptr_t x, long long ldx, uintptr_t up, long long ldu,
+                              uintptr_t w_norm, double eps, uintptr_t w, uintptr_t r, long long ldr, uintptr_t y,
+                              long long ldy, uintptr_t stream, int device) {
+        smk_ctx* c = ctx_for(device);
+        smk_status st;
+        {
+            py::gil_scoped_release release;
+            st = smk_gemv_q_fused(c, (smk_qformat)fmt, M, N, K, reinterpret_cast<const float*>(x), ldx,
+                                  reinterpret_cast<const float*>(up), ldu, reinterpret_cast<const float*>(w_norm), eps,
+                                  reinterpret_cast<const uint8_t*>(w), reinterpret_cast<const float*>(r), ldr,
+                                  reinterpret_cast<float*>(y), ldy, reinterpret_cast<void*>(stream));
+        }
+        check(st);
+    });
     m.def("_rope_attention", [](uintptr_t qkv, uintptr_t inv_freq, uintptr_t pos_dev, int pos, int max_len, int nh,
                                 int nkv, int hd, int interleaved, uintptr_t kc, uintptr_t vc, int cap, float scale,
                                 uintptr_t out, uintptr_t stream, int device) {

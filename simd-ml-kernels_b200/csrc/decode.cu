@@ -221,22 +221,28 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnArgs 
     __syncthreads();   // q in shared memory; the token's k and v rows written (kRope)
     const float* K = a.kc + (size_t)g * a.cap * hd;
     const float* V = a.vc + (size_t)g * a.cap * hd;
-    // Scores: position p0 + j at thread j (kAttnChunk <= threads · passes).
+    // Scores: position p0 + j at thread j (kAttnChunk <= threads · passes). The
+    // K row is read 8 float4 at a time, all 8 loads in flight before the FMAs.
     for (int j = threadIdx.x; j < np; j += kAttnThreads) {
         const float4* kr = reinterpret_cast<const float4*>(K + (size_t)(p0 + j) * hd);
         float acc[kAttnMaxRep];
 #pragma unroll
         for (int h = 0; h < kAttnMaxRep; ++h) acc[h] = 0.0f;
-        for (int d4 = 0; d4 < hd / 4; ++d4) {
-            const float4 kv = kr[d4];
+        for (int d0 = 0; d0 < hd / 4; d0 += 8) {   // hd a multiple of 32: whole groups of 8
+            float4 kv[8];
 #pragma unroll
-            for (int h = 0; h < kAttnMaxRep; ++h) {
-                if (h < rep) {
-                    const float4 qv = reinterpret_cast<const float4*>(qs + h * hd)[d4];
-                    acc[h] = fmaf(qv.x, kv.x, acc[h]);
-                    acc[h] = fmaf(qv.y, kv.y, acc[h]);
-                    acc[h] = fmaf(qv.z, kv.z, acc[h]);
-                    acc[h] = fmaf(qv.w, kv.w, acc[h]);
+            for (int u = 0; u < 8; ++u) kv[u] = kr[d0 + u];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+#pragma unroll
+                for (int h = 0; h < kAttnMaxRep; ++h) {
+                    if (h < rep) {
+                        const float4 qv = reinterpret_cast<const float4*>(qs + h * hd)[d0 + u];
+                        acc[h] = fmaf(qv.x, kv[u].x, acc[h]);
+                        acc[h] = fmaf(qv.y, kv[u].y, acc[h]);
+                        acc[h] = fmaf(qv.z, kv[u].z, acc[h]);
+                        acc[h] = fmaf(qv.w, kv[u].w, acc[h]);
+                    }
                 }
             }
         }
@@ -294,17 +300,29 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnArgs 
     for (int h = 0; h < kAttnMaxRep; ++h)
 #pragma unroll
         for (int u = 0; u < kAttnMaxHd / 32; ++u) o[h][u] = 0.0f;
-    for (int j = warp; j < np; j += nwarps) {
-        const float* vr = V + (size_t)(p0 + j) * hd;
-        float vv[kAttnMaxHd / 32];
+    // Four positions per pass, their V rows loaded together; the FMAs then go
+    // in position order, as one position per pass would.
+    constexpr int kVPass = 4;
+    for (int j0 = warp; j0 < np; j0 += kVPass * nwarps) {
+        float vv[kVPass][kAttnMaxHd / 32];
 #pragma unroll
-        for (int u = 0; u < kAttnMaxHd / 32; ++u) vv[u] = u < du ? vr[lane + 32 * u] : 0.0f;
+        for (int i = 0; i < kVPass; ++i) {
+            const int j = j0 + i * nwarps;
+            const float* vr = V + (size_t)(p0 + min(j, np - 1)) * hd;
 #pragma unroll
-        for (int h = 0; h < kAttnMaxRep; ++h) {
-            if (h >= rep) break;
-            const float e = ps[h * kAttnChunk + j];
+            for (int u = 0; u < kAttnMaxHd / 32; ++u) vv[i][u] = u < du ? vr[lane + 32 * u] : 0.0f;
+        }
 #pragma unroll
-            for (int u = 0; u < kAttnMaxHd / 32; ++u) o[h][u] = fmaf(e, vv[u], o[h][u]);
+        for (int i = 0; i < kVPass; ++i) {
+            const int j = j0 + i * nwarps;
+            if (j >= np) break;   // warp-uniform
+#pragma unroll
+            for (int h = 0; h < kAttnMaxRep; ++h) {
+                if (h >= rep) break;
+                const float e = ps[h * kAttnChunk + j];
+#pragma unroll
+                for (int u = 0; u < kAttnMaxHd / 32; ++u) o[h][u] = fmaf(e, vv[i][u], o[h][u]);
+            }
         }
     }
     // Sum over warps through shared memory.

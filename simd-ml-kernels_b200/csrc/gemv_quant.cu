@@ -79,6 +79,44 @@ __device__ __forceinline__ float4 load_act4(const float* xr, const float* ur, si
     return ur ? silu_mul4(load_x4(xr + k), load_x4(ur + k)) : load_x4(xr + k);
 }
 
+// ---- RMSNorm fused into the quantization (the reference's rms_norm,
+// examples/llama/llama.py:184-188, in add_rmsnorm_kernel's arithmetic) ----
+
+// Σ over the CTA of each thread's partial: a shuffle tree per warp, then the
+// warps' sums in warp order, the same order in every CTA of a launch (so
+// every CTA derives the same scale). All threads call it; all get the sum.
+__device__ __forceinline__ float cta_sum(float v) {
+    __shared__ float red[32];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+    __syncthreads();   // red may still be read by a previous call's threads
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float s = 0.0f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) s = __fadd_rn(s, red[w]);
+    return s;
+}
+// fl(1 / sqrt(fl(ss / n) + eps)), the root and quotient in double.
+__device__ __forceinline__ float rms_inv(float ss, int n, double eps) {
+    return (float)(1.0 / sqrt((double)__fdiv_rn(ss, (float)n) + eps));
+}
+__device__ __forceinline__ float sq_sum4(float4 v) {
+    return __fadd_rn(__fadd_rn(__fmul_rn(v.x, v.x), __fmul_rn(v.y, v.y)),
+                     __fadd_rn(__fmul_rn(v.z, v.z), __fmul_rn(v.w, v.w)));
+}
+// h = w · (v · inv), each product rounded.
+__device__ __forceinline__ float4 norm4(float4 v, const float* w, float inv) {
+    const float4 g = load_x4(w);
+    return make_float4(__fmul_rn(g.x, __fmul_rn(v.x, inv)), __fmul_rn(g.y, __fmul_rn(v.y, inv)),
+                       __fmul_rn(g.z, __fmul_rn(v.z, inv)), __fmul_rn(g.w, __fmul_rn(v.w, inv)));
+}
+// inv of row xr (n values, n % 4 == 0) read by the whole CTA, quads strided over its threads.
+__device__ __forceinline__ float cta_row_rms_inv(const float* xr, int n, double eps) {
+    float ss = 0.0f;
+    for (int i = threadIdx.x * 4; i < n; i += blockDim.x * 4) ss = __fadd_rn(ss, sq_sum4(load_x4(xr + i)));
+    return rms_inv(cta_sum(ss), n, eps);
+}
+
 // One thread's 4 values of a 32-value block, quantized to Q8: all 32 lanes of
 // the warp call this together (full-mask shuffles; the xor offsets stay inside
 // each 8-lane group of one block).
@@ -160,10 +198,13 @@ __device__ __forceinline__ void quantize_x_block(float4 v, int gq, bool valid, c
 // nthreads a multiple of 32. Warp w takes blocks 4w .. 4w+3 (one per 8-lane
 // group), then the next 4·warps, so every lane of a warp runs every
 // iteration. MT: rows of x known at compile time (0: xg.M).
+// nw != nullptr: each row RMS-normalised first (the whole CTA computes the
+// row's scale: every thread of the CTA must call this).
 template <int MT>
 __device__ __forceinline__ void quantize_x_rows(const float* __restrict__ x, long long ldx,
                                                 const float* __restrict__ up, long long ldu, const XGeom& xg,
-                                                uint8_t* xb, int tid, int nthreads) {
+                                                uint8_t* xb, int tid, int nthreads, const float* nw = nullptr,
+                                                double neps = 0.0) {
     const int gq = tid & 7, grp = (tid & 31) >> 3;
     const int wstride = (nthreads >> 5) * 4, nb = xg.nb;
     const int rows = MT > 0 ? MT : xg.M;
@@ -172,12 +213,14 @@ __device__ __forceinline__ void quantize_x_rows(const float* __restrict__ x, lon
         if (m >= rows) break;
         const float* xr = x + (size_t)m * ldx + gq * 4;
         const float* ur = up ? up + (size_t)m * ldu + gq * 4 : nullptr;
+        const float inv = nw ? cta_row_rms_inv(x + (size_t)m * ldx, nb * kQK, neps) : 0.0f;
         for (int wbase = (tid >> 5) * 4; wbase < nb; wbase += kXUnroll * wstride) {
             float4 v[kXUnroll];
 #pragma unroll
             for (int u = 0; u < kXUnroll; ++u) {
                 const int b = wbase + u * wstride + grp;
                 v[u] = b < nb ? load_act4(xr, ur, (size_t)b * kQK) : make_float4(0.f, 0.f, 0.f, 0.f);
+                if (nw && b < nb) v[u] = norm4(v[u], nw + (size_t)b * kQK + gq * 4, inv);
             }
 #pragma unroll
             for (int u = 0; u < kXUnroll; ++u) {
@@ -191,10 +234,12 @@ __device__ __forceinline__ void quantize_x_rows(const float* __restrict__ x, lon
 
 __global__ void __launch_bounds__(kThreadsQuantX) quantize_x_kernel(const float* __restrict__ x, long long ldx,
                                                                      const float* __restrict__ up, long long ldu,
-                                                                     XGeom xg, uint8_t* xq) {
+                                                                     XGeom xg, uint8_t* xq, const float* nw,
+                                                                     double neps) {
     pdl_launch_dependents();
     pdl_wait_primary();   // x comes from the previous kernel; xq may still be read by it
-    quantize_x_rows<0>(x, ldx, up, ldu, xg, xq, blockIdx.x * blockDim.x + threadIdx.x, gridDim.x * blockDim.x);
+    quantize_x_rows<0>(x, ldx, up, ldu, xg, xq, blockIdx.x * blockDim.x + threadIdx.x, gridDim.x * blockDim.x, nw,
+                       neps);
 }
 
 __global__ void __launch_bounds__(256) silu_mul_kernel(long long n, const float* __restrict__ g,
@@ -478,17 +523,20 @@ __device__ __forceinline__ void gather_send(const QGemvParams& p, int M, int TR,
     const GatherStep gs = gather_step(ga);
     const long long cols = (long long)ga->world * ga->npad;
     const int per = M * TR;
-    for (int tile = end - step; tile >= lo; tile -= step) {
-        for (int e = lane; e < per; e += 32) {
-            const int m = e / TR, row = tile * TR + (e - m * TR);
-            if (row < p.N) {
-                const float v = p.y[(size_t)m * p.ldy + row];
-                const long long o = gs.off + m * cols + row;
-                ga->y[o] = v;
-                const unsigned long long w = tagged_word(v, gs.tag);
-                for (int rk = 0; rk < ga->world; ++rk)
-                    if (rk != ga->rank) st_relaxed_sys_u64(ga->ll[rk] + o, w);
-            }
+    // Entries (tile, output row, tile row) of every finished tile spread over
+    // the lanes, so that their loads are in flight together (a tile of one row
+    // would otherwise leave 31 lanes idle and the tiles one L2 trip apart).
+    const int first = end - step, ntiles = first >= lo ? (first - lo) / step + 1 : 0;
+    for (int i = lane; i < ntiles * per; i += 32) {
+        const int ti = i / per, e = i - ti * per, tile = first - ti * step;
+        const int m = e / TR, row = tile * TR + (e - m * TR);
+        if (row < p.N) {
+            const float v = p.y[(size_t)m * p.ldy + row];
+            const long long o = gs.off + m * cols + row;
+            ga->y[o] = v;
+            const unsigned long long w = tagged_word(v, gs.tag);
+            for (int rk = 0; rk < ga->world; ++rk)
+                if (rk != ga->rank) st_relaxed_sys_u64(ga->ll[rk] + o, w);
         }
     }
 }
@@ -543,7 +591,7 @@ __device__ __forceinline__ void gemv_q_fast_body(const QGemvParams& p) {
     if (p.gather) pdl_launch_dependents();
     if constexpr (!kXGlobal) {
         const XGeom xg{M, p.nb, p.log2G, p.ksteps, 0};
-        quantize_x_rows<M>(p.x, p.ldx, p.up, p.ldu, xg, xs, threadIdx.x, blockDim.x);
+        quantize_x_rows<M>(p.x, p.ldx, p.up, p.ldu, xg, xs, threadIdx.x, blockDim.x, p.nw, p.neps);
         __syncthreads();
     }
     const uint8_t* xb = kXGlobal ? p.xq : xs;
@@ -587,7 +635,8 @@ __device__ __forceinline__ void gemv_q_fast_body(const QGemvParams& p) {
             for (int m = 0; m < M; ++m) {
                 float v = acc[m];
                 for (int o = p.G >> 1; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-                if (g == 0 && row < p.N) p.y[(size_t)m * p.ldy + row] = v;
+                if (g == 0 && row < p.N)
+                    p.y[(size_t)m * p.ldy + row] = p.res ? __fadd_rn(p.res[(size_t)m * p.ldr + row], v) : v;
                 acc[m] = 0.0f;
             }
         }
@@ -899,7 +948,7 @@ __device__ __forceinline__ void gemv_q4_r4_body(const QGemvParams& p) {
         if (p.ksteps == 1 && blockDim.x == 512) {
             // 64 blocks × 8 threads: one quad of x per thread, loaded first.
             const int gq = threadIdx.x & 7, b = threadIdx.x >> 3;
-            const float4 v = load_act4(p.x, p.up, (size_t)b * kQK + gq * 4);
+            float4 v = load_act4(p.x, p.up, (size_t)b * kQK + gq * 4);
             if (nitems > 0) {
                 const bool ok = mbar_wait_bounded(&bars[0], 0, p.err);
                 have_pre = __all_sync(0xffffffffu, ok);
@@ -909,9 +958,12 @@ __device__ __forceinline__ void gemv_q4_r4_body(const QGemvParams& p) {
                     for (int i = 0; i < kR4PreRows * 9; ++i) pre[i] = wp[(i / 9) * 288 + i % 9];
                 }
             }
+            // Fused RMSNorm: the row's sum of squares from the quads in the
+            // threads' registers (the whole row: 512 threads × 4 values).
+            if (p.nw) v = norm4(v, p.nw + (size_t)b * kQK + gq * 4, rms_inv(cta_sum(sq_sum4(v)), p.K, p.neps));
             quantize_x_block(v, gq, true, xg, 0, b, xs);
         } else {
-            quantize_x_rows<1>(p.x, p.ldx, p.up, p.ldu, xg, xs, threadIdx.x, blockDim.x);
+            quantize_x_rows<1>(p.x, p.ldx, p.up, p.ldu, xg, xs, threadIdx.x, blockDim.x, p.nw, p.neps);
         }
         __syncthreads();
     }
@@ -940,7 +992,7 @@ __device__ __forceinline__ void gemv_q4_r4_body(const QGemvParams& p) {
         if (cur.ks == p.ksteps - 1) {
             const float v = r4_reduce(acc, lane);
             const int row = cur.tile * 4 + r;
-            if (g == 0 && row < p.N) p.y[row] = v;
+            if (g == 0 && row < p.N) p.y[row] = p.res ? __fadd_rn(p.res[row], v) : v;
 #pragma unroll
             for (int k = 0; k < 4; ++k) acc[k] = 0.0f;
         }
@@ -1618,7 +1670,7 @@ cudaError_t launch_quantize_x(const LaunchCfg& c, const QGemvParams& p, uint8_t*
                                                (long long)c.num_sms * 4);
     const XGeom xg{p.M, p.nb, p.log2G, p.ksteps, p.r4};
     return launch(quantize_x_kernel, dim3((unsigned)std::max<long long>(grid, 1)), dim3(kThreadsQuantX), 0, c, p.x,
-                  p.ldx, p.up, p.ldu, xg, xq);
+                  p.ldx, p.up, p.ldu, xg, xq, p.nw, p.neps);
 }
 
 cudaError_t launch_stage_x(cudaStream_t s, const float* src, float* dst, long long n, int num_sms) {

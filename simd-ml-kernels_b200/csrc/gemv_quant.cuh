@@ -84,6 +84,15 @@ struct QGemvParams {
     const uint8_t* xq;     // quantized x in global memory (nullptr: each CTA quantizes into shared memory)
     int32_t* dump;         // test-only: per-block integer sums [M, N, nb], or nullptr
     unsigned* err;         // device error word
+    // The decode step's neighbours fused in (fast kernels): nw != nullptr:
+    // each row of x is RMS-normalised and scaled by nw before it is quantized,
+    // h = nw · (x · fl(1/sqrt(fl(Σx²/K) + neps))) (the reference's rms_norm);
+    // res != nullptr: y = fl(res + x·Wᵀ), rows ldr apart (res may be y: the
+    // residual stream updated in place, each value read and written by one lane).
+    const float* nw;
+    double neps;
+    const float* res;
+    long long ldr;
 };
 
 // All-gather of y fused into the fast kernel's epilogue (row-sharded GEMV,

@@ -208,6 +208,7 @@ struct smk_ctx {
     // Synchronous quantized GEMVs repeated with the same operands replay a
     // CUDA graph of their copy and kernel (guarded by mu_stage).
     bool host_graphs = true;
+    bool dense_mma = true;   // SMK_OPT_DENSE_MMA: bf16 weights at 4..8 rows on the tensor-core kernel
     cudaStream_t capture_stream = nullptr;   // non-blocking: captures never touch the legacy stream
     std::unordered_map<HostKey, HostGraph, HostKeyHash> graphs;
     unsigned long long host_calls = 0;
@@ -296,7 +297,8 @@ QPlan plan_q(smk_ctx* c, smk::LaunchCfg* l, smk_qformat fmt, int M, int N, int K
 smk_status run_q(smk_ctx* c, smk_qformat fmt, int M, int N, int K, const float* x, int64_t ldx, const uint8_t* Wq,
                  float* y, int64_t ldy, cudaStream_t s, int32_t* dump,
                  const smk::GatherArgs* gather = nullptr, const float* up = nullptr, int64_t ldu = 0,
-                 float* yhost = nullptr, bool force_pdl = false) {
+                 float* yhost = nullptr, bool force_pdl = false, const float* nw = nullptr, double neps = 0.0,
+                 const float* res = nullptr, int64_t ldr = 0) {
     // yhost: the device-mapped address of a page-locked output. The fast
     // kernel then writes y (device memory, same ldy) and copies it there at
     // its end; the other kernels write yhost directly.
@@ -309,7 +311,9 @@ smk_status run_q(smk_ctx* c, smk_qformat fmt, int M, int N, int K, const float* 
     }
     smk::LaunchCfg l = cfg_for(c, s);
     if (force_pdl) l.pdl = true;   // the previous kernel writes x only (a host call's stage_x_kernel)
-    if (!gather && M >= smk::kMmaMinRows && !dump && K % 256 == 0 && (reinterpret_cast<uintptr_t>(Wq) & 15) == 0) {
+    const bool fused = nw || res;   // RMSNorm before / residual add after: the fast kernels only
+    if (!gather && !fused && M >= smk::kMmaMinRows && !dump && K % 256 == 0 &&
+        (reinterpret_cast<uintptr_t>(Wq) & 15) == 0) {
         // Several rows of x: integer tensor-core kernel (bitwise the reference's
         // scalar order), x quantized once into scratch by its own kernel.
         smk::QGemvParams p = {};
@@ -369,6 +373,11 @@ smk_status run_q(smk_ctx* c, smk_qformat fmt, int M, int N, int K, const float* 
     q.p.gather = gather;
     q.p.up = up;
     q.p.ldu = ldu;
+    q.p.nw = nw;
+    q.p.neps = neps;
+    q.p.res = res;
+    q.p.ldr = ldr;
+    if (fused && !q.fast) return fail(SMK_ERR_ARGUMENT, "the fused norm / residual needs K %% 256 == 0 and 16-byte aligned Wq");
     if (yhost) {
         if (q.fast) {
             q.p.yhost = yhost;
@@ -471,6 +480,7 @@ smk_status smk_ctx_set(smk_ctx* c, int option, long long v) {
     }
     switch (option) {
         case SMK_OPT_HOST_GRAPHS: c->host_graphs = v != 0; return SMK_OK;
+        case SMK_OPT_DENSE_MMA: c->dense_mma = v != 0; return SMK_OK;
         case SMK_OPT_PDL: c->pdl = v != 0; return SMK_OK;
         case SMK_OPT_WARPS:
             if (v < 0 || v > 16) return fail(SMK_ERR_ARGUMENT, "warps must be in 0..16 (0: automatic)");
@@ -501,6 +511,7 @@ smk_status smk_ctx_get(smk_ctx* c, int option, long long* v) {
         case SMK_OPT_CTAS_PER_SM: *v = c->ctas_per_sm; return SMK_OK;
         case SMK_OPT_TILE_ORDER: *v = c->tile_order; return SMK_OK;
         case SMK_OPT_HOST_GRAPHS: *v = c->host_graphs; return SMK_OK;
+        case SMK_OPT_DENSE_MMA: *v = c->dense_mma; return SMK_OK;
         default: return fail(SMK_ERR_ARGUMENT, "unknown option %d", option);
     }
 }
@@ -729,6 +740,32 @@ smk_status smk_gemv_q_silu_mul(smk_ctx* c, smk_qformat fmt, int M, int N, int K,
     DeviceGuard g(c->device);
     if (!g.ok) return fail(SMK_ERR_CUDA, "cudaSetDevice(%d) failed", c->device);
     return run_q(c, fmt, M, N, K, gate, ldg, Wq, y, ldy, static_cast<cudaStream_t>(stream), nullptr, nullptr, up, ldu);
+}
+
+smk_status smk_gemv_q_fused(smk_ctx* c, smk_qformat fmt, int M, int N, int K, const float* x, int64_t ldx,
+                            const float* up, int64_t ldu, const float* w_norm, double eps, const uint8_t* Wq,
+                            const float* r, int64_t ldr, float* y, int64_t ldy, void* stream) {
+    if (!c) return fail(SMK_ERR_ARGUMENT, "ctx must not be NULL");
+    smk_status st = check_q_args(fmt, M, N, K);
+    if (st != SMK_OK) return st;
+    if (M == 0 || N == 0) return SMK_OK;
+    if (up && w_norm) return fail(SMK_ERR_ARGUMENT, "the SwiGLU input and the RMSNorm cannot be fused together");
+    if (K == 0) return fail(SMK_ERR_ARGUMENT, "the fused forms need K > 0");
+    if (!y || !x || !Wq) return fail(SMK_ERR_ARGUMENT, "x, Wq and y must not be NULL");
+    if (ldy < N || ldx < K || (up && ldu < K) || (r && ldr < N))
+        return fail(SMK_ERR_ARGUMENT, "ldx, ldu >= K and ldy, ldr >= N required");
+    if (w_norm && !(eps >= 0.0)) return fail(SMK_ERR_ARGUMENT, "eps must be >= 0");
+    if (r && r != y) {
+        // In place (r == y) each value is read and written by one lane; other
+        // overlaps would race.
+        const char *rb = reinterpret_cast<const char*>(r), *re = rb + ((size_t)(M - 1) * ldr + N) * 4;
+        const char *yb = reinterpret_cast<const char*>(y), *ye = yb + ((size_t)(M - 1) * ldy + N) * 4;
+        if (rb < ye && yb < re) return fail(SMK_ERR_ARGUMENT, "r must be y itself or not overlap it");
+    }
+    DeviceGuard g(c->device);
+    if (!g.ok) return fail(SMK_ERR_CUDA, "cudaSetDevice(%d) failed", c->device);
+    return run_q(c, fmt, M, N, K, x, ldx, Wq, y, ldy, static_cast<cudaStream_t>(stream), nullptr, nullptr, up, ldu,
+                 nullptr, false, w_norm, eps, r, ldr);
 }
 
 smk_status smk_silu_mul(smk_ctx* c, int64_t n, const float* gate, const float* up, float* out, void* stream) {
@@ -992,12 +1029,23 @@ smk_status smk_gemv_dense(smk_ctx* c, smk_dtype wt, smk_dtype xt, int M, int N, 
     if (ldc < N || (K > 0 && (ldx < K || ldw < K))) return fail(SMK_ERR_ARGUMENT, "leading dimensions too small");
     DeviceGuard g(c->device);
     if (!g.ok) return fail(SMK_ERR_CUDA, "cudaSetDevice(%d) failed", c->device);
-    smk::DenseParams p;
+    smk::DenseParams p = {};
     p.x = X; p.ldx = ldx; p.w = W; p.ldw = ldw; p.y = C; p.ldy = ldc;
     p.M = M; p.N = N; p.K = K; p.alpha = alpha; p.beta = beta;
     p.err = c->d_err;
-    SMK_CUDA(smk::launch_gemv_dense(static_cast<cudaStream_t>(stream), c->pdl, c->num_sms, (int)wt, (int)xt, p),
-             "dense gemv launch");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const size_t need = c->dense_mma ? smk::dense_mma_scratch((int)wt, (int)xt, M, K, ldw, W) : 0;
+    if (need) {   // bf16 weights, several rows of x: the tensor-core kernel and its x split in scratch
+        {
+            std::lock_guard<std::mutex> lock(c->mu_scratch);
+            DevBuf& b = c->scratch[s];
+            SMK_CUDA(b.reserve(need), "cudaMalloc (scratch)");
+            p.xfrag = b.ptr;
+        }
+        SMK_CUDA(smk::launch_gemv_dense_mma(s, c->pdl, c->num_sms, (int)xt, p), "dense tensor-core gemv launch");
+        return SMK_OK;
+    }
+    SMK_CUDA(smk::launch_gemv_dense(s, c->pdl, c->num_sms, (int)wt, (int)xt, p), "dense gemv launch");
     return SMK_OK;
 }
 

@@ -24,6 +24,9 @@ device, embedding rows).
 from __future__ import annotations
 
 import os as _os
+import sys as _sys
+
+from numpy import ndarray as _np_ndarray
 
 from . import _core
 from ._core import ArgumentError, DTypeError
@@ -64,8 +67,7 @@ def library_path() -> str:
 # ---- torch CUDA tensors --------------------------------------------------------
 
 def _torch():
-    import sys
-    return sys.modules.get("torch")
+    return _sys.modules.get("torch")
 
 
 def _is_cuda_tensor(a) -> bool:
@@ -193,7 +195,7 @@ def _gemv(fmt, core_fn, x, Wq, N, K, out, batched):
     """x a CUDA tensor: validated here, then queued on torch's current stream;
     returns a CUDA tensor. x in host memory: the reference's synchronous
     contract (weights may be device-resident); returns NumPy."""
-    if _is_cuda_tensor(x):
+    if type(x) is not _np_ndarray and _is_cuda_tensor(x):
         t = _torch()
         M = _check_dev_gemv(fmt, x, Wq, N, K, out, batched)
         if out is None:

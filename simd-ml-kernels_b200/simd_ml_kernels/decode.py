@@ -11,14 +11,20 @@ Functions (CUDA tensors, queued on torch's current stream):
     attention_decode(q, k_cache, v_cache, length, nkv, out=None)
     rope_attention(qkv, inv_freq, pos, nh, nkv, hd, k_cache, v_cache, out=None, interleaved=False)
                                                      the two above as one kernel
+    gemv_rmsnorm(x, w_norm, eps, Wq, N, K, fmt="q4_0", out=None)
+                                                     (RMSNorm(x) * w_norm) @ W.T in one GEMV
+    gemv_residual(x, Wq, N, K, r, fmt="q4_0", up=None)
+                                                     r += x @ W.T (or silu(x) * up) in one GEMV
     rope_inv_freq(head_dim, theta, scaling=None)     the frequencies (float32, host)
 
 `LlamaDecoder` holds one model's weights on the device (Q4_0 or Q8_0 blocks,
 q/k/v and gate/up as concatenated row groups), its KV cache and buffers, and
-runs `step(token)`: the embedding row, per layer RMSNorm -> qkv GEMV -> RoPE +
-cache write + attention (one kernel) -> o GEMV -> residual RMSNorm -> gate/up
-GEMV -> down GEMV on silu(gate)*up, then the final norm and the LM-head GEMV.
-Every launch is asynchronous, so a run of steps can be captured in a CUDA graph.
+runs `step(token)`: the embedding row, then per layer five launches: the q/k/v
+GEMV with the attention RMSNorm in its x quantization, RoPE + cache write +
+attention, the o GEMV adding into the residual stream, the gate/up GEMV with
+the MLP RMSNorm, and the down GEMV on silu(gate)*up adding into the residual
+stream; then the LM-head GEMV with the final norm. Every launch is
+asynchronous, so a run of steps can be captured in a CUDA graph.
 """
 
 from __future__ import annotations
@@ -135,6 +141,49 @@ def rope_attention(qkv, inv_freq, pos: int, nh: int, nkv: int, hd: int, k_cache,
                           int(interleaved), k_cache.data_ptr(), v_cache.data_ptr(), cap, s, out.data_ptr(),
                           _stream(qkv), _dev(qkv))
     return out
+
+
+def _fmt_code(fmt: str) -> int:
+    if fmt not in ("q4_0", "q8_0"):
+        raise ValueError("fmt must be 'q4_0' or 'q8_0'")
+    return 0 if fmt == "q4_0" else 1
+
+
+def gemv_rmsnorm(x, w_norm, eps: float, Wq, N: int, K: int, fmt: str = "q4_0", out=None):
+    """y = (RMSNorm(x) * w_norm) @ W.T for x [K] or [M, K]: the reference's
+    rms_norm applied to each row inside the GEMV's x quantization (one launch,
+    x unchanged). y [N] or [M, N]."""
+    torch = _torch()
+    _check(x, "x", torch.float32)
+    _check(w_norm, "w_norm", torch.float32)
+    M = 1 if x.dim() == 1 else x.shape[0]
+    if x.shape[-1] != K or w_norm.numel() != K:
+        raise ValueError("x rows and w_norm must hold K values")
+    if out is None:
+        out = torch.empty((N,) if x.dim() == 1 else (M, N), dtype=torch.float32, device=x.device)
+    _check(out, "out", torch.float32)
+    _core._gemv_q_fused(_fmt_code(fmt), M, N, K, x.data_ptr(), K, 0, 0, w_norm.data_ptr(), float(eps),
+                        Wq.data_ptr(), 0, 0, out.data_ptr(), N, _stream(x), _dev(x))
+    return out
+
+
+def gemv_residual(x, Wq, N: int, K: int, r, fmt: str = "q4_0", up=None):
+    """r += x @ W.T (or (silu(x) * up) @ W.T when up is given) for x [K] or
+    [M, K] and r [N] or [M, N]: the residual add of the reference's decoder
+    step fused into the GEMV's store, in place. Returns r."""
+    torch = _torch()
+    _check(x, "x", torch.float32)
+    _check(r, "r", torch.float32)
+    M = 1 if x.dim() == 1 else x.shape[0]
+    if x.shape[-1] != K or r.numel() != M * N:
+        raise ValueError("x rows must hold K values and r M * N")
+    if up is not None:
+        _check(up, "up", torch.float32)
+        if up.shape != x.shape:
+            raise ValueError("up must match x")
+    _core._gemv_q_fused(_fmt_code(fmt), M, N, K, x.data_ptr(), K, 0 if up is None else up.data_ptr(), K, 0, 0.0,
+                        Wq.data_ptr(), r.data_ptr(), N, r.data_ptr(), N, _stream(x), _dev(x))
+    return r
 
 
 def rope_inv_freq(head_dim: int, theta: float, scaling: dict | None = None) -> np.ndarray:
@@ -278,24 +327,19 @@ class LlamaDecoder:
             raise ValueError(f"KV cache full ({self.cap} positions)")
         nh, nkv, hd = s.heads, s.kv_heads, s.head_dim
         self._embed(token)
-        delta = None
+        fmt, H, F = w.fmt, s.hidden, s.ffn
         for li, L in enumerate(w.layers):
-            add_rmsnorm(b.x, L.attn_norm, s.eps, delta=delta, out=b.h)
-            self._gemv(b.h, L.qkv, b.qkv.numel(), s.hidden, out=b.qkv)
+            gemv_rmsnorm(b.x, L.attn_norm, s.eps, L.qkv, b.qkv.numel(), H, fmt, out=b.qkv)
             rope_attention(b.qkv, self.inv_freq, pos, nh, nkv, hd, b.k_cache[li], b.v_cache[li], out=b.att,
                            interleaved=self.interleaved, max_len=self.cap)
-            self._gemv(b.att.reshape(-1), L.o, s.hidden, nh * hd, out=b.delta)
-            add_rmsnorm(b.x, L.mlp_norm, s.eps, delta=b.delta, out=b.h)
-            self._gemv(b.h, L.gate_up, 2 * s.ffn, s.hidden, out=b.gate_up)
-            self._gemv_silu(b.gate_up[:s.ffn], b.gate_up[s.ffn:], L.down, s.hidden, s.ffn, out=b.delta)
-            delta = b.delta
+            gemv_residual(b.att.reshape(-1), L.o, H, nh * hd, b.x, fmt)
+            gemv_rmsnorm(b.x, L.mlp_norm, s.eps, L.gate_up, 2 * F, H, fmt, out=b.gate_up)
+            gemv_residual(b.gate_up[:F], L.down, H, F, b.x, fmt, up=b.gate_up[F:])
         self.pos = pos + 1
         if not logits:
-            add_rmsnorm(b.x, w.norm, s.eps, delta=delta, out=b.h)
             return None
-        add_rmsnorm(b.x, w.norm, s.eps, delta=delta, out=b.h)
-        self._gemv(b.h, w.lm_head, s.vocab, s.hidden, out=b.logits)
+        gemv_rmsnorm(b.x, w.norm, s.eps, w.lm_head, s.vocab, H, fmt, out=b.logits)
         return b.logits
 
     def launches_per_token(self) -> int:
-        return 1 + 7 * self.shape.layers + 2
+        return 1 + 5 * self.shape.layers + 1

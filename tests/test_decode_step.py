@@ -180,6 +180,58 @@ def test_rope_attention_host_errors(torch):
         dec.rope_attention(qkv, inv, 5, 4, 1, 32, kc, kc.clone(), max_len=4)
 
 
+@pytest.mark.gpu
+@pytest.mark.parametrize("fmt", ["q4_0", "q8_0"])
+@pytest.mark.parametrize("N,K", [(3072, 2048), (2048, 2048), (1000, 4096), (2048, 8192), (128256, 2048)])
+def test_gemv_rmsnorm_equals_unfused(torch, fmt, N, K):
+    """The RMSNorm fused into the GEMV's x quantization gives the bits of
+    add_rmsnorm followed by the GEMV. x holds small integers, so the sum of
+    squares is exact in any order and both paths see the same normalised row;
+    the shapes reach the four-row kernel (K = 2048), the superblock kernel and x
+    quantized once in global memory (K = 8192)."""
+    import simd_ml_kernels as sk
+    rng = np.random.default_rng(N + K)
+    x = rng.integers(-8, 9, K).astype(np.float32)
+    w = (1 + 0.1 * rng.standard_normal(K)).astype(np.float32)
+    W = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    quant = sk.quantize_q4_0 if fmt == "q4_0" else sk.quantize_q8_0
+    gemv = sk.gemv_q4_0 if fmt == "q4_0" else sk.gemv_q8_0
+    Wq = quant(torch.from_numpy(W).cuda()).reshape(-1)
+    xd, wd = torch.from_numpy(x).cuda(), torch.from_numpy(w).cuda()
+    got = dec.gemv_rmsnorm(xd, wd, 1e-5, Wq, N, K, fmt).cpu().numpy()
+    h = dec.add_rmsnorm(xd.clone(), wd, 1e-5)
+    want = gemv(h, Wq, N, K).cpu().numpy()
+    np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32))
+    assert torch.equal(xd, torch.from_numpy(x).cuda())   # x is not modified
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("fmt", ["q4_0", "q8_0"])
+@pytest.mark.parametrize("N,K", [(2048, 2048), (2048, 8192), (1000, 4096)])
+def test_gemv_residual_equals_unfused(torch, fmt, N, K):
+    """The residual add fused into the GEMV's store: r += x @ W.T in place,
+    and r += (silu(gate) * up) @ W.T, each bitwise fl(r + the plain GEMV)."""
+    import simd_ml_kernels as sk
+    rng = np.random.default_rng(3 * N + K)
+    x = rng.standard_normal(K).astype(np.float32)
+    up = rng.standard_normal(K).astype(np.float32)
+    r0 = rng.standard_normal(N).astype(np.float32)
+    W = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    quant = sk.quantize_q4_0 if fmt == "q4_0" else sk.quantize_q8_0
+    gemv = sk.gemv_q4_0 if fmt == "q4_0" else sk.gemv_q8_0
+    silu = sk.gemv_q4_0_silu_mul if fmt == "q4_0" else sk.gemv_q8_0_silu_mul
+    Wq = quant(torch.from_numpy(W).cuda()).reshape(-1)
+    xd, ud = torch.from_numpy(x).cuda(), torch.from_numpy(up).cuda()
+    r = torch.from_numpy(r0).cuda()
+    dec.gemv_residual(xd, Wq, N, K, r, fmt)
+    want = torch.from_numpy(r0).cuda() + gemv(xd, Wq, N, K)
+    assert torch.equal(r.view(torch.int32), want.view(torch.int32))
+    r2 = torch.from_numpy(r0).cuda()
+    dec.gemv_residual(xd, Wq, N, K, r2, fmt, up=ud)
+    want2 = torch.from_numpy(r0).cuda() + silu(xd, ud, Wq, N, K)
+    assert torch.equal(r2.view(torch.int32), want2.view(torch.int32))
+
+
 def _small_model(torch, fmt, seed=11, interleaved=False):
     import simd_ml_kernels as sk
     sh = dec.LlamaShape(hidden=256, layers=2, heads=4, kv_heads=2, head_dim=64, ffn=512, vocab=512, eps=1e-5)

@@ -715,6 +715,66 @@ def test_dense_bf16_special_values(sk, torch):
         assert (np.abs(Y[m:m + 1] - y64) <= bound).all(), f"row {m}"
 
 
+@pytest.mark.parametrize("xtype", ["float32", "bfloat16"])
+@pytest.mark.parametrize("M,N,K", [(4, 4096, 4096), (8, 1003, 512), (5, 37, 128), (8, 14336, 1024), (6, 200, 8192)])
+def test_dense_bf16_tensor_core_kernel(sk, torch, xtype, M, N, K):
+    """bfloat16 weights with 4..8 rows of x take the tensor-core kernel (x split
+    exactly into bf16 parts; one part when x is bfloat16 itself). Against the
+    float64 sums within the reference's dense bound, for tile counts that split
+    K over the warps (small N) and N not a multiple of 16, and the same call on
+    the CUDA-core kernel (SMK_OPT_DENSE_MMA = 0) within the same bound."""
+    from simd_ml_kernels import _core
+    rng = np.random.default_rng(M * 7 + N + K)
+    W32 = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    X = rng.standard_normal((M, K)).astype(np.float32)
+    Wbits = O.bf16_bits(W32)
+    if xtype == "float32":   # the device entry: fp32 x, bf16 W (torch tensors)
+        run = lambda: sk.gemv_dense(torch.from_numpy(X).cuda(), torch.from_numpy(W32).to(torch.bfloat16).cuda())  # noqa: E731
+        want, mag = O.dense_ref64(X, "f32", Wbits, "bf16")
+    else:   # the reference's sgemm_bf16: both operands bf16 (host arrays)
+        Xbits = O.bf16_bits(X)
+
+        def run():
+            C = np.zeros((M, N), np.float32)
+            sk.sgemm_bf16(Xbits, Wbits, C=C, trans_b=True)
+            return C
+        want, mag = O.dense_ref64(Xbits, "bf16", Wbits, "bf16")
+    bound = 2 * (K + 2) * U * mag + 1e-300
+    try:
+        for mma in (1, 0):
+            _core._ctx_set(7, mma)
+            got = run()
+            got = got.cpu().numpy() if hasattr(got, "cpu") else got
+            assert (np.abs(got - want) <= bound).all(), f"mma={mma}: max err/bound {np.max(np.abs(got - want) / bound):.3g}"
+    finally:
+        _core._ctx_set(7, 1)
+    assert _core._device_error(torch.cuda.current_stream().cuda_stream) == 0
+
+
+def test_dense_bf16_tensor_core_infinite_weight(sk, torch):
+    """An infinite weight meets x values whose lower bf16 parts are zero (x = 1,
+    2, 0.5 ...): the reference's single product gives ±inf, the tensor-core
+    kernel's low-part product 0·inf would give NaN, so that output is recomputed
+    in plain fp32 and comes out ±inf; a zero x next to an infinite weight gives
+    NaN in both."""
+    M, N, K = 4, 64, 256
+    rng = np.random.default_rng(5)
+    W32 = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    W32[3, 10] = np.inf
+    W32[7, 20] = -np.inf
+    X = np.round(rng.standard_normal((M, K)) * 4).astype(np.float32) / 4   # few significant bits
+    X[:, 10] = 2.0
+    X[:, 20] = 0.5
+    X[2, 20] = 0.0
+    Y = sk.gemv_dense(torch.from_numpy(X).cuda(), torch.from_numpy(W32).to(torch.bfloat16).cuda()).cpu().numpy()
+    assert (Y[:, 3] == np.inf).all()
+    assert (Y[[0, 1, 3], 7] == -np.inf).all() and np.isnan(Y[2, 7])
+    fin = np.ones(N, bool)
+    fin[[3, 7]] = False
+    y64, mag = O.dense_ref64(X, "f32", O.bf16_bits(W32[fin]), "bf16")
+    assert (np.abs(Y[:, fin] - y64) <= 2 * (K + 2) * U * mag + 1e-300).all()
+
+
 def test_dense_rejects_non_decode(sk):
     A = np.ones((9, 16), np.float32)
     B = np.ones((4, 16), np.float32)
