@@ -1081,6 +1081,83 @@ def cpu_arms(host: dict, extra: dict) -> dict:
     return out
 
 
+def profile_case(torch, args) -> dict:
+    """One GEMV shape on one GPU (--case KIND:M:N:K): weights N(0, 0.02) and x
+    N(0, 1) from torch's generator (seed 7) on the device, rotated copies past
+    2x L2, `--steps` chained calls after `--warmup`; what profilers capture."""
+    import simd_ml_kernels as sk
+    if args.case.startswith("llama-decode:"):
+        return profile_decode(torch, sk, int(args.case.split(":")[1]))
+    kind, M, N, K = args.case.split(":")
+    M, N, K = int(M), int(N), int(K)
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev).manual_seed(7)
+    W = torch.randn((N, K), generator=g, device=dev) * 0.02
+    X = torch.randn((M, K), generator=g, device=dev)
+    Y = torch.empty((M, N), device=dev)
+    if kind in ("q4_0", "q8_0"):
+        w = (sk.quantize_q4_0 if kind == "q4_0" else sk.quantize_q8_0)(W).reshape(-1)
+        batch = sk.gemv_q4_0_batch if kind == "q4_0" else sk.gemv_q8_0_batch
+        call = lambda w_: batch(X, w_, N, K, out=Y)   # noqa: E731
+        nbytes = gemv_bytes(q_bytes(kind, N, K), M, N, K)
+    else:
+        w = W.to(getattr(torch, kind))
+        call = lambda w_: sk.gemv_dense(X, w_, out=Y)   # noqa: E731
+        nbytes = N * K * w.element_size() + 4 * M * K + 4 * M * N
+    del W
+    l2 = torch.cuda.get_device_properties(dev).L2_cache_size
+    stream = torch.cuda.Stream(device=dev)
+    r = rotated_case(torch, dev, stream, w, call, nbytes, l2, measured_peaks(), n=args.steps)
+    return {"case": args.case, **r}
+
+
+def profile_decode(torch, sk, tokens: int) -> dict:
+    """--case llama-decode:T: T whole decode tokens of config 2's architecture
+    (LlamaDecoder) in one CUDA graph, on weights drawn on the device (torch,
+    seed 7, N(0, 0.02) -> Q4_0; norms 1 + N(0, 0.01)): a short launch list of
+    the decode step for profilers."""
+    from simd_ml_kernels import decode as D
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev).manual_seed(7)
+
+    def q(n, k):
+        return sk.quantize_q4_0(torch.randn((n, k), generator=g, device=dev) * 0.02).reshape(-1)
+
+    def norm():
+        return 1 + 0.1 * torch.randn(2048, generator=g, device=dev)
+
+    layers = [D.LlamaLayerWeights(attn_norm=norm(), qkv=q(3072, 2048), o=q(2048, 2048), mlp_norm=norm(),
+                                  gate_up=q(16384, 2048), down=q(2048, 8192)) for _ in range(LLAMA_LAYERS)]
+    emb = q(LLAMA_VOCAB, 2048)
+    shape = D.LlamaShape(hidden=2048, layers=LLAMA_LAYERS, heads=32, kv_heads=8, head_dim=64, ffn=8192,
+                         vocab=LLAMA_VOCAB, eps=1e-5)
+    inv = D.rope_inv_freq(64, 500000.0, {"factor": 32.0, "high_freq_factor": 4.0, "low_freq_factor": 1.0,
+                                         "original_max_position_embeddings": 8192, "rope_type": "llama3"})
+    dec = D.LlamaDecoder(shape, D.LlamaWeights(layers=layers, norm=norm(), embed=emb, lm_head=emb), inv,
+                         capacity=max(256, tokens))
+    stream = torch.cuda.Stream(device=dev)
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        dec.step(1)
+        dec.reset()
+        with torch.cuda.graph(gr, stream=stream):
+            for t in range(tokens):
+                dec.step((7919 * t + 13) % LLAMA_VOCAB)
+        dec.reset()
+        gr.replay()
+        dec.reset()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        gr.replay()
+        e.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = s.elapsed_time(e) / tokens
+    return {"case": f"llama-decode:{tokens}", "tok_s": round(1e3 / ms, 1), "ms_per_token": ms,
+            "launches_per_token": dec.launches_per_token()}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1093,6 +1170,9 @@ def main() -> None:
                     help="decode steps per Llama-stack CUDA graph (fewer: shorter profiler launch lists)")
     ap.add_argument("--only-gemv", action="store_true",
                     help="time the headline GEMV only (no other configs, e2e or CPU arms): for profilers")
+    ap.add_argument("--case", default=None,
+                    help="KIND:M:N:K (KIND q4_0, q8_0, float32, bfloat16 or float16): time that one GEMV on "
+                         "seeded device data instead of the bench, one GPU (for profilers)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -1123,6 +1203,9 @@ def main() -> None:
     import torch.distributed as dist
     from datetime import timedelta
 
+    if args.case:
+        print(json.dumps(profile_case(torch, args)))
+        return
     if world > 1:
         os.environ.setdefault("NCCL_DEBUG", "WARN")   # stdout carries only the JSON line
         torch.cuda.set_device(local_rank)

@@ -14,8 +14,9 @@
 // is x truncated to bf16, mid the remainder truncated, lo what is left, which
 // has at most 8 significant bits. Each part meets W in its own MMA, so every
 // product is exact and only the fp32 sums round (the dense bound of the
-// reference's tests, 2(K+2)·2^-24·Σ|x||w|). hi goes to one accumulator and
-// mid + lo to another, added once at the end. bf16 x is its own single part.
+// reference's tests, 2(K+2)·2^-24·Σ|x||w|). Each part has its own
+// accumulator (three independent MMA chains); mid + lo, then hi + that, at
+// the end. bf16 x is its own single part.
 //
 // Layout: a split kernel writes the parts once per call in B-fragment order
 // (dm_xfrag_bytes: per 16-value block kb, per part, 32 lanes × (two bf16x2
@@ -131,11 +132,14 @@ __device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
 }
 
 // d += A·B: A 16 × 16 bf16 (rows of W), B 16 × 8 bf16 (rows of x as columns), fp32.
+// A function of its register operands only (not volatile), so the compiler
+// schedules it by its dependencies; the shared-memory loads feeding it stay
+// ordered after the stage's barrier wait.
 __device__ __forceinline__ void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint2 b) {
-    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-                 "{%0,%1,%2,%3};"
-                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b.x), "r"(b.y));
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b.x), "r"(b.y));
 }
 
 struct DMGeom {
@@ -213,7 +217,8 @@ __global__ void __launch_bounds__(kDMWarps * 32, 1) gemv_dense_mma(const DensePa
     int failed = 0, c_slot = 0, consumed = 0;
     uint32_t c_phase = 0;
     for (int r = 0; r < rounds; ++r) {   // CTA-uniform: every warp meets every barrier
-        float hi[4] = {0.f, 0.f, 0.f, 0.f}, lo[4] = {0.f, 0.f, 0.f, 0.f};
+        // One accumulator per part: three independent MMA chains (hi, mid, lo).
+        float hi[4] = {0.f, 0.f, 0.f, 0.f}, mid[4] = {0.f, 0.f, 0.f, 0.f}, lo[4] = {0.f, 0.f, 0.f, 0.f};
         if (r < my_rounds) {
             for (int k = 0; k < nks && !failed; ++k) {
                 if (__any_sync(0xffffffffu, !mbar_wait_bounded(&bars[c_slot], c_phase, p.err))) {
@@ -222,14 +227,28 @@ __global__ void __launch_bounds__(kDMWarps * 32, 1) gemv_dense_mma(const DensePa
                 }
                 const uint32_t st = ring_w + (uint32_t)(c_slot * STAGE);
                 const uint2* xs = reinterpret_cast<const uint2*>(ring + (size_t)c_slot * STAGE + kDMWBytes);
+                // Four 16-value blocks at a time: their A fragments and x fragments
+                // loaded first, then their MMAs.
 #pragma unroll
-                for (int kb = 0; kb < 8; ++kb) {
-                    const int box = kb >> 2, chunk = 2 * (kb & 3) + (li >> 1);
-                    uint32_t a[4];
-                    ldsm_x4(a, st + (uint32_t)(box * 16 * kDMBox * 2 + wrow * kDMBox * 2 + ((chunk ^ (wrow & 7)) << 4)));
-                    mma_bf16(hi, a, xs[(kb * NP) * 32 + lane]);
+                for (int k4 = 0; k4 < 8; k4 += 4) {
+                    uint32_t a[4][4];
+                    uint2 bx[4][NP];
 #pragma unroll
-                    for (int q = 1; q < NP; ++q) mma_bf16(lo, a, xs[(kb * NP + q) * 32 + lane]);
+                    for (int u = 0; u < 4; ++u) {
+                        const int kb = k4 + u, box = kb >> 2, chunk = 2 * (kb & 3) + (li >> 1);
+                        ldsm_x4(a[u], st + (uint32_t)(box * 16 * kDMBox * 2 + wrow * kDMBox * 2 +
+                                                      ((chunk ^ (wrow & 7)) << 4)));
+#pragma unroll
+                        for (int q = 0; q < NP; ++q) bx[u][q] = xs[(kb * NP + q) * 32 + lane];
+                    }
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        mma_bf16(hi, a[u], bx[u][0]);
+                        if constexpr (NP == 3) {
+                            mma_bf16(mid, a[u], bx[u][1]);
+                            mma_bf16(lo, a[u], bx[u][2]);
+                        }
+                    }
                 }
                 __syncwarp();
                 if (issued < nitems) {
@@ -245,6 +264,8 @@ __global__ void __launch_bounds__(kDMWarps * 32, 1) gemv_dense_mma(const DensePa
             }
         }
         if (S > 1) {   // part 0 adds the parts' sums, in part order
+#pragma unroll
+            for (int i = 0; i < 4; ++i) lo[i] = __fadd_rn(mid[i], lo[i]);   // the low parts' sum, then the parts
             float* mine = parts + (warp * 32 + lane) * 8;
 #pragma unroll
             for (int i = 0; i < 4; ++i) { mine[i] = hi[i]; mine[4 + i] = lo[i]; }
@@ -260,6 +281,10 @@ __global__ void __launch_bounds__(kDMWarps * 32, 1) gemv_dense_mma(const DensePa
                 }
             }
             __syncthreads();
+        }
+        if (S == 1) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) lo[i] = __fadd_rn(mid[i], lo[i]);
         }
         if (part == 0 && r < my_rounds && !failed) {
             const int tile = tile_of(r);

@@ -1108,18 +1108,21 @@ __device__ __forceinline__ void mma_issue(const CUtensorMap* wmap, int tile, int
 }
 
 // The fragment words of one pair of blocks (2i, 2i+1) of a 16-row item for
-// lane (g, t): A of both blocks, and the rows' fp16 scales.
+// lane (g, t): A of both blocks, and the rows' fp16 scales. wr: word 0 of row g
+// of the item, wt = wr + t; the rest of each address is a constant (pair and
+// rr unrolled), so the loads need no address arithmetic.
 template <int F>
-__device__ __forceinline__ void mma_frag_pair(const uint8_t* st, int pair, int g, int t, uint32_t (&ae)[4],
+__device__ __forceinline__ void mma_frag_pair(const uint32_t* wr, const uint32_t* wt, int pair, uint32_t (&ae)[4],
                                               uint32_t (&ao)[4], uint32_t (&sc)[2][2]) {
-    constexpr int BB = block_bytes(F), RS = mma_rs<F>();
+    constexpr int PW = 2 * block_bytes(F) / 4, RW = mma_rs<F>() / 4;   // words per block pair, per row
 #pragma unroll
     for (int rr = 0; rr < 2; ++rr) {
-        const uint32_t* w = reinterpret_cast<const uint32_t*>(st + (g + 8 * rr) * RS + pair * 2 * BB);
+        const uint32_t* w = wr + rr * 8 * RW + pair * PW;
+        const uint32_t* u = wt + rr * 8 * RW + pair * PW;
         if constexpr (F == kQ4_0) {
             // even block: scale in bytes 0-1, quant word t at byte 2 + 4t; odd block:
             // scale in bytes 18-19 (high half of word 4), quant word t is word 5 + t.
-            const uint32_t qe = funnel(w[t], w[t + 1], 16), qo = w[5 + t];
+            const uint32_t qe = funnel(u[0], u[1], 16), qo = u[5];
             ae[rr] = qe & 0x0F0F0F0Fu;
             ae[2 + rr] = (qe >> 4) & 0x0F0F0F0Fu;
             ao[rr] = qo & 0x0F0F0F0Fu;
@@ -1129,10 +1132,10 @@ __device__ __forceinline__ void mma_frag_pair(const uint8_t* st, int pair, int g
         } else {
             // even block: quant word u at byte 2 + 4u; odd block (byte 34 on): scale in
             // the high half of word 8, quant word u is word 9 + u.
-            ae[rr] = funnel(w[t], w[t + 1], 16);
-            ae[2 + rr] = funnel(w[4 + t], w[5 + t], 16);
-            ao[rr] = w[9 + t];
-            ao[2 + rr] = w[13 + t];
+            ae[rr] = funnel(u[0], u[1], 16);
+            ae[2 + rr] = funnel(u[4], u[5], 16);
+            ao[rr] = u[9];
+            ao[2 + rr] = u[13];
             sc[0][rr] = w[0] & 0xffffu;
             sc[1][rr] = w[8] >> 16;
         }
@@ -1268,8 +1271,11 @@ __global__ void __launch_bounds__(kMmaWarps * 32, 1) gemv_q_mma(const QGemvParam
         xbase = xsm;
     }
     failed = __syncthreads_or(failed);
-    const uint2* xf = reinterpret_cast<const uint2*>(xbase);
-    const float4* xd = reinterpret_cast<const float4*>(xbase + (size_t)xnb_here * 256);
+    // This lane's fragments of block 0 of the x held at xbase: B words of row g
+    // at (b·8 + g)·4 + t, (dx, bias) pairs at b·4 + t; and its weight row g.
+    const uint2* xf_lane = reinterpret_cast<const uint2*>(xbase) + g * 4 + t;
+    const float4* xd_lane = reinterpret_cast<const float4*>(xbase + (size_t)xnb_here * 256) + t;
+    const uint32_t* ring_w = reinterpret_cast<const uint32_t*>(ring) + g * (RS / 4);
 
     int c_slot = 0, consumed = 0;
     uint32_t c_phase = 0;
@@ -1283,21 +1289,22 @@ __global__ void __launch_bounds__(kMmaWarps * 32, 1) gemv_q_mma(const QGemvParam
                     failed = 1;
                     break;
                 }
-                const uint8_t* st = ring + (size_t)c_slot * ITEM;
-                const int b0 = (ks_lo + k) * KB;
+                const uint32_t* wr = ring_w + c_slot * (ITEM / 4);
+                const int bx = (ks_lo + k) * KB - xoff;   // the item's first block within the x held at xbase
+                const uint2* xfi = xf_lane + bx * 32;
+                const float4* xdi = xd_lane + bx * 4;
                 // All MMAs of the item first, then the scaling in block order.
                 int c[KB][4];
                 uint32_t sc[KB][2];
                 float2 dxs[KB];
 #pragma unroll
                 for (int pr = 0; pr < KB / 2; ++pr) {
-                    const int b = b0 + 2 * pr - xoff;   // index within the x held at xbase
-                    const uint2 xe = ld_xfrag<kXS>(xf + ((size_t)b * 8 + g) * 4 + t);
-                    const uint2 xo = ld_xfrag<kXS>(xf + ((size_t)(b + 1) * 8 + g) * 4 + t);
-                    const float4 de = ld_xfrag<kXS>(xd + (size_t)b * 4 + t);
-                    const float4 dn = ld_xfrag<kXS>(xd + (size_t)(b + 1) * 4 + t);
+                    const uint2 xe = ld_xfrag<kXS>(xfi + pr * 64);
+                    const uint2 xo = ld_xfrag<kXS>(xfi + pr * 64 + 32);
+                    const float4 de = ld_xfrag<kXS>(xdi + pr * 8);
+                    const float4 dn = ld_xfrag<kXS>(xdi + pr * 8 + 4);
                     uint32_t ae[4], ao[4], s2[2][2];
-                    mma_frag_pair<F>(st, pr, g, t, ae, ao, s2);
+                    mma_frag_pair<F>(wr, wr + t, pr, ae, ao, s2);
                     mma_q<F>(ae, xe, F == kQ4_0 ? __float_as_int(de.y) : kIntToFloatMagic,
                              F == kQ4_0 ? __float_as_int(de.w) : kIntToFloatMagic, c[2 * pr]);
                     mma_q<F>(ao, xo, F == kQ4_0 ? __float_as_int(dn.y) : kIntToFloatMagic,
