@@ -105,8 +105,7 @@ __device__ __forceinline__ float sq_sum4(float4 v) {
                      __fadd_rn(__fmul_rn(v.z, v.z), __fmul_rn(v.w, v.w)));
 }
 // h = w · (v · inv), each product rounded.
-__device__ __forceinline__ float4 norm4(float4 v, const float* w, float inv) {
-    const float4 g = load_x4(w);
+__device__ __forceinline__ float4 norm4v(float4 v, float4 g, float inv) {
     return make_float4(__fmul_rn(g.x, __fmul_rn(v.x, inv)), __fmul_rn(g.y, __fmul_rn(v.y, inv)),
                        __fmul_rn(g.z, __fmul_rn(v.z, inv)), __fmul_rn(g.w, __fmul_rn(v.w, inv)));
 }
@@ -216,11 +215,22 @@ __device__ __forceinline__ void quantize_x_rows(const float* __restrict__ x, lon
         const float inv = nw ? cta_row_rms_inv(x + (size_t)m * ldx, nb * kQK, neps) : 0.0f;
         for (int wbase = (tid >> 5) * 4; wbase < nb; wbase += kXUnroll * wstride) {
             float4 v[kXUnroll];
+            if (nw) {
+                float4 gw[kXUnroll];
 #pragma unroll
-            for (int u = 0; u < kXUnroll; ++u) {
-                const int b = wbase + u * wstride + grp;
-                v[u] = b < nb ? load_act4(xr, ur, (size_t)b * kQK) : make_float4(0.f, 0.f, 0.f, 0.f);
-                if (nw && b < nb) v[u] = norm4(v[u], nw + (size_t)b * kQK + gq * 4, inv);
+                for (int u = 0; u < kXUnroll; ++u) {   // x and the norm's weights, all loads in flight together
+                    const int b = wbase + u * wstride + grp;
+                    v[u] = b < nb ? load_x4(xr + (size_t)b * kQK) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    gw[u] = b < nb ? load_x4(nw + (size_t)b * kQK + gq * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+#pragma unroll
+                for (int u = 0; u < kXUnroll; ++u) v[u] = norm4v(v[u], gw[u], inv);
+            } else {
+#pragma unroll
+                for (int u = 0; u < kXUnroll; ++u) {
+                    const int b = wbase + u * wstride + grp;
+                    v[u] = b < nb ? load_act4(xr, ur, (size_t)b * kQK) : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
             }
 #pragma unroll
             for (int u = 0; u < kXUnroll; ++u) {
@@ -949,6 +959,8 @@ __device__ __forceinline__ void gemv_q4_r4_body(const QGemvParams& p) {
             // 64 blocks × 8 threads: one quad of x per thread, loaded first.
             const int gq = threadIdx.x & 7, b = threadIdx.x >> 3;
             float4 v = load_act4(p.x, p.up, (size_t)b * kQK + gq * 4);
+            // The norm's weights load together with x: one L2 round trip for both.
+            const float4 nwq = p.nw ? load_x4(p.nw + (size_t)b * kQK + gq * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
             if (nitems > 0) {
                 const bool ok = mbar_wait_bounded(&bars[0], 0, p.err);
                 have_pre = __all_sync(0xffffffffu, ok);
@@ -960,7 +972,7 @@ __device__ __forceinline__ void gemv_q4_r4_body(const QGemvParams& p) {
             }
             // Fused RMSNorm: the row's sum of squares from the quads in the
             // threads' registers (the whole row: 512 threads × 4 values).
-            if (p.nw) v = norm4(v, p.nw + (size_t)b * kQK + gq * 4, rms_inv(cta_sum(sq_sum4(v)), p.K, p.neps));
+            if (p.nw) v = norm4v(v, nwq, rms_inv(cta_sum(sq_sum4(v)), p.K, p.neps));
             quantize_x_block(v, gq, true, xg, 0, b, xs);
         } else {
             quantize_x_rows<1>(p.x, p.ldx, p.up, p.ldu, xg, xs, threadIdx.x, blockDim.x, p.nw, p.neps);
@@ -973,9 +985,11 @@ __device__ __forceinline__ void gemv_q4_r4_body(const QGemvParams& p) {
     if (p.gather && blockIdx.x == 0) gather_pad(p.gather, 1, p.N, threadIdx.x, blockDim.x);
     float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 
+    float resv = 0.0f;   // fused residual: the row's value, loaded when its tile starts
     for (int it = 0; it < nitems; ++it) {
         const uint8_t* xslot = xb + ((size_t)cur.ks * 32 + lane) * 80;
         const uint8_t* st = stages + (size_t)cur.slot * (32 * SBB);
+        if (p.res && cur.ks == 0 && g == 0 && cur.tile * 4 + r < p.N) resv = p.res[cur.tile * 4 + r];
         if (it == 0 && have_pre) {
             r4_item<!kXGlobal, kR4PreRows>(st, xslot, lane, acc, pre);
         } else {
@@ -992,7 +1006,7 @@ __device__ __forceinline__ void gemv_q4_r4_body(const QGemvParams& p) {
         if (cur.ks == p.ksteps - 1) {
             const float v = r4_reduce(acc, lane);
             const int row = cur.tile * 4 + r;
-            if (g == 0 && row < p.N) p.y[row] = p.res ? __fadd_rn(p.res[row], v) : v;
+            if (g == 0 && row < p.N) p.y[row] = p.res ? __fadd_rn(resv, v) : v;
 #pragma unroll
             for (int k = 0; k < 4; ++k) acc[k] = 0.0f;
         }

@@ -342,4 +342,7 @@ class LlamaDecoder:
         return b.logits
 
     def launches_per_token(self) -> int:
-        return 1 + 5 * self.shape.layers + 1
+        # The embedding row; per layer five GEMV-side launches plus the kernel
+        # that forms and quantizes silu(gate) * up for the down projection; the
+        # LM head.
+        return 1 + 6 * self.shape.layers + 1
