@@ -22,10 +22,13 @@ config 2 Llama-3.2-1B GEMV stack, config 3 dense, config 4 large Q4_0 at
 M = 1 and 8), each with its roofline fraction and the reference's CPU
 kernel timed on this host with all threads and with one pinned thread.
 
-N > 1 (torchrun): weak scaling for the headline (each rank holds its 8192-row
-slice of a [8192*N, 2048] matrix, the reference's row slicing, and every step
-all-gathers y over NVLink inside the GEMV), plus config 4 split by rows over
-the ranks (strong scaling).
+N > 1 (torchrun): weak scaling for the headline. Every rank runs config-0
+steps on its own 8192-row slice of a [8192*N, 2048] matrix, with no
+collective: the north star row-shards only config 4's large matrices. Timed
+after it, in the same line (`config0_row_sharded`), the same slices as one
+row-sharded GEMV whose y is all-gathered over NVLink inside the GEMV every
+step; and config 4 split by rows over the ranks (strong scaling, the
+reference's row slicing) with the gather.
 
 --impl reference: the reference's own CPU kernel (Mattral/simd-ml-kernels
 compiled from its sources, oracle/_ref) on the same workload and config with
@@ -376,9 +379,9 @@ def time_reference_arm(steps: int, warmup: int, world: int) -> dict | None:
 def headline_config(world: int) -> dict:
     """The `config` of the headline line, identical in both arms."""
     return {"workload": "config 0: Q4_0 decode GEMV M=1 K=2048 N=8192" +
-                        (f" per GPU, rows sharded over {world} GPUs (N={N_ROWS * world} in all), y all-gathered"
-                         if world > 1 else ""),
-            "M": 1, "K": K_COLS, "N": N_ROWS * world, "seed": 0, "weights": "N(0, 0.02) -> ggml Q4_0",
+                        (f" on each of {world} GPUs, independent steps, no collective (rank r: rows "
+                         f"8192r..8192r+8191 of the seed-0 [{N_ROWS * world}, 2048] matrix)" if world > 1 else ""),
+            "M": 1, "K": K_COLS, "N": N_ROWS, "gpus": world, "seed": 0, "weights": "N(0, 0.02) -> ggml Q4_0",
             "bytes_per_step": STEP_BYTES * world}
 
 
@@ -604,23 +607,31 @@ def gpu_bench(args, rank: int, world: int, local_rank: int) -> dict | None:
     ws = [Wq0] + [Wq0.clone() for _ in range(copies - 1)]
     x = torch.from_numpy(x0[0]).to(dev)
     y = torch.empty(N_ROWS, device=dev)
+    # N > 1: every GPU runs its own config-0 steps (its slice of the seed-0
+    # [8192·N, 2048] matrix; rank 0's rows are config 0's), no collective: the
+    # north star row-shards only config 4's large matrices. The same slices as
+    # one row-sharded GEMV with y all-gathered are timed after the headline.
     nvlink = world > 1 and args.gather == "nvlink"
     gathered = torch.empty((world, N_ROWS), device=dev) if world > 1 and not nvlink else None
     sg = shard.ShardedGemv("q4_0", Wq0, N_ROWS * world, K_COLS, gather="nvlink") if nvlink else None
-    launches_per_step = 2 if nvlink else 1
+    launches_per_step = 1
 
     def one_step(i):
+        sk.gemv_q4_0(x, ws[i % copies], N_ROWS, K_COLS, out=y)
+
+    def sharded_step(i):
         if nvlink:   # GEMV storing its slice into every rank's y over NVLink, then the peers' signals
             _core._gemv_q_gather(sg._g, 0, 1, N_ROWS, K_COLS, x.data_ptr(), K_COLS, ws[i % copies].data_ptr(),
                                  stream.cuda_stream, local_rank)
             return
         sk.gemv_q4_0(x, ws[i % copies], N_ROWS, K_COLS, out=y)
-        if world > 1:
-            dist.all_gather_into_tensor(gathered, y)
+        dist.all_gather_into_tensor(gathered, y)
 
     with torch.cuda.stream(stream):
         for i in range(args.warmup):
             one_step(i)
+            if world > 1:
+                sharded_step(i)
     torch.cuda.synchronize(dev)
     signal = None
     if nvlink:   # the fused gather's fixed cost: NVLink flag round trips, and data-free gather steps
@@ -645,13 +656,27 @@ def gpu_bench(args, rank: int, world: int, local_rank: int) -> dict | None:
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_max = float(t.item())
-    # Kernel-only time per step (no all-gather), for the roofline.
-    kernel_ms = ms
+    kernel_ms = ms   # this rank's GEMV alone, for the roofline
+    # Ranks that ran the timed steps, each on its own GPU (a sum over the group).
+    active = torch.tensor([1.0], device=dev)
     if world > 1:
-        kernel_ms = chained_ms(torch, dev, stream, lambda i: sk.gemv_q4_0(x, ws[i % copies], N_ROWS, K_COLS, out=y),
-                               steps, copies)
+        dist.all_reduce(active)
+    gpus_active = int(active.item())
     value = STEP_BYTES * world * steps / (ms_max * 1e-3) / 1e9
     cfg = headline_config(world)
+    row_sharded = None
+    if world > 1:
+        sms = chained_ms(torch, dev, stream, sharded_step, steps, copies, barrier=barrier)
+        t = torch.tensor([sms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        us = float(t.item()) * 1e3 / steps
+        row_sharded = {
+            "workload": f"config 0's rows sharded: one [{N_ROWS * world}, {K_COLS}] Q4_0 GEMV, {N_ROWS} rows per GPU, "
+                        "every step's y all-gathered to every GPU before the next step starts",
+            "gather": "fused NVLink stores (tagged words) + wait kernel" if nvlink else "NCCL all-gather",
+            "us_per_step": round(us, 3), "gb_s_aggregate": round(STEP_BYTES * world / (us * 1e-6) / 1e9, 1),
+            "gemv_alone_us_per_step": round(ms_max * 1e3 / steps, 3),
+            "gpu_launches_per_step": 2 if nvlink else 1, "nvlink_signal": signal}
 
     if args.only_gemv:
         prod.close()
@@ -709,7 +734,9 @@ def gpu_bench(args, rank: int, world: int, local_rank: int) -> dict | None:
 
     # End to end through the public API: x from page-locked host memory, y back to host memory,
     # weights resident on the device (uploaded once, as a model's).
-    e2e = e2e_headline(torch, sk, shard, dev, local_rank, world, ws, copies, sg, x0[0])
+    e2e = e2e_headline(torch, sk, shard, dev, local_rank, world, ws, copies, None, x0[0])
+    e2e_sharded = e2e_headline(torch, sk, shard, dev, local_rank, world, ws, copies, sg, x0[0], sharded=True) \
+        if world > 1 else None
     if sg is not None:
         sg.close()   # release the gather buffers before the process group goes
 
@@ -731,20 +758,20 @@ def gpu_bench(args, rank: int, world: int, local_rank: int) -> dict | None:
         "timing": {"l2_policy": f"{copies} rotated weight copies ({copies * W_BYTES / 2**20:.0f} MiB > 2x L2 "
                                 f"{l2 / 2**20:.0f} MiB): inputs larger than L2",
                    "launch": "CUDA graphs, programmatic dependent launch; start/end events recorded inside the "
-                             f"graphs after {copies} untimed steps (steady state)"
-                             + (", NVLink gather fused into the GEMV" if nvlink else "")},
+                             f"graphs after {copies} untimed steps (steady state)"},
         "roofline": rl,
         "e2e": e2e,
         "gpu_launches": steps * launches_per_step,
+        "gpus_active": gpus_active,
         "clocks": clocks.summary(),
     }
     if CHAINED_FALLBACKS:
         out["timing"]["in_graph_events"] = f"unreadable; {len(CHAINED_FALLBACKS)} cases timed over whole replays"
 
-    if world > 1:
-        out["kernel_only_ms_per_step"] = kernel_ms / steps
-        if signal is not None:
-            out["nvlink_signal"] = signal
+    if row_sharded is not None:
+        out["config0_row_sharded"] = row_sharded
+    if e2e_sharded is not None:
+        out["e2e_row_sharded"] = e2e_sharded
     out.update(extra)
     if world == 1:
         cb = extra["cpu_arms"].get("config0")
@@ -956,17 +983,21 @@ def llama_full_decode(torch, sk, dev, stream, weights, tokens: int, peak, wbytes
             "launch": f"one CUDA graph of {tokens} whole decode steps from position 0, PDL"}
 
 
-def e2e_headline(torch, sk, shard, dev, local_rank, world, ws, copies, sg, x_np) -> dict:
+def e2e_headline(torch, sk, shard, dev, local_rank, world, ws, copies, sg, x_np, sharded: bool = False) -> dict:
     """The headline metric through the public API with host buffers: every call
     copies x (page-locked host memory) to the device and returns y in host memory.
-    At least 2,000 timed calls after 200 warm-up calls; per-call times."""
+    At least 2,000 timed calls after 200 warm-up calls; per-call times. N > 1:
+    every rank's own calls, the median of the slowest rank; `sharded`: calls of
+    the row-sharded GEMV that return the all-gathered y."""
     import torch.distributed as dist
     xh = torch.from_numpy(np.ascontiguousarray(x_np)).pin_memory()
     xh_np = xh.numpy()
     sk.set_pdl(False, local_rank)
     calls = 2000
     ts = []
-    if world == 1:
+    if not sharded:
+        if world > 1:
+            dist.barrier()
         for i in range(200):
             sk.gemv_q4_0(xh_np, ws[i % copies], N_ROWS, K_COLS)
         for i in range(calls):
@@ -974,8 +1005,12 @@ def e2e_headline(torch, sk, shard, dev, local_rank, world, ws, copies, sg, x_np)
             yh = sk.gemv_q4_0(xh_np, ws[i % copies], N_ROWS, K_COLS)
             ts.append(time.perf_counter() - t0)
         assert yh.shape == (N_ROWS,)
+        if world > 1:
+            t = torch.tensor([statistics.median(ts)], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
         d2h = 4 * N_ROWS
-        api = "simd_ml_kernels.gemv_q4_0(numpy x in page-locked memory, device-resident weights) -> numpy y"
+        api = "simd_ml_kernels.gemv_q4_0(numpy x in page-locked memory, device-resident weights) -> numpy y" + \
+            (", on every GPU" if world > 1 else "")
     else:
         if sg is None:
             sg = shard.ShardedGemv("q4_0", ws[0], N_ROWS * world, K_COLS)
@@ -990,13 +1025,14 @@ def e2e_headline(torch, sk, shard, dev, local_rank, world, ws, copies, sg, x_np)
             ts.append(time.perf_counter() - t0)
         t = torch.tensor([statistics.median(ts)], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        d2h = 4 * N_ROWS * world
+        d2h = 4 * N_ROWS * world * world   # every rank reads the whole gathered y
         api = "ShardedGemv.forward(x host->device, fused NVLink gather) + y device->host"
     sk.set_pdl(True, local_rank)
     q = quantiles(ts)
     nb = STEP_BYTES * world
-    return {"value": round(nb / q["median"] / 1e9, 2), "unit": "GB/s", "h2d_bytes_per_step": 4 * K_COLS,
-            "d2h_bytes_per_step": d2h, "us_median": round(q["median"] * 1e6, 3),
+    med = float(t.item()) if world > 1 else q["median"]   # the slowest rank's median
+    return {"value": round(nb / med / 1e9, 2), "unit": "GB/s", "h2d_bytes_per_step": 4 * K_COLS * world,
+            "d2h_bytes_per_step": d2h if sharded else d2h * world, "us_median": round(med * 1e6, 3),
             "us_p25": round(q["p25"] * 1e6, 3), "us_p75": round(q["p75"] * 1e6, 3),
             "us_mean": round(q["mean"] * 1e6, 3), "steps": calls, "api": api}
 

@@ -91,9 +91,16 @@ smk_status smk_ctx_destroy(smk_ctx* ctx);
  *                   captured graphs.
  *   SMK_OPT_DENSE_MMA  1 (default): smk_gemv_dense with bfloat16 weights and
  *                   4..8 rows of x takes the tensor-core kernel (x split
- *                   exactly into bf16 parts); 0: the CUDA-core kernel. */
+ *                   exactly into bf16 parts); 0: the CUDA-core kernel.
+ *   SMK_OPT_PREFETCH_DELAY  SM clock cycles (0..100000) that the Q4_0
+ *                   one-row kernel of K = 2048-multiple shapes (without a fused
+ *                   norm, residual or gather) holds back its first weight
+ *                   copies when it starts. Under SMK_OPT_PDL it
+ *                   starts while the GEMV before it is about to read its x;
+ *                   a short hold measured faster in such chains. Results do
+ *                   not depend on it. Default 100. */
 enum { SMK_OPT_PDL = 1, SMK_OPT_WARPS = 2, SMK_OPT_STAGES = 3, SMK_OPT_CTAS_PER_SM = 4, SMK_OPT_TILE_ORDER = 5,
-       SMK_OPT_HOST_GRAPHS = 6, SMK_OPT_DENSE_MMA = 7 };
+       SMK_OPT_HOST_GRAPHS = 6, SMK_OPT_DENSE_MMA = 7, SMK_OPT_PREFETCH_DELAY = 8 };
 smk_status smk_ctx_set(smk_ctx* ctx, int option, long long value);
 smk_status smk_ctx_get(smk_ctx* ctx, int option, long long* value);
 /* The CUDA device that owns `ptr` (device or managed memory), or -1 for host memory. */

@@ -523,13 +523,17 @@ __device__ __forceinline__ void gather_pad(const GatherArgs* ga, int M, int n, i
 // CTA's first tile (p.contiguous) or 0; ctaid is read anew so that nothing
 // from before the loop has to be kept. The receivers wait for the step's last
 // tile in any case, so sending after the loop costs them nothing.
+// First tile of CTA bx's contiguous range (the range of bx is [first(bx),
+// first(bx + 1))): an even share of the tiles, the first cta_r CTAs one more.
+// The launcher splits ntiles = cta_q · grid + cta_r, so the device divides nothing.
+__device__ __forceinline__ int cta_first_tile(const QGemvParams& p, int bx) { return bx * p.cta_q + min(bx, p.cta_r); }
+
 __device__ __forceinline__ void gather_send(const QGemvParams& p, int M, int TR, int end, int step, int lane) {
     const GatherArgs* ga = p.gather;
     __syncwarp();   // the lanes' stores to p.y are visible to the whole warp
-    unsigned bx, nbx;
+    unsigned bx;
     asm volatile("mov.u32 %0, %%ctaid.x;" : "=r"(bx));
-    asm volatile("mov.u32 %0, %%nctaid.x;" : "=r"(nbx));
-    const int lo = p.contiguous ? (int)((long long)bx * p.ntiles / nbx) : 0;
+    const int lo = p.contiguous ? cta_first_tile(p, (int)bx) : 0;
     const GatherStep gs = gather_step(ga);
     const long long cols = (long long)ga->world * ga->npad;
     const int per = M * TR;
@@ -574,8 +578,8 @@ __device__ __forceinline__ void gemv_q_fast_body(const QGemvParams& p) {
     int GW, gw, tiles_end;
     if (p.contiguous) {
         GW = nwarps;
-        gw = (int)((long long)blockIdx.x * p.ntiles / gridDim.x) + warp;
-        tiles_end = (int)((long long)(blockIdx.x + 1) * p.ntiles / gridDim.x);
+        gw = cta_first_tile(p, blockIdx.x) + warp;
+        tiles_end = cta_first_tile(p, blockIdx.x + 1);
     } else {
         GW = gridDim.x * nwarps;
         gw = warp * gridDim.x + blockIdx.x;
@@ -935,8 +939,8 @@ __device__ __forceinline__ void gemv_q4_r4_body(const QGemvParams& p) {
     int GW, gw, tiles_end;
     if (p.contiguous) {
         GW = nwarps;
-        gw = (int)((long long)blockIdx.x * p.ntiles / gridDim.x) + warp;
-        tiles_end = (int)((long long)(blockIdx.x + 1) * p.ntiles / gridDim.x);
+        gw = cta_first_tile(p, blockIdx.x) + warp;
+        tiles_end = cta_first_tile(p, blockIdx.x + 1);
     } else {
         GW = gridDim.x * nwarps;
         gw = warp * gridDim.x + blockIdx.x;
@@ -952,6 +956,19 @@ __device__ __forceinline__ void gemv_q4_r4_body(const QGemvParams& p) {
     __syncwarp();
     ItemCursor cur{gw, 0, 0, 0u}, iss{gw, 0, 0, 0u};
     int issued = 0;
+    // Chained under programmatic dependent launch, this kernel starts while the
+    // GEMV before it is about to read its x. Holding the first weight copies
+    // back p.issue_delay cycles (a bounded spin) measured faster on B200 for the
+    // plain kernel (config 0: 2.39 against 2.57 us per chained step at 100
+    // cycles, less gain from 200 cycles on; 64-bit tile-range divisions that
+    // once preceded the copies had acted as such a hold) and no faster for the
+    // decode step's fused variants, which therefore never hold. The copies
+    // still land long before this kernel's own x.
+    if (kExt == 0 && p.issue_delay > 0) {
+        const long long t0 = clock64();
+        for (int spin = 0; spin < 4096 && clock64() - t0 < p.issue_delay; ++spin) {
+        }
+    }
     for (; issued < min(p.stages, nitems); ++issued) {
         issue_item<kQ4_0>(p, iss.tile, iss.ks, iss.slot, stages, bars, lane);
         iss.next(p, GW);
@@ -1075,9 +1092,12 @@ void (*r4_kernel(const QGemvParams& p))(QGemvParams) {
 
 // Q8 activations for the MMA path, written by quantize_x_mma_kernel: per
 // block b the B-fragment words of row m (0..7) for lane t, (word t, word 4+t)
-// side by side at ((b·8 + m)·4 + t)·8 bytes; after nb·256 bytes, the pair
-// (dx, bits of kIntToFloatMagic − 8·Σq) of (b, m) at (b·8 + m)·8.
-// float(isum) comes from the magic-number add (kIntToFloatMagic).
+// side by side at ((b·8 + m)·4 + t)·8 bytes; after nb·256 bytes, 64 bytes per
+// block: c(m) = kIntToFloatMagic − 8·Σq(m) of rows 0..7 (32 bytes), then dx of
+// rows 0..7 (32 bytes), so lane t reads the pairs of x rows (2t, 2t+1) with one
+// 8-byte load each; the c pair is the first half of the MMA's accumulator
+// input. Rows ≥ M have c = kIntToFloatMagic and dx = 0. float(isum) comes from
+// the magic-number add (kIntToFloatMagic).
 constexpr int kMmaWarps = 16;
 // A warp item is 16 rows × 8 blocks, fetched as one box of a 2-D tensor map
 // over the weights (rows of nb·block bytes; Q4_0 as bytes, Q8_0 as 16-bit
@@ -1087,6 +1107,9 @@ constexpr int kMmaWarps = 16;
 // distinct banks.
 template <int F> __host__ __device__ constexpr int mma_kb() { return 8; }
 template <int F> __host__ __device__ constexpr int mma_rs() { return 8 * block_bytes(F); }
+// Quantized x per block for the MMA path: B fragments 256 bytes, accumulator
+// inputs and scales 64 bytes (at nb·256 + b·64).
+constexpr int kMmaXFragBytes = 256, kMmaXcdBytes = 64;
 
 __global__ void __launch_bounds__(kThreadsQuantX) quantize_x_mma_kernel(const float* __restrict__ x, long long ldx,
                                                                          const float* __restrict__ up, long long ldu,
@@ -1110,29 +1133,35 @@ __global__ void __launch_bounds__(kThreadsQuantX) quantize_x_mma_kernel(const fl
         const Q8Quad q = quantize_quad(v);
         if (!valid) continue;
         reinterpret_cast<uint32_t*>(xq)[((size_t)(b * 8 + m) * 4 + (gq & 3)) * 2 + (gq >> 2)] = m < M ? q.word : 0u;
-        if (gq == 0)
-            reinterpret_cast<float2*>(xq + (size_t)nb * 256)[(size_t)b * 8 + m] =
-                m < M ? make_float2(q.dx, __int_as_float(kIntToFloatMagic - 8 * q.s))
-                      : make_float2(0.0f, __int_as_float(kIntToFloatMagic));
+        if (gq == 0) {
+            uint8_t* cd = xq + (size_t)nb * kMmaXFragBytes + (size_t)b * kMmaXcdBytes;
+            reinterpret_cast<int*>(cd)[m] = m < M ? kIntToFloatMagic - 8 * q.s : kIntToFloatMagic;
+            reinterpret_cast<float*>(cd + 32)[m] = m < M ? q.dx : 0.0f;
+        }
     }
 }
 
-// c = A·B + (m0, m1, m0, m1): the int32 sums of rows (g, g+8) × x rows (2t, 2t+1)
-// start from the magic-number bits of their x row (kIntToFloatMagic, with the
-// Q4_0 bias −8·Σq folded in), so c comes out as the bits of a float whose
-// value is 2^23 + 2^22 + isum: one exact subtraction converts it.
+// c = A·B + (m.x, m.y, m.x, m.y): the int32 sums of rows (g, g+8) × x rows
+// (2t, 2t+1) start from the magic-number bits of their x row (kIntToFloatMagic,
+// with the Q4_0 bias −8·Σq folded in), so c comes out as the bits of a float
+// whose value is 2^23 + 2^22 + isum: one exact subtraction converts it. m is
+// loaded as one pair, the first half of the accumulator input the instruction
+// takes.
 template <int F>
-__device__ __forceinline__ void mma_q(const uint32_t (&a)[4], uint2 b, int m0, int m1, int (&c)[4]) {
+__device__ __forceinline__ void mma_q(const uint32_t (&a)[4], uint2 b, int2 m, int (&c)[4]) {
+    const int4 cin = make_int4(m.x, m.y, m.x, m.y);
     if constexpr (F == kQ4_0)
         asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-                     "{%10,%11,%10,%11};"
+                     "{%10,%11,%12,%13};"
                      : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
-                     : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b.x), "r"(b.y), "r"(m0), "r"(m1));
+                     : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b.x), "r"(b.y), "r"(cin.x), "r"(cin.y),
+                       "r"(cin.z), "r"(cin.w));
     else
         asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-                     "{%10,%11,%10,%11};"
+                     "{%10,%11,%12,%13};"
                      : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
-                     : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b.x), "r"(b.y), "r"(m0), "r"(m1));
+                     : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b.x), "r"(b.y), "r"(cin.x), "r"(cin.y),
+                       "r"(cin.z), "r"(cin.w));
 }
 
 template <int F>
@@ -1146,9 +1175,11 @@ __device__ __forceinline__ void mma_issue(const CUtensorMap* wmap, int tile, int
 }
 
 // The fragment words of one pair of blocks (2i, 2i+1) of a 16-row item for
-// lane (g, t): A of both blocks, and the rows' fp16 scales. wr: word 0 of row g
-// of the item, wt = wr + t; the rest of each address is a constant (pair and
-// rr unrolled), so the loads need no address arithmetic.
+// lane (g, t): A of both blocks, and the words holding the rows' fp16 scales
+// (the even block's in the low half of sc[0][rr], the odd block's in the high
+// half of sc[1][rr]). wr: word 0 of row g of the item, wt = wr + t; the rest of
+// each address is a constant (pair and rr unrolled), so the loads need no
+// address arithmetic.
 template <int F>
 __device__ __forceinline__ void mma_frag_pair(const uint32_t* wr, const uint32_t* wt, int pair, uint32_t (&ae)[4],
                                               uint32_t (&ao)[4], uint32_t (&sc)[2][2]) {
@@ -1165,8 +1196,8 @@ __device__ __forceinline__ void mma_frag_pair(const uint32_t* wr, const uint32_t
             ae[2 + rr] = (qe >> 4) & 0x0F0F0F0Fu;
             ao[rr] = qo & 0x0F0F0F0Fu;
             ao[2 + rr] = (qo >> 4) & 0x0F0F0F0Fu;
-            sc[0][rr] = w[0] & 0xffffu;
-            sc[1][rr] = w[4] >> 16;
+            sc[0][rr] = w[0];
+            sc[1][rr] = w[4];
         } else {
             // even block: quant word u at byte 2 + 4u; odd block (byte 34 on): scale in
             // the high half of word 8, quant word u is word 9 + u.
@@ -1174,8 +1205,8 @@ __device__ __forceinline__ void mma_frag_pair(const uint32_t* wr, const uint32_t
             ae[2 + rr] = funnel(u[4], u[5], 16);
             ao[rr] = u[9];
             ao[2 + rr] = u[13];
-            sc[0][rr] = w[0] & 0xffffu;
-            sc[1][rr] = w[8] >> 16;
+            sc[0][rr] = w[0];
+            sc[1][rr] = w[8];
         }
     }
 }
@@ -1187,14 +1218,18 @@ __device__ __forceinline__ void mma_frag_pair(const uint32_t* wr, const uint32_t
 // through the packed FP32 unit (fadd2_rn / fmul2_rn: two IEEE operations each).
 // The product that is added to acc is a scalar __fmul_rn: a packed product
 // feeding a packed sum is contracted into a fused multiply-add by the code
-// generator even with explicit rounding (measured on B200: 44 % of such
-// pairs differ from the two roundings), which would break the reference's order.
+// generator even with explicit rounding, and so is the product written as a
+// packed fma with −0 (measured on B200: 35–44 % of such pairs, and 75 % of
+// 8-step sums of the fma form, differ from the scalar roundings), which would
+// break the reference's order. kHi: the scales sit in the high halves of sc
+// (the odd block of a pair).
+template <bool kHi>
 __device__ __forceinline__ void mma_accumulate(const int (&c)[4], const uint32_t (&sc)[2], float2 dx,
                                                float2 (&acc)[2]) {
     const float2 unmagic = make_float2(-12582912.0f, -12582912.0f);
 #pragma unroll
     for (int rr = 0; rr < 2; ++rr) {
-        const float dw = half_bits_to_float(sc[rr]);
+        const float dw = kHi ? half_hi_to_float(sc[rr]) : half_lo_to_float(sc[rr]);
         const float2 i = fadd2_rn(make_float2(__int_as_float(c[2 * rr]), __int_as_float(c[2 * rr + 1])), unmagic);
         const float2 sc2 = fmul2_rn(make_float2(dw, dw), dx);
         acc[rr].x = __fadd_rn(acc[rr].x, __fmul_rn(i.x, sc2.x));
@@ -1209,7 +1244,7 @@ __host__ __device__ inline size_t mma_x_offset(int warps, int stages) {
     return ((size_t)(warps * stages + 1) * 8 + 127) & ~(size_t)127;
 }
 __host__ __device__ inline size_t mma_part_offset(int warps, int stages, int nb, bool xs) {
-    return mma_x_offset(warps, stages) + (xs ? (((size_t)nb * 320 + 127) & ~(size_t)127) : 0);
+    return mma_x_offset(warps, stages) + (xs ? (((size_t)nb * (kMmaXFragBytes + kMmaXcdBytes) + 127) & ~(size_t)127) : 0);
 }
 __host__ __device__ inline size_t mma_ring_offset(int warps, int stages, int nb, bool xs) {
     return mma_part_offset(warps, stages, nb, xs) + (size_t)warps * 32 * 16;
@@ -1300,19 +1335,23 @@ __global__ void __launch_bounds__(kMmaWarps * 32, 1) gemv_q_mma(const QGemvParam
         xnb_here = kspan * KB;
         xoff = xb0;
         if (threadIdx.x == 0) {
-            const uint32_t qbytes = (uint32_t)xnb_here * 256u, dbytes = (uint32_t)xnb_here * 64u;
+            const uint32_t qbytes = (uint32_t)xnb_here * kMmaXFragBytes, dbytes = (uint32_t)xnb_here * kMmaXcdBytes;
             mbar_arrive_expect_tx(xbar, qbytes + dbytes);
-            tma_load_1d(xsm, p.xq + (size_t)xb0 * 256, qbytes, xbar);
-            tma_load_1d(xsm + qbytes, p.xq + (size_t)p.nb * 256 + (size_t)xb0 * 64, dbytes, xbar);
+            tma_load_1d(xsm, p.xq + (size_t)xb0 * kMmaXFragBytes, qbytes, xbar);
+            tma_load_1d(xsm + qbytes, p.xq + (size_t)p.nb * kMmaXFragBytes + (size_t)xb0 * kMmaXcdBytes, dbytes,
+                        xbar);
         }
         failed = !mbar_wait_bounded(xbar, 0u, p.err);
         xbase = xsm;
     }
     failed = __syncthreads_or(failed);
     // This lane's fragments of block 0 of the x held at xbase: B words of row g
-    // at (b·8 + g)·4 + t, (dx, bias) pairs at b·4 + t; and its weight row g.
+    // at (b·8 + g)·4 + t; the accumulator input pair and the dx pair of x rows
+    // (2t, 2t+1) in the block's 64 bytes; and its weight row g.
     const uint2* xf_lane = reinterpret_cast<const uint2*>(xbase) + g * 4 + t;
-    const float4* xd_lane = reinterpret_cast<const float4*>(xbase + (size_t)xnb_here * 256) + t;
+    const uint8_t* xcd = xbase + (size_t)xnb_here * kMmaXFragBytes;
+    const int2* xc_lane = reinterpret_cast<const int2*>(xcd) + t;
+    const float2* xd_lane = reinterpret_cast<const float2*>(xcd + 32) + t;
     const uint32_t* ring_w = reinterpret_cast<const uint32_t*>(ring) + g * (RS / 4);
 
     int c_slot = 0, consumed = 0;
@@ -1330,32 +1369,35 @@ __global__ void __launch_bounds__(kMmaWarps * 32, 1) gemv_q_mma(const QGemvParam
                 const uint32_t* wr = ring_w + c_slot * (ITEM / 4);
                 const int bx = (ks_lo + k) * KB - xoff;   // the item's first block within the x held at xbase
                 const uint2* xfi = xf_lane + bx * 32;
-                const float4* xdi = xd_lane + bx * 4;
+                const int2* xci = xc_lane + bx * (kMmaXcdBytes / 8);
+                const float2* xdi = xd_lane + bx * (kMmaXcdBytes / 8);
                 // All MMAs of the item first, then the scaling in block order.
                 int c[KB][4];
                 uint32_t sc[KB][2];
                 float2 dxs[KB];
+                const int2 magic2 = make_int2(kIntToFloatMagic, kIntToFloatMagic);
 #pragma unroll
                 for (int pr = 0; pr < KB / 2; ++pr) {
                     const uint2 xe = ld_xfrag<kXS>(xfi + pr * 64);
                     const uint2 xo = ld_xfrag<kXS>(xfi + pr * 64 + 32);
-                    const float4 de = ld_xfrag<kXS>(xdi + pr * 8);
-                    const float4 dn = ld_xfrag<kXS>(xdi + pr * 8 + 4);
                     uint32_t ae[4], ao[4], s2[2][2];
                     mma_frag_pair<F>(wr, wr + t, pr, ae, ao, s2);
-                    mma_q<F>(ae, xe, F == kQ4_0 ? __float_as_int(de.y) : kIntToFloatMagic,
-                             F == kQ4_0 ? __float_as_int(de.w) : kIntToFloatMagic, c[2 * pr]);
-                    mma_q<F>(ao, xo, F == kQ4_0 ? __float_as_int(dn.y) : kIntToFloatMagic,
-                             F == kQ4_0 ? __float_as_int(dn.w) : kIntToFloatMagic, c[2 * pr + 1]);
-                    dxs[2 * pr] = make_float2(de.x, de.z);
-                    dxs[2 * pr + 1] = make_float2(dn.x, dn.z);
+                    mma_q<F>(ae, xe, F == kQ4_0 ? ld_xfrag<kXS>(xci + (2 * pr) * (kMmaXcdBytes / 8)) : magic2,
+                             c[2 * pr]);
+                    mma_q<F>(ao, xo, F == kQ4_0 ? ld_xfrag<kXS>(xci + (2 * pr + 1) * (kMmaXcdBytes / 8)) : magic2,
+                             c[2 * pr + 1]);
+                    dxs[2 * pr] = ld_xfrag<kXS>(xdi + (2 * pr) * (kMmaXcdBytes / 8));
+                    dxs[2 * pr + 1] = ld_xfrag<kXS>(xdi + (2 * pr + 1) * (kMmaXcdBytes / 8));
                     sc[2 * pr][0] = s2[0][0];
                     sc[2 * pr][1] = s2[0][1];
                     sc[2 * pr + 1][0] = s2[1][0];
                     sc[2 * pr + 1][1] = s2[1][1];
                 }
 #pragma unroll
-                for (int j = 0; j < KB; ++j) mma_accumulate(c[j], sc[j], dxs[j], acc);
+                for (int j = 0; j < KB; ++j) {
+                    if (j & 1) mma_accumulate<true>(c[j], sc[j], dxs[j], acc);
+                    else mma_accumulate<false>(c[j], sc[j], dxs[j], acc);
+                }
                 __syncwarp();
                 if (issued < nitems) {
                     fence_proxy_async_smem();
@@ -1636,8 +1678,11 @@ cudaError_t launch_fast_m(const LaunchCfg& c, const QGemvParams& p, size_t smem,
     const long long cap = (long long)std::min(per_sm, std::max(c.ctas_per_sm, 1)) * c.num_sms;
     const long long want = std::max<long long>(((long long)p.ntiles + c.warps - 1) / c.warps,
                                                std::min<long long>(p.ntiles, c.num_sms));
-    const long long grid = std::min(want, cap);
-    return launch(k, dim3((unsigned)std::max<long long>(grid, 1)), dim3(c.warps * 32), smem, c, p);
+    const int grid = (int)std::max<long long>(std::min(want, cap), 1);
+    QGemvParams q = p;
+    q.cta_q = p.ntiles / grid;
+    q.cta_r = p.ntiles % grid;
+    return launch(k, dim3((unsigned)grid), dim3(c.warps * 32), smem, c, q);
 }
 
 template <int F, int M>
@@ -1759,7 +1804,7 @@ cudaError_t launch_gather_pingpong(cudaStream_t s, const GatherArgs* g_dev, unsi
     return cudaGetLastError();
 }
 
-size_t xmma_bytes(int nb) { return (size_t)nb * 320; }
+size_t xmma_bytes(int nb) { return (size_t)nb * (kMmaXFragBytes + kMmaXcdBytes); }
 
 cudaError_t launch_quantize_x_mma(const LaunchCfg& c, const QGemvParams& p, uint8_t* xq) {
     const long long groups = (long long)p.nb * 8;

@@ -63,6 +63,8 @@ struct QGemvParams {
     int stages;            // shared-memory stages per warp (fast kernel)
     int r4;                // fast kernel: the four-row layout (Q4_0, M = 1, K % 2048 == 0); set by plan_tiles
     int contiguous;        // fast kernel: 1 = each CTA takes a contiguous range of tiles, 0 = tiles interleaved over CTAs
+    int cta_q, cta_r;      // contiguous ranges: ntiles = cta_q · grid + cta_r (set by the launcher, see cta_first_tile)
+    int issue_delay;       // four-row kernel: SM cycles its warps hold back their first weight copies
     int split;             // tensor-core kernel: K parts per 16-row tile (set by its launcher)
     // Tensor-core kernel with x larger than shared memory: K is cut into
     // kparts parts across CTAs, each CTA holding only its part's slice of x

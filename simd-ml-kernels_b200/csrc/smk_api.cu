@@ -209,6 +209,7 @@ struct smk_ctx {
     // CUDA graph of their copy and kernel (guarded by mu_stage).
     bool host_graphs = true;
     bool dense_mma = true;   // SMK_OPT_DENSE_MMA: bf16 weights at 4..8 rows on the tensor-core kernel
+    int prefetch_delay = 100;   // SMK_OPT_PREFETCH_DELAY: cycles the four-row kernel holds back its weight copies
     cudaStream_t capture_stream = nullptr;   // non-blocking: captures never touch the legacy stream
     std::unordered_map<HostKey, HostGraph, HostKeyHash> graphs;
     unsigned long long host_calls = 0;
@@ -245,6 +246,7 @@ void auto_shape(smk_ctx* c, smk::QGemvParams& p, smk::LaunchCfg* l, int* stages)
     if (c->ctas_per_sm <= 0) l->ctas_per_sm = large ? 1 : 2;
     *stages = c->stages > 0 ? c->stages : (large ? 2 : 1);
     p.contiguous = c->tile_order == 1 ? 0 : 1;
+    p.issue_delay = c->prefetch_delay;
 }
 
 smk_status check_q_args(smk_qformat fmt, int M, int N, int K) {
@@ -481,6 +483,10 @@ smk_status smk_ctx_set(smk_ctx* c, int option, long long v) {
     switch (option) {
         case SMK_OPT_HOST_GRAPHS: c->host_graphs = v != 0; return SMK_OK;
         case SMK_OPT_DENSE_MMA: c->dense_mma = v != 0; return SMK_OK;
+        case SMK_OPT_PREFETCH_DELAY:
+            if (v < 0 || v > 100000) return fail(SMK_ERR_ARGUMENT, "prefetch delay must be in 0..100000 cycles");
+            c->prefetch_delay = (int)v;
+            return SMK_OK;
         case SMK_OPT_PDL: c->pdl = v != 0; return SMK_OK;
         case SMK_OPT_WARPS:
             if (v < 0 || v > 16) return fail(SMK_ERR_ARGUMENT, "warps must be in 0..16 (0: automatic)");
@@ -512,6 +518,7 @@ smk_status smk_ctx_get(smk_ctx* c, int option, long long* v) {
         case SMK_OPT_TILE_ORDER: *v = c->tile_order; return SMK_OK;
         case SMK_OPT_HOST_GRAPHS: *v = c->host_graphs; return SMK_OK;
         case SMK_OPT_DENSE_MMA: *v = c->dense_mma; return SMK_OK;
+        case SMK_OPT_PREFETCH_DELAY: *v = c->prefetch_delay; return SMK_OK;
         default: return fail(SMK_ERR_ARGUMENT, "unknown option %d", option);
     }
 }

@@ -145,9 +145,9 @@ __device__ __forceinline__ void st_release_sys_u32(unsigned* p, unsigned v) {
 
 // Two IEEE float32 products / sums in one packed instruction (sm_100), each
 // rounded to nearest on its own. A packed product that feeds a packed sum is
-// fused into one multiply-add by the code generator, explicit .rn or not
-// (checked on B200), so use them only where no sum consumes a product whose
-// rounding matters.
+// fused into one multiply-add by the code generator, explicit .rn or not, and
+// so is a product written as fma(a, b, −0) (both checked on B200), so use them
+// only where no sum consumes a product whose rounding matters.
 __device__ __forceinline__ unsigned long long pack_f2(float2 v) {
     return (unsigned long long)__float_as_uint(v.x) | ((unsigned long long)__float_as_uint(v.y) << 32);
 }
@@ -163,6 +163,18 @@ __device__ __forceinline__ float2 fadd2_rn(float2 a, float2 b) {
     unsigned long long d;
     asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(pack_f2(a)), "l"(pack_f2(b)));
     return unpack_f2(d);
+}
+
+// The binary16 in the low / high half of a word, as float (exact).
+__device__ __forceinline__ float half_lo_to_float(uint32_t w) {
+    float f;
+    asm("{ .reg .f16 l, h; mov.b32 {l, h}, %1; cvt.f32.f16 %0, l; }" : "=f"(f) : "r"(w));
+    return f;
+}
+__device__ __forceinline__ float half_hi_to_float(uint32_t w) {
+    float f;
+    asm("{ .reg .f16 l, h; mov.b32 {l, h}, %1; cvt.f32.f16 %0, h; }" : "=f"(f) : "r"(w));
+    return f;
 }
 
 // Programmatic dependent launch. Both are no-ops when the kernel was not

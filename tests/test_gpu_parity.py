@@ -574,6 +574,39 @@ def test_host_call_graph_replay_tracks_operands(sk, torch, M):
     assert _core._device_error(torch.cuda.current_stream().cuda_stream) == 0
 
 
+def test_prefetch_delay_option_changes_no_result(sk, torch):
+    """SMK_OPT_PREFETCH_DELAY (8) only moves the four-row kernel's first weight
+    copies in time: outputs are bitwise equal for every setting, chained under
+    programmatic dependent launch or not; out-of-range values are refused."""
+    from simd_ml_kernels import _core
+    N, K = 8192, 2048
+    rng = np.random.default_rng(95)
+    W = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    wd = torch.from_numpy(O.quantize("q4_0", W).ravel()).cuda()
+    x = torch.from_numpy(rng.standard_normal((4, K)).astype(np.float32)).cuda()
+    ys = {}
+    try:
+        for pdl in (False, True):
+            sk.set_pdl(pdl, 0)
+            for delay in (0, 1, 100, 5000, 100000):
+                _core._ctx_set(8, delay)
+                y = torch.empty((4, N), device="cuda")
+                for i in range(4):   # chained launches on one stream
+                    sk.gemv_q4_0(x[i], wd, N, K, out=y[i])
+                ys[(pdl, delay)] = y.cpu().numpy()
+        with pytest.raises(sk.ArgumentError, match="prefetch delay"):
+            _core._ctx_set(8, -1)
+        with pytest.raises(sk.ArgumentError, match="prefetch delay"):
+            _core._ctx_set(8, 100001)
+    finally:
+        _core._ctx_set(8, 100)
+        sk.set_pdl(False, 0)
+    want = ys[(False, 0)]
+    for k, y in ys.items():
+        np.testing.assert_array_equal(y.view(np.uint32), want.view(np.uint32), err_msg=str(k))
+    assert _core._device_error(torch.cuda.current_stream().cuda_stream) == 0
+
+
 @pytest.mark.parametrize("N,K", [(1003, 2048), (8192, 2048), (517, 2080), (4096, 4096)])
 def test_host_output_copy_bitwise_equal(sk, torch, N, K):
     """Host outputs from the fast kernel are copied to page-locked memory by
