@@ -1069,6 +1069,119 @@ void (*r4_kernel(const QGemvParams& p))(QGemvParams) {
     return gemv_q4_r4<kXGlobal, 0>;
 }
 
+// ---- four-row kernel, K split over warps ----------------------------------------------
+//
+// Few four-row tiles and long rows (K a multiple of 2048, at least 8192, fewer
+// than 8 tiles per SM: the Llama down projection 2048×8192, a 70B layer's
+// 8192×28672 sharded over GPUs): one warp per tile would leave most warps idle
+// and walk all of K alone. Here the k-steps of a tile are split over S warps
+// of a CTA (p.split). CTA c takes the tile groups c, c + grid, ... of T =
+// warps / S tiles; warp w works on tile w / S of a group over the k-steps
+// [part·ks/S, (part+1)·ks/S), part = w % S, with x quantized once in global
+// memory (the four-row slot layout). Each warp's four row sums (r4_reduce) go
+// to shared memory and the part-0 warp adds the S parts in part order:
+// deterministic, within the reference's bound (rounded differently from one
+// warp walking K). Variants: the residual add (kExtRes) and the fused gather
+// (kExtGather); an RMSNorm of x happens in the quantize kernel before.
+__host__ __device__ inline size_t r4s_smem(int warps, int stages) {
+    return (((size_t)warps * stages * 8 + 127) & ~(size_t)127) + (((size_t)warps * 16 + 127) & ~(size_t)127) +
+           (size_t)warps * stages * 32 * 144;
+}
+
+template <int kExt>
+__global__ void __launch_bounds__(512, 2) gemv_q4_r4s(const QGemvParams p) {
+    constexpr bool kGather = (kExt & kExtGather) != 0, kRes = (kExt & kExtRes) != 0;
+    constexpr int SBB = 144;
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    const int S = p.split, T = nwarps / S, part = warp % S, tl = warp / S;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem) + warp * p.stages;
+    size_t off = ((size_t)nwarps * p.stages * 8 + 127) & ~(size_t)127;
+    float* sums = reinterpret_cast<float*>(smem + off);   // [warp][row of the tile]
+    off += ((size_t)nwarps * 16 + 127) & ~(size_t)127;
+    uint8_t* stages = smem + off + (size_t)warp * p.stages * 32 * SBB;
+
+    if constexpr (!kGather) pdl_launch_dependents();
+    const int ks_lo = part * p.ksteps / S, nks = (part + 1) * p.ksteps / S - ks_lo;
+    const int ngroups = (p.ntiles + T - 1) / T, bx = (int)blockIdx.x, nbx = (int)gridDim.x;
+    const int rounds = bx < ngroups ? (ngroups - 1 - bx) / nbx + 1 : 0;   // CTA-uniform
+    auto tile_of = [&](int rd) { return (bx + rd * nbx) * T + tl; };
+    int valid = rounds;   // rounds with this warp's tile inside N (only the last group runs past it)
+    while (valid > 0 && tile_of(valid - 1) >= p.ntiles) --valid;
+    const int nitems = valid * nks;
+    if (lane == 0) {
+        for (int i = 0; i < p.stages; ++i) mbar_init(&bars[i], 1);
+        fence_mbar_init();
+    }
+    __syncwarp();
+    int i_r = 0, i_k = 0, i_slot = 0, issued = 0;
+    auto issue_next = [&]() {
+        issue_item<kQ4_0>(p, tile_of(i_r), ks_lo + i_k, i_slot, stages, bars, lane);
+        if (++i_k == nks) { i_k = 0; ++i_r; }
+        if (++i_slot == p.stages) i_slot = 0;
+        ++issued;
+    };
+    while (issued < min(p.stages, nitems)) issue_next();   // weights only: x is the previous kernel's output
+
+    pdl_wait_primary();
+    if constexpr (kGather) pdl_launch_dependents();
+    GatherStep gs{0, 0u};
+    if constexpr (kGather) {
+        gs = gather_step(p.gather);
+        if (bx == 0) gather_pad(p.gather, 1, p.N, threadIdx.x, blockDim.x);
+    }
+    const int r = lane >> 3, g = lane & 7;
+    const uint32_t no_pre[kR4PreRows * 9] = {};
+    int failed = 0, c_slot = 0, consumed = 0;
+    uint32_t c_phase = 0;
+    for (int rd = 0; rd < rounds; ++rd) {   // CTA-uniform: every warp meets every barrier
+        float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        if (rd < valid) {
+            for (int k = 0; k < nks && !failed; ++k) {
+                if (__any_sync(0xffffffffu, !mbar_wait_bounded(&bars[c_slot], c_phase, p.err))) {   // warp-uniform
+                    failed = 1;
+                    break;
+                }
+                const uint8_t* xslot = p.xq + ((size_t)(ks_lo + k) * 32 + lane) * 80;
+                r4_item<false, 0>(stages + (size_t)c_slot * (32 * SBB), xslot, lane, acc, no_pre);
+                __syncwarp();
+                if (issued < nitems) {
+                    fence_proxy_async_smem();
+                    issue_next();
+                }
+                ++consumed;
+                if (++c_slot == p.stages) { c_slot = 0; c_phase ^= 1u; }
+            }
+        }
+        const float v = r4_reduce(acc, lane);
+        if (g == 0) sums[warp * 4 + r] = v;
+        const int any_failed = __syncthreads_or(failed);
+        if (part == 0 && g == 0 && rd < valid && !any_failed) {
+            const int row = tile_of(rd) * 4 + r;
+            if (row < p.N) {
+                float t = sums[tl * S * 4 + r];
+                for (int q = 1; q < S; ++q) t = __fadd_rn(t, sums[(tl * S + q) * 4 + r]);   // the parts in K order
+                if constexpr (kRes) t = __fadd_rn(p.res[row], t);
+                p.y[row] = t;
+                if constexpr (kGather) {
+                    const GatherArgs* ga = p.gather;
+                    const long long o = gs.off + row;
+                    ga->y[o] = t;
+                    const unsigned long long w = tagged_word(t, gs.tag);
+                    for (int rk = 0; rk < ga->world; ++rk)
+                        if (rk != ga->rank) st_relaxed_sys_u64(ga->ll[rk] + o, w);
+                }
+            }
+        }
+        __syncthreads();   // the sums are read before the next round writes them
+    }
+    if (failed) {   // this warp's copies still in flight land (bounded) before the CTA exits
+        for (int k = consumed; k < issued; ++k)
+            mbar_wait_bounded(&bars[k % p.stages], (uint32_t)((k / p.stages) & 1), nullptr);
+    }
+    if (p.yhost) copy_y_to_host(p);
+}
+
 // ---- tensor-core kernel for 3..8 rows of x -------------------------------------------
 //
 // With several rows of x, the block dots are an integer matrix product per
@@ -1651,10 +1764,41 @@ cudaError_t launch(Kern kernel, dim3 grid, dim3 block, size_t smem, const Launch
     return cudaLaunchKernelEx(&cfg, kernel, args...);
 }
 
+// The split four-row kernel for p (x quantized in global memory, few tiles):
+// S parts per tile, the largest power of two up to 16 and the k-steps whose
+// parts still fit the GPU's warps in one round; stages: two when a part has
+// more than one k-step.
+cudaError_t launch_r4_split(const LaunchCfg& c, const QGemvParams& p) {
+    const int warps = 16;
+    QGemvParams q = p;
+    q.split = 1;
+    while (q.split < warps && 2 * q.split <= p.ksteps &&
+           (long long)p.ntiles * 2 * q.split <= (long long)c.num_sms * warps)
+        q.split *= 2;
+    q.stages = (p.ksteps + q.split - 1) / q.split > 1 ? 2 : 1;
+    void (*k)(QGemvParams);
+    if (p.gather) k = gemv_q4_r4s<kExtGather>;
+    else if (p.res) k = gemv_q4_r4s<kExtRes>;
+    else k = gemv_q4_r4s<0>;
+    const size_t smem = r4s_smem(warps, q.stages);
+    int per_sm = 0;
+    cudaError_t e = occupancy_cached((const void*)k, warps * 32, smem, &per_sm);
+    if (e != cudaSuccess) return e;
+    if (per_sm < 1) return cudaErrorInvalidConfiguration;
+    const int T = warps / q.split;
+    const long long groups = (p.ntiles + T - 1) / T;
+    const long long grid = std::max<long long>(1, std::min<long long>(groups, (long long)per_sm * c.num_sms));
+    return launch(k, dim3((unsigned)grid), dim3(warps * 32), smem, c, q);
+}
+
 template <int F, int M>
 cudaError_t launch_fast_m(const LaunchCfg& c, const QGemvParams& p, size_t smem, bool dump) {
     void (*k)(QGemvParams);
     if constexpr (F == 0 && M == 1) {
+        if (p.r4 && r4_split(p, c.num_sms)) {
+            if (!p.xq) return cudaErrorInvalidValue;   // x quantized (and normalised) in global memory first
+            return launch_r4_split(c, p);
+        }
         if (p.r4) k = p.xq ? r4_kernel<true>(p) : r4_kernel<false>(p);
         else if (p.xq) k = gemv_q_fast2<F, M, true, false>;
         else if (dump) k = gemv_q_fast<F, M, false, true>;
@@ -1713,13 +1857,17 @@ cudaError_t occupancy(const void* fn, int threads, size_t smem, int* per_sm) {
 
 bool r4_shape(int N, int K, int num_sms) {
     if (K == 2048) return true;
-    // Longer rows: a warp runs the k-steps of its tiles one after another, so the
-    // layout needs tiles for every warp (8 per SM), and it is used where x is
-    // quantized once into global memory (K >= 8192, N <= 16384). Measured on
-    // B200, graph-chained: 8192x28672 23.6 us against 28.8; the Llama down
-    // projection 2048x8192 (3.5 tiles per SM) and 28672x8192 (x in shared
-    // memory) were slower this way.
-    return K % 2048 == 0 && K >= 8192 && N <= 16384 && (long long)N >= 32LL * num_sms;
+    // Longer rows, where x is quantized once into global memory (K >= 8192,
+    // N <= 16384), with tiles for every warp (8 per SM) or K >= 16384 (then
+    // fewer tiles take the split-K kernel, r4_split). Measured on B200,
+    // graph-chained: 8192x28672 23.6 us against 28.8; 28672x8192 (x in shared
+    // memory) and, at K = 8192, the Llama down projection 2048x8192 were slower
+    // this way, split or not (6.88 us in the superblock kernel, 7.50 split).
+    return K % 2048 == 0 && K >= 8192 && N <= 16384 && ((long long)N >= 32LL * num_sms || K >= 16384);
+}
+
+bool r4_split(const QGemvParams& p, int num_sms) {
+    return p.r4 && p.ksteps >= 8 && (long long)p.ntiles < 8LL * num_sms;
 }
 
 void plan_tiles(QGemvParams& p, bool fast, int fmt, bool allow_r4, int num_sms) {

@@ -128,8 +128,11 @@ struct GatherArgs {
 void plan_tiles(QGemvParams& p, bool fast, int fmt = -1, bool allow_r4 = true, int num_sms = 148);
 // Shapes that take the four-row layout: K == 2048; or K a multiple of 2048, at
 // least 8192, with N <= 16384 (x quantized once into global memory) and at
-// least 8 four-row tiles per SM.
+// least 8 four-row tiles per SM, or K >= 16384.
 bool r4_shape(int N, int K, int num_sms);
+// Four-row plans with fewer than 8 tiles per SM (K >= 16384): the kernel
+// that splits each tile's k-steps over several warps (x in global memory).
+bool r4_split(const QGemvParams& p, int num_sms);
 // Bytes of quantized x of this plan (either layout).
 inline size_t x_bytes(const QGemvParams& p) { return p.r4 ? xq_r4_bytes(p.ksteps) : xq_total_bytes(p.M, p.ksteps); }
 

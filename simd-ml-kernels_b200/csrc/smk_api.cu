@@ -400,6 +400,8 @@ smk_status run_q(smk_ctx* c, smk_qformat fmt, int M, int N, int K, const float* 
     // 3,177 against 3,132 tok/s). 28672x8192 measured 3 % slower that way and
     // K = 2048 (config 0) far slower, so those keep x in shared memory.
     if (!up && !gather && !dump && q.fast && q.x_in_smem && K >= 8192 && N <= 16384) q.x_in_smem = false;
+    // The four-row kernel that splits K over warps reads x from global memory.
+    if (q.fast && q.x_in_smem && !dump && smk::r4_split(q.p, c->num_sms)) q.x_in_smem = false;
     if (!q.x_in_smem) {
         uint8_t* xq;
         {

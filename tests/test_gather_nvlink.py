@@ -85,6 +85,22 @@ def _rank(rank, world, port, out_dir):
         assert (Y - sk.gemv_q4_0_batch(X, Wq, N, K)).abs().max().item() <= 1e-5 * Y.abs().max().item()
         assert _core._device_error(stream) == 0
         sg.close()
+        # Long rows, few tiles per GPU: the kernel that splits K over warps, with
+        # the gather fused in; two steps in a row against the unsharded GEMV
+        # (split differently, so within the bound).
+        N2, K2 = 1002, 16384
+        W2 = sk.quantize_q4_0(torch.randn((N2, K2), generator=g, device="cuda") * 0.02).reshape(-1)
+        rb2 = K2 // 32 * 18
+        lo2, hi2 = shard.row_slice(N2, rank, world)
+        sg2 = shard.ShardedGemv("q4_0", W2[lo2 * rb2:hi2 * rb2].clone(), N2, K2, gather="nvlink")
+        for step in range(2):
+            x2 = torch.randn(K2, generator=torch.Generator(device="cuda").manual_seed(200 + step), device="cuda")
+            Y2 = sg2.forward(x2).reshape(N2).clone()
+            want2 = sk.gemv_q4_0(x2, W2, N2, K2)
+            torch.cuda.synchronize()
+            assert (Y2 - want2).abs().max().item() <= 1e-5 * want2.abs().max().item(), f"long rows, step {step}"
+        assert _core._device_error(stream) == 0
+        sg2.close()
     except Exception as exc:  # noqa: BLE001 - reported to the parent
         status = f"error: {type(exc).__name__}: {exc}"
     with open(os.path.join(out_dir, f"rank{rank}.txt"), "w") as f:

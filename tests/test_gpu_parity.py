@@ -316,10 +316,11 @@ def test_gemv_silu_mul_equals_unfused(sk, torch, fmt, M, N, K):
 
 
 @pytest.mark.parametrize("fmt", ["q4_0", "q8_0"])
-@pytest.mark.parametrize("K", [8192, 28672])
+@pytest.mark.parametrize("K", [8192, 12288])
 def test_x_in_global_equals_x_in_shared(sk, torch, fmt, K):
     """With K >= 8192 and at most 16384 rows, x is quantized once into global
-    scratch; with more rows each CTA quantizes it into shared memory. A row's
+    scratch; with more rows each CTA quantizes it into shared memory. (At
+    K >= 16384 so few rows take the split-K kernel, test_q4_0_split_k_rows.) A row's
     arithmetic is the same either way: the first 2048 rows of a 16392-row
     GEMV equal a 2048-row GEMV over the same rows, bit for bit, and stay
     within the bound of the float64 sums."""
@@ -632,6 +633,26 @@ def test_host_output_copy_bitwise_equal(sk, torch, N, K):
         np.testing.assert_array_equal(y1.view(np.uint32), want.view(np.uint32))
     from simd_ml_kernels import _core
     assert _core._device_error(0) == 0
+
+
+@pytest.mark.parametrize("N,K", [(1, 16384), (3, 28672), (1000, 16384), (2048, 28672), (4095, 16384), (4733, 28672),
+                                 (1024, 57344)])
+def test_q4_0_split_k_rows(sk, torch, N, K):
+    """Q4_0, one row of x, K a multiple of 2048 from 16384 and fewer than 8
+    four-row tiles per SM: the kernel that splits each tile's k-steps over
+    several warps. Outputs within the bound of the float64 sum; the host-memory
+    call (NumPy in and out, y copied to page-locked memory by the kernel's last
+    CTA) equals the device call bitwise, on two calls in a row."""
+    x, Wq = make_case(7 * N + K, N, K, "q4_0", scale=0.02)
+    y64, mag = O.ref64("q4_0", x, Wq, N, K)
+    wd = torch.from_numpy(Wq.ravel()).cuda()
+    yd = sk.gemv_q4_0(torch.from_numpy(x).cuda(), wd, N, K).cpu().numpy()
+    assert_gemv_close(yd, y64, mag, K, f"N={N} K={K}")
+    for _ in range(2):
+        yh = sk.gemv_q4_0(x, wd, N, K)
+        np.testing.assert_array_equal(yh.view(np.uint32), yd.view(np.uint32))
+    from simd_ml_kernels import _core
+    assert _core._device_error(torch.cuda.current_stream().cuda_stream) == 0
 
 
 def test_row_shards_bitwise_equal_full(sk, torch):
