@@ -801,9 +801,9 @@ def rotated_case(torch, dev, stream, w, call, nbytes: int, l2: int, peak: dict, 
 def sharded_case(torch, sk, _core, shard, dev, stream, N, K, wq, X, rank, world, local_rank, l2, peak,
                  barrier) -> dict:
     """Config 4 shape (N, K): this rank's row slice at M = 1 and M = 8. N = 1: the
-    GEMV; N > 1: the GEMV with the all-gather of y (fused NVLink stores at M = 1,
-    NCCL all-gather after the tensor-core GEMV at M = 8), strong scaling, max over
-    ranks."""
+    GEMV; N > 1: the GEMV with the all-gather of y fused into its stores over
+    NVLink (the one-row kernels at M = 1, the tensor-core kernel at M = 8),
+    strong scaling, max over ranks."""
     lo, hi = shard.row_slice(N, rank, world)
     n = hi - lo
     copies = max(2, -(-2 * l2 // max(1, wq.numel())) + 1)
@@ -814,19 +814,11 @@ def sharded_case(torch, sk, _core, shard, dev, stream, N, K, wq, X, rank, world,
         yd = torch.empty((M, n), device=dev)
         sg = None
         if world > 1:
-            sg = shard.ShardedGemv("q4_0", wq, N, K, gather="nvlink" if M == 1 else "nccl")
-            if M == 1:
-                def step(i, sg=sg, xd=xd):
-                    _core._gemv_q_gather(sg._g, 0, 1, n, K, xd.data_ptr(), K, ws[i % copies].data_ptr(),
-                                         stream.cuda_stream, local_rank)
-            else:
-                recv = torch.empty((world, M, sg.pad), device=dev)
-                send = torch.zeros((M, sg.pad), device=dev)
-                import torch.distributed as dist
+            sg = shard.ShardedGemv("q4_0", wq, N, K, gather="nvlink")
 
-                def step(i, xd=xd, send=send, recv=recv):
-                    sk.gemv_q4_0_batch(xd, ws[i % copies], n, K, out=send[:, :n])
-                    dist.all_gather_into_tensor(recv, send)
+            def step(i, sg=sg, xd=xd, M=M):
+                _core._gemv_q_gather(sg._g, 0, M, n, K, xd.data_ptr(), K, ws[i % copies].data_ptr(),
+                                     stream.cuda_stream, local_rank)
         elif M == 1:
             def step(i, xd=xd, yd=yd):
                 sk.gemv_q4_0(xd[0], ws[i % copies], n, K, out=yd[0])
@@ -847,7 +839,7 @@ def sharded_case(torch, sk, _core, shard, dev, stream, N, K, wq, X, rank, world,
         res[key] = {"us": round(us, 3), "gb_s_aggregate": round(nbytes / (us * 1e-6) / 1e9, 1),
                     "rows_per_gpu": n, "bytes": nbytes, "roofline": roofline(nbytes, us, peak),
                     "roofline_per_gpu": roofline(nbytes // world, us, peak),
-                    "gather": None if world == 1 else ("fused NVLink stores" if M == 1 else "NCCL all-gather")}
+                    "gather": None if world == 1 else "fused NVLink stores"}
         del xd, yd
     del ws
     return res

@@ -1379,7 +1379,11 @@ __device__ __forceinline__ T ld_xfrag(const T* p) {
 // in shared memory and part 0 adds the S partial sums in order, so the result
 // is deterministic but rounded differently. The launcher splits K only when
 // the tiles alone cannot fill the GPU.
-template <int F, bool kXS>
+//
+// kGather: y is this rank's staging slice of a row-sharded GEMV (p.gather), and
+// every final output also goes to this rank's full-y area and, as a tagged
+// word, to every peer's receive area (the one-row kernels' fused gather).
+template <int F, bool kXS, bool kGather>
 __global__ void __launch_bounds__(kMmaWarps * 32, 1) gemv_q_mma(const QGemvParams p, const __grid_constant__ CUtensorMap wmap) {
     constexpr int KB = mma_kb<F>(), RS = mma_rs<F>(), ITEM = 16 * RS;
     extern __shared__ __align__(128) uint8_t smem[];
@@ -1392,7 +1396,7 @@ __global__ void __launch_bounds__(kMmaWarps * 32, 1) gemv_q_mma(const QGemvParam
     float4* parts = reinterpret_cast<float4*>(smem + mma_part_offset(nwarps, p.stages, xnb, kXS));
     uint8_t* ring = smem + mma_ring_offset(nwarps, p.stages, xnb, kXS) + (size_t)warp * p.stages * ITEM;
 
-    pdl_launch_dependents();
+    if constexpr (!kGather) pdl_launch_dependents();   // with a gather: after griddepcontrol.wait
     const int ntiles = (p.N + 15) / 16, ksteps = p.nb / KB;   // K % 256 == 0: whole items
     // K parts across CTAs (kparts > 1): CTA c works on part c / C of K, over
     // the tile groups of its index c % C within the part.
@@ -1439,6 +1443,28 @@ __global__ void __launch_bounds__(kMmaWarps * 32, 1) gemv_q_mma(const QGemvParam
     while (issued < min(p.stages, nitems)) issue_next();
 
     pdl_wait_primary();   // x was quantized by the previous kernel
+    // The gather's wait kernel reads the epoch when it starts: launched only once
+    // the previous one has finished, which the wait above implies.
+    if constexpr (kGather) pdl_launch_dependents();
+    GatherStep gs{0, 0u};
+    long long gcols = 0;
+    if constexpr (kGather) {
+        gs = gather_step(p.gather);
+        gcols = (long long)p.gather->world * p.gather->npad;
+        if (blockIdx.x == 0) gather_pad(p.gather, p.M, p.N, threadIdx.x, blockDim.x);
+    }
+    // A final output value: y, and with a gather the full-y areas.
+    auto emit = [&](int m, int row, float v) {
+        p.y[(size_t)m * p.ldy + row] = v;
+        if constexpr (kGather) {
+            const GatherArgs* ga = p.gather;
+            const long long o = gs.off + m * gcols + row;
+            ga->y[o] = v;
+            const unsigned long long w = tagged_word(v, gs.tag);
+            for (int rk = 0; rk < ga->world; ++rk)
+                if (rk != ga->rank) st_relaxed_sys_u64(ga->ll[rk] + o, w);
+        }
+    };
     const uint8_t* xbase = p.xq;
     int failed = 0;
     int xnb_here = p.nb, xoff = 0;   // blocks of x at xbase, and the block index of the first
@@ -1525,8 +1551,8 @@ __global__ void __launch_bounds__(kMmaWarps * 32, 1) gemv_q_mma(const QGemvParam
 #pragma unroll
                 for (int rr = 0; rr < 2; ++rr) {
                     const int row = tile * 16 + g + 8 * rr;
-                    if (row < p.N && 2 * t < p.M) p.y[(size_t)(2 * t) * p.ldy + row] = acc[rr].x;
-                    if (row < p.N && 2 * t + 1 < p.M) p.y[(size_t)(2 * t + 1) * p.ldy + row] = acc[rr].y;
+                    if (row < p.N && 2 * t < p.M) emit(2 * t, row, acc[rr].x);
+                    if (row < p.N && 2 * t + 1 < p.M) emit(2 * t + 1, row, acc[rr].y);
                 }
             }
         } else {
@@ -1550,7 +1576,10 @@ __global__ void __launch_bounds__(kMmaWarps * 32, 1) gemv_q_mma(const QGemvParam
                     const int row = tile * 16 + g + 8 * rr;
 #pragma unroll
                     for (int j = 0; j < 2; ++j)
-                        if (row < p.N && 2 * t + j < p.M) out[(size_t)(2 * t + j) * ldo + row] = vals[2 * rr + j];
+                        if (row < p.N && 2 * t + j < p.M) {
+                            if (P > 1) out[(size_t)(2 * t + j) * ldo + row] = vals[2 * rr + j];
+                            else emit(2 * t + j, row, vals[2 * rr + j]);
+                        }
                 }
             }
             __syncthreads();
@@ -1575,7 +1604,7 @@ __global__ void __launch_bounds__(kMmaWarps * 32, 1) gemv_q_mma(const QGemvParam
                     float sum = __ldcg(p.partial + (size_t)m * p.N + row);
                     for (int q = 1; q < P; ++q)
                         sum = __fadd_rn(sum, __ldcg(p.partial + ((size_t)q * p.M + m) * p.N + row));
-                    p.y[(size_t)m * p.ldy + row] = sum;
+                    emit(m, row, sum);
                 }
             }
         }
@@ -2004,8 +2033,13 @@ cudaError_t launch_gemv_q_mma(const LaunchCfg& c, int fmt, const QGemvParams& p,
     cudaError_t me = encode_weight_map(fmt, p, &wmap);
     if (me != cudaSuccess) return me;
     void (*k)(QGemvParams, CUtensorMap);
-    if (fmt == kQ4_0) k = x_in_smem ? gemv_q_mma<kQ4_0, true> : gemv_q_mma<kQ4_0, false>;
-    else k = x_in_smem ? gemv_q_mma<kQ8_0, true> : gemv_q_mma<kQ8_0, false>;
+    if (p.gather) {
+        if (fmt == kQ4_0) k = x_in_smem ? gemv_q_mma<kQ4_0, true, true> : gemv_q_mma<kQ4_0, false, true>;
+        else k = x_in_smem ? gemv_q_mma<kQ8_0, true, true> : gemv_q_mma<kQ8_0, false, true>;
+    } else {
+        if (fmt == kQ4_0) k = x_in_smem ? gemv_q_mma<kQ4_0, true, false> : gemv_q_mma<kQ4_0, false, false>;
+        else k = x_in_smem ? gemv_q_mma<kQ8_0, true, false> : gemv_q_mma<kQ8_0, false, false>;
+    }
     const int P = p.kparts > 1 ? p.kparts : 1;
     if (P > 1 && (!x_in_smem || !p.partial || !p.tickets)) return cudaErrorInvalidValue;
     const size_t smem = gemv_q_mma_smem(fmt, p.stages, p.xnb > 0 ? p.xnb : p.nb, x_in_smem);

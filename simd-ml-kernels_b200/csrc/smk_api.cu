@@ -314,11 +314,12 @@ smk_status run_q(smk_ctx* c, smk_qformat fmt, int M, int N, int K, const float* 
     smk::LaunchCfg l = cfg_for(c, s);
     if (force_pdl) l.pdl = true;   // the previous kernel writes x only (a host call's stage_x_kernel)
     const bool fused = nw || res;   // RMSNorm before / residual add after: the fast kernels only
-    if (!gather && !fused && M >= smk::kMmaMinRows && !dump && K % 256 == 0 &&
-        (reinterpret_cast<uintptr_t>(Wq) & 15) == 0) {
+    if (!fused && M >= smk::kMmaMinRows && !dump && K % 256 == 0 && (reinterpret_cast<uintptr_t>(Wq) & 15) == 0) {
         // Several rows of x: integer tensor-core kernel (bitwise the reference's
-        // scalar order), x quantized once into scratch by its own kernel.
+        // scalar order), x quantized once into scratch by its own kernel; with
+        // a gather, the outputs also go out to the peers from its stores.
         smk::QGemvParams p = {};
+        p.gather = gather;
         p.x = x; p.ldx = ldx; p.w = Wq; p.y = yhost ? yhost : y; p.ldy = ldy;
         p.up = up; p.ldu = ldu;
         p.M = M; p.N = N; p.K = K; p.nb = K / 32;

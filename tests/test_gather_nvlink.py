@@ -2,7 +2,8 @@
 2 GPUs, one spawned process each, NCCL only for the set-up handshake. Every
 step's gathered y equals the unsharded GEMV on one GPU (bitwise for one and
 two rows of x, which take the same kernel; within the reference's bound of the
-float64 sums for four rows), a reader queued on the stream before the next
+float64 sums for four and eight rows, which take the tensor-core kernel with
+the gather fused into its stores), a reader queued on the stream before the next
 step sees the step's result intact (the contract: y_full is valid until this
 rank's next call), and no device error is raised. Needs two GPUs; skipped
 otherwise."""
@@ -55,8 +56,8 @@ def _rank(rank, world, port, out_dir):
         lo, hi = shard.row_slice(N, rank, world)
         sg = shard.ShardedGemv("q4_0", Wq[lo * rb:hi * rb].clone(), N, K, gather="nvlink")
         prev = None
-        for step in range(6):
-            M = (1, 2, 4)[step % 3]
+        for step in range(8):
+            M = (1, 2, 4, 8)[step % 4]
             X = torch.randn((M, K), generator=torch.Generator(device="cuda").manual_seed(100 + step), device="cuda")
             Y = sg.forward(X if M > 1 else X[0]).reshape(M, N)
             copy = Y.clone()   # a reader queued on the stream before the next call
