@@ -28,13 +28,14 @@ struct DenseParams {
 
 cudaError_t launch_gemv_dense(cudaStream_t s, bool pdl, int num_sms, int w_kind, int x_kind, const DenseParams& p);
 
-// Tensor-core path (gemv_dense_mma.cu): bfloat16 W and kDenseMmaMinRows..8
-// rows of float32 or bfloat16 x, K a multiple of 128, W 16-byte aligned with
+// Tensor-core path (gemv_dense_mma.cu): bfloat16 W with float32 or bfloat16 x,
+// or float16 W with float32 x, kDenseMmaMinRows..8 rows, K a multiple of 128,
+// W 16-byte aligned with
 // a 16-byte row stride. dense_mma_scratch gives the scratch bytes it needs for
 // the call (0: the call does not take it); launch_gemv_dense_mma runs it with
 // p.xfrag pointing at that scratch (two kernels: the split of x, the GEMV).
 constexpr int kDenseMmaMinRows = 4;
 size_t dense_mma_scratch(int w_kind, int x_kind, int M, int K, long long ldw, const void* w);
-cudaError_t launch_gemv_dense_mma(cudaStream_t s, bool pdl, int num_sms, int x_kind, const DenseParams& p);
+cudaError_t launch_gemv_dense_mma(cudaStream_t s, bool pdl, int num_sms, int w_kind, int x_kind, const DenseParams& p);
 
 }  // namespace smk

@@ -148,17 +148,34 @@ struct DMGeom {
     int S;        // K parts per tile (power of two, <= kDMWarps)
 };
 
-// One output recomputed in plain fp32 (x in its own type, W bf16), k in order.
-template <int XK>
+// One output recomputed in plain fp32 (x in its own type, W bf16 or fp16), k in order.
+template <int WK, int XK>
 __device__ float dense_dot_fp32(const DenseParams& p, int row, int m) {
     const uint16_t* w = static_cast<const uint16_t*>(p.w) + (size_t)row * p.ldw;
     float s = 0.0f;
-    for (int k = 0; k < p.K; ++k)
-        s = __fmaf_rn(x_at<XK>(p.x, (long long)m * p.ldx + k), __uint_as_float((uint32_t)w[k] << 16), s);
+    for (int k = 0; k < p.K; ++k) {
+        const float wv = WK == kF16 ? __half2float(__ushort_as_half(w[k])) : __uint_as_float((uint32_t)w[k] << 16);
+        s = __fmaf_rn(x_at<XK>(p.x, (long long)m * p.ldx + k), wv, s);
+    }
     return s;
 }
 
-template <int XK, int NP>
+// An A-fragment register of two fp16 weights as two registers of bf16 pairs,
+// w = hi + lo exactly: hi is w (exact in fp32) truncated to bf16, lo the
+// remainder, at most 3 significant bits (fp16 has 11, bf16 8), exact in bf16
+// for every finite fp16 including subnormals. An infinity leaves lo = NaN:
+// its outputs are recomputed in plain fp32 (the NaN check below).
+__device__ __forceinline__ void split_f16x2(uint32_t h, uint32_t& hi, uint32_t& lo) {
+    const float f0 = half_lo_to_float(h), f1 = half_hi_to_float(h);
+    const uint32_t b0 = __float_as_uint(f0), b1 = __float_as_uint(f1);
+    hi = __byte_perm(b0, b1, 0x7632);
+    const float r0 = __fsub_rn(f0, __uint_as_float(b0 & 0xffff0000u)), r1 = __fsub_rn(f1, __uint_as_float(b1 & 0xffff0000u));
+    lo = __byte_perm(__float_as_uint(r0), __float_as_uint(r1), 0x7632);
+}
+
+// WK: kBF16 (W used as it is) or kF16 (each weight split into two bf16 parts,
+// so every part of x meets both: six MMAs per 16 × 16 tile, all products exact).
+template <int WK, int XK, int NP>
 __global__ void __launch_bounds__(kDMWarps * 32, 1) gemv_dense_mma(const DenseParams p, const DMGeom g,
                                                                    const __grid_constant__ CUtensorMap wmap) {
     constexpr int XB = dm_xbytes(NP), STAGE = dm_stage(NP);
@@ -243,10 +260,22 @@ __global__ void __launch_bounds__(kDMWarps * 32, 1) gemv_dense_mma(const DensePa
                     }
 #pragma unroll
                     for (int u = 0; u < 4; ++u) {
-                        mma_bf16(hi, a[u], bx[u][0]);
-                        if constexpr (NP == 3) {
-                            mma_bf16(mid, a[u], bx[u][1]);
-                            mma_bf16(lo, a[u], bx[u][2]);
+                        if constexpr (WK == kF16) {   // fp32 x only (NP == 3)
+                            uint32_t ah[4], al[4];
+#pragma unroll
+                            for (int i = 0; i < 4; ++i) split_f16x2(a[u][i], ah[i], al[i]);
+                            mma_bf16(hi, ah, bx[u][0]);
+                            mma_bf16(mid, ah, bx[u][1]);
+                            mma_bf16(mid, al, bx[u][0]);
+                            mma_bf16(lo, ah, bx[u][2]);
+                            mma_bf16(lo, al, bx[u][1]);
+                            mma_bf16(lo, al, bx[u][2]);
+                        } else {
+                            mma_bf16(hi, a[u], bx[u][0]);
+                            if constexpr (NP == 3) {
+                                mma_bf16(mid, a[u], bx[u][1]);
+                                mma_bf16(lo, a[u], bx[u][2]);
+                            }
                         }
                     }
                 }
@@ -296,7 +325,7 @@ __global__ void __launch_bounds__(kDMWarps * 32, 1) gemv_dense_mma(const DensePa
                     const int m = 2 * t + j;
                     if (row < p.N && m < p.M) {
                         const float h = hi[2 * rr + j], l = lo[2 * rr + j];
-                        const float v = (isnan(l) && !isnan(h)) ? dense_dot_fp32<XK>(p, row, m) : __fadd_rn(h, l);
+                        const float v = (isnan(l) && !isnan(h)) ? dense_dot_fp32<WK, XK>(p, row, m) : __fadd_rn(h, l);
                         float* c = p.y + (size_t)m * p.ldy + row;
                         const float cb = p.beta == 0.0f ? 0.0f : (p.beta == 1.0f ? *c : __fmul_rn(p.beta, *c));
                         *c = __fadd_rn(cb, __fmul_rn(p.alpha, v));
@@ -334,7 +363,7 @@ int dm_parts_of(int x_kind) { return x_kind == kF32 ? 3 : 1; }
 }  // namespace
 
 size_t dense_mma_scratch(int w_kind, int x_kind, int M, int K, long long ldw, const void* w) {
-    if (w_kind != kBF16 || (x_kind != kF32 && x_kind != kBF16)) return 0;
+    if (!(w_kind == kBF16 && (x_kind == kF32 || x_kind == kBF16)) && !(w_kind == kF16 && x_kind == kF32)) return 0;
     if (M < kDenseMmaMinRows || M > 8 || K < kDMItemK || K % kDMItemK != 0) return 0;
     if ((ldw * 2) % 16 != 0 || (reinterpret_cast<uintptr_t>(w) & 15) != 0) return 0;
     int dev = 0, optin = 0;
@@ -345,7 +374,7 @@ size_t dense_mma_scratch(int w_kind, int x_kind, int M, int K, long long ldw, co
     return (size_t)(K / 16) * dm_parts_of(x_kind) * 256;
 }
 
-cudaError_t launch_gemv_dense_mma(cudaStream_t s, bool pdl, int num_sms, int x_kind, const DenseParams& p) {
+cudaError_t launch_gemv_dense_mma(cudaStream_t s, bool pdl, int num_sms, int w_kind, int x_kind, const DenseParams& p) {
     if (!p.xfrag) return cudaErrorInvalidValue;
     PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
     if (!enc) return cudaErrorNotSupported;
@@ -356,7 +385,8 @@ cudaError_t launch_gemv_dense_mma(cudaStream_t s, bool pdl, int num_sms, int x_k
     const cuuint64_t strides[1] = {(cuuint64_t)p.ldw * 2};
     const cuuint32_t box[2] = {(cuuint32_t)kDMBox, 16u};
     const cuuint32_t estr[2] = {1u, 1u};
-    if (enc(&wmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(p.w), dims, strides, box, estr,
+    if (enc(&wmap, w_kind == kF16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+            const_cast<void*>(p.w), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
         return cudaErrorNotSupported;
@@ -381,7 +411,8 @@ cudaError_t launch_gemv_dense_mma(cudaStream_t s, bool pdl, int num_sms, int x_k
     g.S = 1;
     while (g.S < kDMWarps && 2 * g.S <= g.nk && (long long)g.ntiles * g.S * 2 <= grid * kDMWarps) g.S *= 2;
     const size_t smem = dm_smem(np);
-    auto k = x_kind == kF32 ? gemv_dense_mma<kF32, 3> : gemv_dense_mma<kBF16, 1>;
+    auto k = w_kind == kF16 ? gemv_dense_mma<kF16, kF32, 3>
+                            : (x_kind == kF32 ? gemv_dense_mma<kBF16, kF32, 3> : gemv_dense_mma<kBF16, kBF16, 1>);
     int per_sm = 0;
     e = occupancy((const void*)k, kDMWarps * 32, smem, &per_sm);   // also raises the kernel's shared-memory limit
     if (e != cudaSuccess) return e;

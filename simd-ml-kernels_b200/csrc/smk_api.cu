@@ -1052,7 +1052,7 @@ smk_status smk_gemv_dense(smk_ctx* c, smk_dtype wt, smk_dtype xt, int M, int N, 
             SMK_CUDA(b.reserve(need), "cudaMalloc (scratch)");
             p.xfrag = b.ptr;
         }
-        SMK_CUDA(smk::launch_gemv_dense_mma(s, c->pdl, c->num_sms, (int)xt, p), "dense tensor-core gemv launch");
+        SMK_CUDA(smk::launch_gemv_dense_mma(s, c->pdl, c->num_sms, (int)wt, (int)xt, p), "dense tensor-core gemv launch");
         return SMK_OK;
     }
     SMK_CUDA(smk::launch_gemv_dense(s, c->pdl, c->num_sms, (int)wt, (int)xt, p), "dense gemv launch");

@@ -829,6 +829,53 @@ def test_dense_bf16_tensor_core_infinite_weight(sk, torch):
     assert (np.abs(Y[:, fin] - y64) <= 2 * (K + 2) * U * mag + 1e-300).all()
 
 
+@pytest.mark.parametrize("M,N,K", [(4, 4096, 4096), (8, 1003, 512), (5, 37, 128), (8, 14336, 1024), (6, 200, 8192)])
+def test_dense_f16_tensor_core_kernel(sk, torch, M, N, K):
+    """float16 weights with 4..8 rows of float32 x take the tensor-core kernel:
+    each weight split exactly into two bf16 parts (hi, and a lo of at most 3
+    significant bits), x into three, every product exact. Weights with a wide
+    spread of magnitudes (fp16 subnormals included) against the float64 sums
+    within the reference's dense bound, on the tensor-core kernel and on the
+    CUDA-core kernel (SMK_OPT_DENSE_MMA = 0)."""
+    from simd_ml_kernels import _core
+    rng = np.random.default_rng(M * 11 + N + K)
+    W16 = (rng.standard_normal((N, K)) * 0.02 * np.exp2(rng.integers(-14, 6, (N, K)))).astype(np.float16)
+    X = rng.standard_normal((M, K)).astype(np.float32)
+    want, mag = O.dense_ref64(X, "f32", W16.view(np.uint16), "f16")
+    bound = 2 * (K + 2) * U * mag + 1e-300
+    wd = torch.from_numpy(W16).cuda()
+    try:
+        for mma in (1, 0):
+            _core._ctx_set(7, mma)
+            got = sk.gemv_dense(torch.from_numpy(X).cuda(), wd).cpu().numpy()
+            assert (np.abs(got - want) <= bound).all(), f"mma={mma}: max err/bound {np.max(np.abs(got - want) / bound):.3g}"
+    finally:
+        _core._ctx_set(7, 1)
+    assert _core._device_error(torch.cuda.current_stream().cuda_stream) == 0
+
+
+def test_dense_f16_tensor_core_infinite_weight(sk, torch):
+    """An infinite fp16 weight makes its lo part NaN in the tensor-core kernel;
+    the output is recomputed in plain fp32: ±inf as the reference's single
+    product gives, NaN where the weight meets a zero x."""
+    M, N, K = 4, 64, 256
+    rng = np.random.default_rng(6)
+    W16 = (rng.standard_normal((N, K)) * 0.02).astype(np.float16)
+    W16[3, 10] = np.inf
+    W16[7, 20] = -np.inf
+    X = rng.standard_normal((M, K)).astype(np.float32)
+    X[:, 10] = 2.0
+    X[:, 20] = 0.5
+    X[2, 20] = 0.0
+    Y = sk.gemv_dense(torch.from_numpy(X).cuda(), torch.from_numpy(W16).cuda()).cpu().numpy()
+    assert (Y[:, 3] == np.inf).all()
+    assert (Y[[0, 1, 3], 7] == -np.inf).all() and np.isnan(Y[2, 7])
+    fin = np.ones(N, bool)
+    fin[[3, 7]] = False
+    y64, mag = O.dense_ref64(X, "f32", W16[fin].view(np.uint16), "f16")
+    assert (np.abs(Y[:, fin] - y64) <= 2 * (K + 2) * U * mag + 1e-300).all()
+
+
 def test_dense_rejects_non_decode(sk):
     A = np.ones((9, 16), np.float32)
     B = np.ones((4, 16), np.float32)
