@@ -90,8 +90,9 @@ smk_status smk_ctx_destroy(smk_ctx* ctx);
  *                   call launches directly. Setting any option drops the
  *                   captured graphs.
  *   SMK_OPT_DENSE_MMA  1 (default): smk_gemv_dense with bfloat16 weights and
- *                   4..8 rows of x takes the tensor-core kernel (x split
- *                   exactly into bf16 parts); 0: the CUDA-core kernel.
+ *                   4..8 rows of x, or float16 weights and 6..8 rows of float32
+ *                   x, takes the tensor-core kernel (x split exactly into bf16
+ *                   parts, fp16 weights into two); 0: the CUDA-core kernel.
  *   SMK_OPT_PREFETCH_DELAY  SM clock cycles (0..100000) that the Q4_0
  *                   one-row kernel of K = 2048-multiple shapes (without a fused
  *                   norm, residual or gather) holds back its first weight

@@ -34,7 +34,7 @@ cudaError_t launch_gemv_dense(cudaStream_t s, bool pdl, int num_sms, int w_kind,
 // a 16-byte row stride. dense_mma_scratch gives the scratch bytes it needs for
 // the call (0: the call does not take it); launch_gemv_dense_mma runs it with
 // p.xfrag pointing at that scratch (two kernels: the split of x, the GEMV).
-constexpr int kDenseMmaMinRows = 4;
+constexpr int kDenseMmaMinRows = 4, kDenseMmaMinRowsF16 = 6;
 size_t dense_mma_scratch(int w_kind, int x_kind, int M, int K, long long ldw, const void* w);
 cudaError_t launch_gemv_dense_mma(cudaStream_t s, bool pdl, int num_sms, int w_kind, int x_kind, const DenseParams& p);
 

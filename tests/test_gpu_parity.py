@@ -829,9 +829,9 @@ def test_dense_bf16_tensor_core_infinite_weight(sk, torch):
     assert (np.abs(Y[:, fin] - y64) <= 2 * (K + 2) * U * mag + 1e-300).all()
 
 
-@pytest.mark.parametrize("M,N,K", [(4, 4096, 4096), (8, 1003, 512), (5, 37, 128), (8, 14336, 1024), (6, 200, 8192)])
+@pytest.mark.parametrize("M,N,K", [(6, 4096, 4096), (8, 1003, 512), (7, 37, 128), (8, 14336, 1024), (6, 200, 8192)])
 def test_dense_f16_tensor_core_kernel(sk, torch, M, N, K):
-    """float16 weights with 4..8 rows of float32 x take the tensor-core kernel:
+    """float16 weights with 6..8 rows of float32 x take the tensor-core kernel:
     each weight split exactly into two bf16 parts (hi, and a lo of at most 3
     significant bits), x into three, every product exact. Weights with a wide
     spread of magnitudes (fp16 subnormals included) against the float64 sums
@@ -858,7 +858,7 @@ def test_dense_f16_tensor_core_infinite_weight(sk, torch):
     """An infinite fp16 weight makes its lo part NaN in the tensor-core kernel;
     the output is recomputed in plain fp32: ±inf as the reference's single
     product gives, NaN where the weight meets a zero x."""
-    M, N, K = 4, 64, 256
+    M, N, K = 6, 64, 256
     rng = np.random.default_rng(6)
     W16 = (rng.standard_normal((N, K)) * 0.02).astype(np.float16)
     W16[3, 10] = np.inf
