@@ -4,8 +4,9 @@ W [N, K] is split by output rows into one contiguous slice per rank, whole
 8-row groups each, sizes within one group of each other: the reference's
 OpenMP split (gemv_slice, src/dispatch/dispatch.cpp:373-379,
 kGemvRowGroup = 8) moved from threads to GPUs. Each output row is computed by
-one rank with the same kernel and order as unsharded, so the gathered y is
-bitwise identical for any rank count. x is replicated (every rank quantizes
+one rank with the same arithmetic as unsharded whenever the slice takes the
+same kernel as the whole matrix (always at K = 2048), so the gathered y is
+then bitwise identical for any rank count. x is replicated (every rank quantizes
 it itself, deterministically); y slices are all-gathered over NVLink, either
 by the GEMV kernel itself (gather="nvlink": each rank's kernel stores its
 slice into every peer's receive buffer through CUDA IPC mappings, each value
