@@ -234,8 +234,11 @@ __global__ void __launch_bounds__(kDMWarps * 32, 1) gemv_dense_mma(const DensePa
     int failed = 0, c_slot = 0, consumed = 0;
     uint32_t c_phase = 0;
     for (int r = 0; r < rounds; ++r) {   // CTA-uniform: every warp meets every barrier
-        // One accumulator per part: three independent MMA chains (hi, mid, lo).
+        // One accumulator per part: three independent MMA chains (hi, mid, lo);
+        // fp16 weights: one per product of their parts (six chains), so no chain
+        // takes more than one MMA per block, folded into mid and lo at the end.
         float hi[4] = {0.f, 0.f, 0.f, 0.f}, mid[4] = {0.f, 0.f, 0.f, 0.f}, lo[4] = {0.f, 0.f, 0.f, 0.f};
+        float mid2[4] = {0.f, 0.f, 0.f, 0.f}, lo2[4] = {0.f, 0.f, 0.f, 0.f}, lo3[4] = {0.f, 0.f, 0.f, 0.f};
         if (r < my_rounds) {
             for (int k = 0; k < nks && !failed; ++k) {
                 if (__any_sync(0xffffffffu, !mbar_wait_bounded(&bars[c_slot], c_phase, p.err))) {
@@ -266,10 +269,10 @@ __global__ void __launch_bounds__(kDMWarps * 32, 1) gemv_dense_mma(const DensePa
                             for (int i = 0; i < 4; ++i) split_f16x2(a[u][i], ah[i], al[i]);
                             mma_bf16(hi, ah, bx[u][0]);
                             mma_bf16(mid, ah, bx[u][1]);
-                            mma_bf16(mid, al, bx[u][0]);
+                            mma_bf16(mid2, al, bx[u][0]);
                             mma_bf16(lo, ah, bx[u][2]);
-                            mma_bf16(lo, al, bx[u][1]);
-                            mma_bf16(lo, al, bx[u][2]);
+                            mma_bf16(lo2, al, bx[u][1]);
+                            mma_bf16(lo3, al, bx[u][2]);
                         } else {
                             mma_bf16(hi, a[u], bx[u][0]);
                             if constexpr (NP == 3) {
@@ -290,6 +293,13 @@ __global__ void __launch_bounds__(kDMWarps * 32, 1) gemv_dense_mma(const DensePa
                 }
                 ++consumed;
                 if (++c_slot == kDMStages) { c_slot = 0; c_phase ^= 1u; }
+            }
+        }
+        if constexpr (WK == kF16) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                mid[i] = __fadd_rn(mid[i], mid2[i]);
+                lo[i] = __fadd_rn(__fadd_rn(lo[i], lo2[i]), lo3[i]);
             }
         }
         if (S > 1) {   // part 0 adds the parts' sums, in part order
